@@ -1,0 +1,687 @@
+// asmllm_b200/csrc/capi.cu -- the C ABI of libasmllm.so (declared in include/asmllm.h).
+//
+// The synchronous entries keep the reference library's names and signatures
+// (THRISHAL12345/asmllm build_kernel.py:85-104, src/runtime/threadpool.h:37-102)
+// and its calling contract: the caller owns every buffer, y is valid on return
+// (src/kernels/arm64/matmul_q4_neon.S returns after its stores).  Pointers may
+// be host memory (numpy arrays, as the reference's ctypes callers pass) or
+// device memory.  Host buffers are staged through per-device buffers; weights
+// registered with asm_weights_register stay resident in HBM.
+//
+// The reference returns void and has no error channel; here a failure sets a
+// per-thread error (asm_get_last_error) and prints one line to stderr.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/asmllm.h"
+#include "matvec.cuh"
+
+using namespace asmllm;
+
+namespace {
+
+// --------------------------------------------------------------------------
+// Error channel
+// --------------------------------------------------------------------------
+thread_local int t_err_code = ASM_OK;
+thread_local std::string t_err_msg;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  t_err_code = code;
+  t_err_msg = buf;
+  fprintf(stderr, "asmllm: %s\n", buf);
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(ASM_E_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// --------------------------------------------------------------------------
+// Pointer classification (cached per exact address)
+// --------------------------------------------------------------------------
+enum PtrKind { kHostPageable = 0, kHostPinned = 1, kDevice = 2 };
+
+std::mutex g_kind_mu;
+std::unordered_map<const void*, std::pair<int, int>> g_kind_cache;  // ptr -> (kind, device)
+
+PtrKind classify(const void* p, int* device) {
+  {
+    std::lock_guard<std::mutex> lk(g_kind_mu);
+    auto it = g_kind_cache.find(p);
+    if (it != g_kind_cache.end()) {
+      if (device) *device = it->second.second;
+      return (PtrKind)it->second.first;
+    }
+  }
+  cudaPointerAttributes a;
+  PtrKind k = kHostPageable;
+  int dev = -1;
+  cudaError_t e = cudaPointerGetAttributes(&a, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // unknown pointer: plain host memory
+  } else if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+    k = kDevice;
+    dev = a.device;
+  } else if (a.type == cudaMemoryTypeHost) {
+    k = kHostPinned;
+    dev = a.device;
+  }
+  // Pageable host memory is not cached: a later cudaHostRegister may pin it.
+  if (k != kHostPageable) {
+    std::lock_guard<std::mutex> lk(g_kind_mu);
+    if (g_kind_cache.size() > 8192) g_kind_cache.clear();
+    g_kind_cache[p] = {(int)k, dev};
+  }
+  if (device) *device = dev;
+  return k;
+}
+
+// --------------------------------------------------------------------------
+// Per-device state: a blocking stream (ordered after the legacy default
+// stream, which torch uses unless told otherwise) and staging buffers.
+// --------------------------------------------------------------------------
+struct Buf {
+  void* p = nullptr;
+  size_t cap = 0;
+};
+
+struct DeviceState {
+  bool init = false;
+  cudaStream_t stream = nullptr;
+  Buf dev[4];   // device staging: weights, scales, x, y
+  Buf host[2];  // pinned host staging: x, y
+  std::mutex mu;
+};
+
+constexpr int kMaxDev = 64;
+DeviceState g_state[kMaxDev];
+std::mutex g_state_mu;
+int g_num_threads = 0;
+
+int get_state(DeviceState** out, int* dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return set_error(ASM_E_UNSUPPORTED, "device %d out of range", dev);
+  DeviceState& st = g_state[dev];
+  std::lock_guard<std::mutex> lk(g_state_mu);
+  if (!st.init) {
+    e = cudaStreamCreateWithFlags(&st.stream, cudaStreamDefault);
+    if (e != cudaSuccess) return cuda_error(e, "cudaStreamCreate");
+    st.init = true;
+  }
+  *out = &st;
+  if (dev_out) *dev_out = dev;
+  return ASM_OK;
+}
+
+int ensure_dev(Buf& b, size_t bytes) {
+  if (b.cap >= bytes) return ASM_OK;
+  if (b.p) cudaFree(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  size_t cap = bytes < 4096 ? 4096 : bytes;
+  cudaError_t e = cudaMalloc(&b.p, cap);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc (staging)");
+  b.cap = cap;
+  return ASM_OK;
+}
+
+int ensure_host(Buf& b, size_t bytes) {
+  if (b.cap >= bytes) return ASM_OK;
+  if (b.p) cudaFreeHost(b.p);
+  b.p = nullptr;
+  b.cap = 0;
+  size_t cap = bytes < 4096 ? 4096 : bytes;
+  cudaError_t e = cudaHostAlloc(&b.p, cap, cudaHostAllocDefault);
+  if (e != cudaSuccess) return cuda_error(e, "cudaHostAlloc (staging)");
+  b.cap = cap;
+  return ASM_OK;
+}
+
+// --------------------------------------------------------------------------
+// Registered (resident) weights
+// --------------------------------------------------------------------------
+struct RegEntry {
+  const void* host_w = nullptr;
+  const float* host_s = nullptr;
+  int64_t M = 0, K = 0;
+  int fmt = 0;
+  int dev = 0;
+  void* d_w = nullptr;
+  void* d_s = nullptr;
+  bool f16 = false;
+  size_t bytes = 0;
+};
+
+std::mutex g_reg_mu;
+std::unordered_map<const void*, RegEntry> g_reg;
+
+void free_entry(RegEntry& e) {
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != e.dev) cudaSetDevice(e.dev);
+  if (e.d_w) cudaFree(e.d_w);
+  if (e.d_s) cudaFree(e.d_s);
+  if (cur != e.dev) cudaSetDevice(cur);
+  e.d_w = e.d_s = nullptr;
+}
+
+size_t weight_bytes(int fmt, int64_t M, int64_t K) {
+  return (size_t)M * (size_t)(K / 32) * (fmt == kFmtQ4_0 ? 16u : 32u);
+}
+
+int validate(const char* name, const void* w, const void* s, const void* x, const void* y,
+             int64_t M, int64_t K) {
+  if (M < 0 || K < 0) return set_error(ASM_E_INVALID, "%s: negative size M=%lld K=%lld", name, (long long)M, (long long)K);
+  if (K % 32 != 0) return set_error(ASM_E_INVALID, "%s: K=%lld is not a multiple of 32", name, (long long)K);
+  if (M > 0x7fffffffLL || K / 32 > 0x7fffffffLL)
+    return set_error(ASM_E_UNSUPPORTED, "%s: size too large M=%lld K=%lld", name, (long long)M, (long long)K);
+  if (M > 0 && y == nullptr) return set_error(ASM_E_INVALID, "%s: y is NULL", name);
+  if (M > 0 && K > 0 && (w == nullptr || s == nullptr || x == nullptr))
+    return set_error(ASM_E_INVALID, "%s: NULL input pointer", name);
+  return ASM_OK;
+}
+
+int check_max_k(const char* name, int fmt, bool fp32_act, int64_t K, int dev) {
+  const int64_t mk = max_k(fmt, fp32_act, dev);
+  if (K > mk)
+    return set_error(ASM_E_UNSUPPORTED, "%s: K=%lld exceeds the supported maximum %lld", name,
+                     (long long)K, (long long)mk);
+  return ASM_OK;
+}
+
+// Device view of a caller buffer: the pointer itself when it is device
+// memory on `dev`, else a staged copy (host -> device) in `slot`.
+int device_in(DeviceState& st, int dev, const void* p, size_t bytes, int slot, const void** out,
+              const char* name) {
+  int pdev = -1;
+  const PtrKind k = classify(p, &pdev);
+  if (k == kDevice) {
+    if (pdev != dev)
+      return set_error(ASM_E_INVALID, "%s: buffer lives on device %d but the current device is %d", name, pdev, dev);
+    *out = p;
+    return ASM_OK;
+  }
+  int rc = ensure_dev(st.dev[slot], bytes);
+  if (rc) return rc;
+  const void* src = p;
+  if (k == kHostPageable && slot == 2) {
+    // Small activation vectors go through pinned staging (true async DMA).
+    rc = ensure_host(st.host[0], bytes);
+    if (rc) return rc;
+    memcpy(st.host[0].p, p, bytes);
+    src = st.host[0].p;
+  }
+  cudaError_t e = cudaMemcpyAsync(st.dev[slot].p, src, bytes, cudaMemcpyHostToDevice, st.stream);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyAsync H2D");
+  *out = st.dev[slot].p;
+  return ASM_OK;
+}
+
+void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const float* s,
+                 const float* x, float* y, int64_t M, int64_t K) {
+  if (validate(name, w, s, x, y, M, K)) return;
+  if (M == 0) return;
+  DeviceState* stp = nullptr;
+  int dev = 0;
+  if (get_state(&stp, &dev)) return;
+  DeviceState& st = *stp;
+  if (check_max_k(name, fmt, fp32_act, K, dev)) return;
+  std::lock_guard<std::mutex> lk(st.mu);
+
+  MatvecArgs a;
+  a.fmt = fmt;
+  a.fp32_act = fp32_act;
+  a.M = M;
+  a.K = K;
+
+  // Weights: resident copy if registered, else the caller's device buffer or a staged copy.
+  bool have_w = false;
+  if (K > 0) {
+    std::lock_guard<std::mutex> rl(g_reg_mu);
+    auto it = g_reg.find(w);
+    if (it != g_reg.end() && it->second.host_s == s && it->second.M == M && it->second.K == K &&
+        it->second.fmt == fmt && it->second.dev == dev) {
+      a.w = it->second.d_w;
+      a.scales = it->second.d_s;
+      a.scales_f16 = it->second.f16;
+      have_w = true;
+    }
+  }
+  if (K > 0 && !have_w) {
+    if (device_in(st, dev, w, weight_bytes(fmt, M, K), 0, &a.w, name)) return;
+    if (device_in(st, dev, s, (size_t)M * (K / 32) * sizeof(float), 1, &a.scales, name)) return;
+  }
+  if (K > 0) {
+    const void* dx = nullptr;
+    if (device_in(st, dev, x, (size_t)K * sizeof(float), 2, &dx, name)) return;
+    a.x = static_cast<const float*>(dx);
+  }
+
+  int ydev = -1;
+  const PtrKind yk = classify(y, &ydev);
+  const size_t ybytes = (size_t)M * sizeof(float);
+  if (yk == kDevice) {
+    if (ydev != dev) {
+      set_error(ASM_E_INVALID, "%s: y lives on device %d but the current device is %d", name, ydev, dev);
+      return;
+    }
+    a.y = y;
+  } else {
+    if (ensure_dev(st.dev[3], ybytes)) return;
+    a.y = static_cast<float*>(st.dev[3].p);
+  }
+
+  cudaError_t e = launch_matvec(a, st.stream);
+  if (e != cudaSuccess) {
+    cuda_error(e, name);
+    return;
+  }
+  float* ybounce = nullptr;
+  if (yk == kHostPinned) {
+    e = cudaMemcpyAsync(y, a.y, ybytes, cudaMemcpyDeviceToHost, st.stream);
+  } else if (yk == kHostPageable) {
+    if (ensure_host(st.host[1], ybytes)) return;
+    ybounce = static_cast<float*>(st.host[1].p);
+    e = cudaMemcpyAsync(ybounce, a.y, ybytes, cudaMemcpyDeviceToHost, st.stream);
+  }
+  if (e != cudaSuccess) {
+    cuda_error(e, "cudaMemcpyAsync D2H");
+    return;
+  }
+  e = cudaStreamSynchronize(st.stream);
+  if (e != cudaSuccess) {
+    cuda_error(e, name);
+    return;
+  }
+  if (ybounce) memcpy(y, ybounce, ybytes);
+}
+
+// --------------------------------------------------------------------------
+// Async entries: device pointers only
+// --------------------------------------------------------------------------
+int require_device(const char* name, const void* p, const char* what) {
+  int pdev = -1;
+  if (classify(p, &pdev) != kDevice)
+    return set_error(ASM_E_NOT_DEVICE, "%s: %s is not a device pointer", name, what);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (pdev != cur)
+    return set_error(ASM_E_INVALID, "%s: %s lives on device %d, current device is %d", name, what, pdev, cur);
+  return ASM_OK;
+}
+
+int async_matvec(const char* name, int fmt, bool fp32_act, bool f16s, const void* w, const void* s,
+                 const float* x, float* y, int32_t* isums, int64_t M, int64_t K, void* stream) {
+  int rc = validate(name, w, s, x, y, M, K);
+  if (rc) return rc;
+  if (M == 0) return ASM_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if ((rc = check_max_k(name, fmt, fp32_act, K, dev))) return rc;
+  if ((rc = require_device(name, y, "y"))) return rc;
+  if (K > 0) {
+    if ((rc = require_device(name, w, "qweights"))) return rc;
+    if ((rc = require_device(name, s, "scales"))) return rc;
+    if ((rc = require_device(name, x, "x"))) return rc;
+  }
+  if (isums && (rc = require_device(name, isums, "isums"))) return rc;
+  MatvecArgs a;
+  a.fmt = fmt;
+  a.fp32_act = fp32_act;
+  a.scales_f16 = f16s;
+  a.w = w;
+  a.scales = s;
+  a.x = x;
+  a.y = y;
+  a.isums = isums;
+  a.M = M;
+  a.K = K;
+  e = launch_matvec(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+}  // namespace
+
+// ==========================================================================
+// Exported entry points
+// ==========================================================================
+extern "C" {
+
+ASMLLM_API void asm_matmul_q4(const uint8_t* qweights, const float* scales, const float* x,
+                              float* y, int64_t M, int64_t K) {
+  sync_matvec("asm_matmul_q4", kFmtQ4_0, false, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q4_avx512(const uint8_t* qweights, const float* scales,
+                                     const float* x, float* y, int64_t M, int64_t K) {
+  sync_matvec("asm_matmul_q4_avx512", kFmtQ4_0, true, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q4_f32(const uint8_t* qweights, const float* scales, const float* x,
+                                  float* y, int64_t M, int64_t K) {
+  sync_matvec("asm_matmul_q4_f32", kFmtQ4_0, true, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q8(const int8_t* qweights, const float* scales, const float* x,
+                              float* y, int64_t M, int64_t K) {
+  sync_matvec("asm_matmul_q8", kFmtQ8_0, true, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q8q8(const int8_t* qweights, const float* scales, const float* x,
+                                float* y, int64_t M, int64_t K) {
+  sync_matvec("asm_matmul_q8q8", kFmtQ8_0, false, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q4_mt(const uint8_t* qweights, const float* scales, const float* x,
+                                 float* y, int64_t M, int64_t K, int num_threads) {
+  (void)num_threads;
+  sync_matvec("asm_matmul_q4_mt", kFmtQ4_0, false, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q4_avx512_mt(const uint8_t* qweights, const float* scales,
+                                        const float* x, float* y, int64_t M, int64_t K,
+                                        int num_threads) {
+  (void)num_threads;
+  sync_matvec("asm_matmul_q4_avx512_mt", kFmtQ4_0, true, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q8_mt(const int8_t* qweights, const float* scales, const float* x,
+                                 float* y, int64_t M, int64_t K, int num_threads) {
+  (void)num_threads;
+  sync_matvec("asm_matmul_q8_mt", kFmtQ8_0, true, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_threadpool_dispatch_q8(const int8_t* qweights, const float* scales,
+                                           const float* x, float* y, int64_t M, int64_t K) {
+  sync_matvec("asm_threadpool_dispatch_q8", kFmtQ8_0, true, qweights, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_threadpool_init(int num_threads) {
+  g_num_threads = num_threads;
+  DeviceState* st = nullptr;
+  get_state(&st, nullptr);
+}
+
+ASMLLM_API void asm_threadpool_shutdown(void) {
+  {
+    std::lock_guard<std::mutex> rl(g_reg_mu);
+    for (auto& kv : g_reg) free_entry(kv.second);
+    g_reg.clear();
+  }
+  int cur = 0;
+  cudaGetDevice(&cur);
+  for (int d = 0; d < kMaxDev; ++d) {
+    DeviceState& st = g_state[d];
+    std::lock_guard<std::mutex> lk(st.mu);
+    if (!st.init) continue;
+    cudaSetDevice(d);
+    cudaStreamSynchronize(st.stream);
+    for (auto& b : st.dev) {
+      if (b.p) cudaFree(b.p);
+      b = Buf();
+    }
+    for (auto& b : st.host) {
+      if (b.p) cudaFreeHost(b.p);
+      b = Buf();
+    }
+    cudaStreamDestroy(st.stream);
+    st.stream = nullptr;
+    st.init = false;
+  }
+  cudaSetDevice(cur);
+  {
+    std::lock_guard<std::mutex> lk(g_kind_mu);
+    g_kind_cache.clear();
+  }
+  g_num_threads = 0;
+}
+
+ASMLLM_API int asm_threadpool_get_num_threads(void) { return g_num_threads; }
+
+ASMLLM_API void asm_quantize_q8_0(const float* x, int8_t* xq, float* xd, int64_t K) {
+  const char* name = "asm_quantize_q8_0";
+  if (K < 0 || K % 32 != 0) {
+    set_error(ASM_E_INVALID, "%s: K=%lld must be a non-negative multiple of 32", name, (long long)K);
+    return;
+  }
+  if (K == 0) return;
+  if (!x || !xq || !xd) {
+    set_error(ASM_E_INVALID, "%s: NULL pointer", name);
+    return;
+  }
+  DeviceState* stp = nullptr;
+  int dev = 0;
+  if (get_state(&stp, &dev)) return;
+  DeviceState& st = *stp;
+  std::lock_guard<std::mutex> lk(st.mu);
+  const int64_t nb = K / 32;
+  const void* dx = nullptr;
+  if (device_in(st, dev, x, (size_t)K * 4, 2, &dx, name)) return;
+  int qdev = -1, ddev = -1;
+  const PtrKind qk = classify(xq, &qdev), dk = classify(xd, &ddev);
+  int8_t* dq = xq;
+  float* dd = xd;
+  // Outputs that are host memory are produced in the weight staging slots.
+  if (qk != kDevice) {
+    if (ensure_dev(st.dev[0], (size_t)K)) return;
+    dq = static_cast<int8_t*>(st.dev[0].p);
+  }
+  if (dk != kDevice) {
+    if (ensure_dev(st.dev[1], (size_t)nb * 4)) return;
+    dd = static_cast<float*>(st.dev[1].p);
+  }
+  cudaError_t e = launch_quantize(static_cast<const float*>(dx), dq, dd, nb, st.stream);
+  if (e != cudaSuccess) {
+    cuda_error(e, name);
+    return;
+  }
+  if (qk != kDevice) e = cudaMemcpyAsync(xq, dq, (size_t)K, cudaMemcpyDeviceToHost, st.stream);
+  if (e == cudaSuccess && dk != kDevice)
+    e = cudaMemcpyAsync(xd, dd, (size_t)nb * 4, cudaMemcpyDeviceToHost, st.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st.stream);
+  if (e != cudaSuccess) cuda_error(e, name);
+}
+
+ASMLLM_API int asm_weights_register(const void* qweights, const float* scales, int64_t M,
+                                    int64_t K, int fmt) {
+  const char* name = "asm_weights_register";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0)
+    return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 (Q4_0) or 8 (Q8_0)", name, fmt);
+  if (M <= 0 || K <= 0) return set_error(ASM_E_INVALID, "%s: M and K must be positive", name);
+  int rc = validate(name, qweights, scales, scales, scales, M, K);
+  if (rc) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (classify(qweights, nullptr) == kDevice || classify(scales, nullptr) == kDevice)
+    return set_error(ASM_E_INVALID, "%s: expects host buffers (device buffers are already resident)", name);
+  asm_weights_unregister(qweights);
+
+  const size_t wb = weight_bytes(fmt, M, K);
+  const size_t n = (size_t)M * (size_t)(K / 32);
+  // fp16 scales when every scale survives the round trip exactly.
+  bool f16 = true;
+  std::vector<__half> hs(n);
+  for (size_t i = 0; i < n; ++i) {
+    hs[i] = __float2half_rn(scales[i]);
+    const float back = __half2float(hs[i]);
+    if (!(back == scales[i]) && !(back != back && scales[i] != scales[i])) {
+      f16 = false;
+      break;
+    }
+  }
+  RegEntry r;
+  r.host_w = qweights;
+  r.host_s = scales;
+  r.M = M;
+  r.K = K;
+  r.fmt = fmt;
+  r.dev = dev;
+  r.f16 = f16;
+  const size_t sb = n * (f16 ? 2 : 4);
+  if ((e = cudaMalloc(&r.d_w, wb)) != cudaSuccess) return cuda_error(e, "cudaMalloc (weights)");
+  if ((e = cudaMalloc(&r.d_s, sb)) != cudaSuccess) {
+    cudaFree(r.d_w);
+    return cuda_error(e, "cudaMalloc (scales)");
+  }
+  e = cudaMemcpy(r.d_w, qweights, wb, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(r.d_s, f16 ? (const void*)hs.data() : (const void*)scales, sb, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    free_entry(r);
+    return cuda_error(e, "cudaMemcpy (register)");
+  }
+  r.bytes = wb + sb;
+  std::lock_guard<std::mutex> rl(g_reg_mu);
+  g_reg[qweights] = r;
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_weights_unregister(const void* qweights) {
+  std::lock_guard<std::mutex> rl(g_reg_mu);
+  auto it = g_reg.find(qweights);
+  if (it == g_reg.end()) return ASM_OK;
+  // Calls on the library streams that may still read the copy finish first.
+  for (int d = 0; d < kMaxDev; ++d)
+    if (g_state[d].init) cudaStreamSynchronize(g_state[d].stream);
+  free_entry(it->second);
+  g_reg.erase(it);
+  return ASM_OK;
+}
+
+ASMLLM_API int64_t asm_weights_resident_bytes(int* count) {
+  std::lock_guard<std::mutex> rl(g_reg_mu);
+  int64_t total = 0;
+  for (auto& kv : g_reg) total += (int64_t)kv.second.bytes;
+  if (count) *count = (int)g_reg.size();
+  return total;
+}
+
+ASMLLM_API int asm_get_last_error(char* buf, size_t n) {
+  const int code = t_err_code;
+  if (buf && n) {
+    const size_t len = t_err_msg.size() < n - 1 ? t_err_msg.size() : n - 1;
+    memcpy(buf, t_err_msg.data(), len);
+    buf[len] = '\0';
+  }
+  t_err_code = ASM_OK;
+  t_err_msg.clear();
+  return code;
+}
+
+ASMLLM_API int asm_matmul_q4_async(const uint8_t* qweights, const float* scales, const float* x,
+                                   float* y, int64_t M, int64_t K, void* stream) {
+  return async_matvec("asm_matmul_q4_async", kFmtQ4_0, false, false, qweights, scales, x, y,
+                      nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_matmul_q4_f16s_async(const uint8_t* qweights, const uint16_t* scales_f16,
+                                        const float* x, float* y, int64_t M, int64_t K,
+                                        void* stream) {
+  return async_matvec("asm_matmul_q4_f16s_async", kFmtQ4_0, false, true, qweights, scales_f16, x,
+                      y, nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_matmul_q8q8_async(const int8_t* qweights, const float* scales, const float* x,
+                                     float* y, int64_t M, int64_t K, void* stream) {
+  return async_matvec("asm_matmul_q8q8_async", kFmtQ8_0, false, false, qweights, scales, x, y,
+                      nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_matmul_q8q8_f16s_async(const int8_t* qweights, const uint16_t* scales_f16,
+                                          const float* x, float* y, int64_t M, int64_t K,
+                                          void* stream) {
+  return async_matvec("asm_matmul_q8q8_f16s_async", kFmtQ8_0, false, true, qweights, scales_f16,
+                      x, y, nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_matmul_q4_f32_async(const uint8_t* qweights, const float* scales,
+                                       const float* x, float* y, int64_t M, int64_t K,
+                                       void* stream) {
+  return async_matvec("asm_matmul_q4_f32_async", kFmtQ4_0, true, false, qweights, scales, x, y,
+                      nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_matmul_q8_async(const int8_t* qweights, const float* scales, const float* x,
+                                   float* y, int64_t M, int64_t K, void* stream) {
+  return async_matvec("asm_matmul_q8_async", kFmtQ8_0, true, false, qweights, scales, x, y,
+                      nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_block_sums_async(int fmt, const void* qweights, const float* scales,
+                                    const float* x, float* y, int32_t* isums, int64_t M,
+                                    int64_t K, void* stream) {
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0)
+    return set_error(ASM_E_INVALID, "asm_block_sums_async: fmt %d is not 2 or 8", fmt);
+  if (M > 0 && K > 0 && !isums) return set_error(ASM_E_INVALID, "asm_block_sums_async: isums is NULL");
+  return async_matvec("asm_block_sums_async", fmt, false, false, qweights, scales, x, y, isums, M,
+                      K, stream);
+}
+
+ASMLLM_API int asm_quantize_q8_0_async(const float* x, int8_t* xq, float* xd, int64_t N,
+                                       int64_t K, void* stream) {
+  const char* name = "asm_quantize_q8_0_async";
+  if (N < 0 || K < 0 || K % 32 != 0)
+    return set_error(ASM_E_INVALID, "%s: N=%lld K=%lld (K must be a multiple of 32)", name,
+                     (long long)N, (long long)K);
+  if (N == 0 || K == 0) return ASM_OK;
+  int rc;
+  if ((rc = require_device(name, x, "x")) || (rc = require_device(name, xq, "xq")) ||
+      (rc = require_device(name, xd, "xd")))
+    return rc;
+  cudaError_t e = launch_quantize(x, xq, xd, N * (K / 32), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_gguf_split_async(int fmt, const uint8_t* raw, uint8_t* qs, void* scales,
+                                    int scales_are_f16, int64_t nblocks, void* stream) {
+  const char* name = "asm_gguf_split_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0)
+    return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (nblocks < 0) return set_error(ASM_E_INVALID, "%s: negative block count", name);
+  if (nblocks == 0) return ASM_OK;
+  if ((uintptr_t)raw % 2 != 0 || (uintptr_t)qs % 4 != 0)
+    return set_error(ASM_E_INVALID, "%s: raw must be 2-byte and qs 4-byte aligned", name);
+  int rc;
+  if ((rc = require_device(name, raw, "raw")) || (rc = require_device(name, qs, "qs")) ||
+      (rc = require_device(name, scales, "scales")))
+    return rc;
+  cudaError_t e = launch_gguf_split(fmt, raw, qs, scales, scales_are_f16 ? 1 : 0, nblocks,
+                                    static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int64_t asm_max_k(int fmt, int fp32_activations) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return max_k(fmt == kFmtQ8_0 ? kFmtQ8_0 : kFmtQ4_0, fp32_activations != 0, dev);
+}
+
+ASMLLM_API const char* asm_version(void) { return "asmllm-b200 0.1 (sm_100a)"; }
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+"""Loads build/libasmllm.so (the sm_100a C-ABI library) with ctypes.
+
+Mirrors the reference's loader `try_load_native_library`
+(THRISHAL12345/asmllm tests/correctness/test_runner.py:52-68), which looks for
+build/libasmllm.so under the project root, with two differences: the library
+is built from asmllm_b200/csrc when it is missing or stale, and a failure to
+build or load raises instead of returning None.  There is no CPU fallback:
+every op in this package runs through this library.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+ASM_OK, ASM_E_INVALID, ASM_E_UNSUPPORTED, ASM_E_CUDA, ASM_E_NOT_DEVICE = 0, 1, 2, 3, 4
+FMT_Q4_0, FMT_Q8_0 = 2, 8
+
+vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+
+# name -> (argtypes, restype); every symbol include/asmllm.h declares.
+SIGNATURES = {
+    # reference ABI
+    "asm_matmul_q4": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_matmul_q4_avx512": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_matmul_q8": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_matmul_q4_mt": ([vp, vp, vp, vp, i64, i64, c_int], None),
+    "asm_matmul_q8_mt": ([vp, vp, vp, vp, i64, i64, c_int], None),
+    "asm_matmul_q4_avx512_mt": ([vp, vp, vp, vp, i64, i64, c_int], None),
+    "asm_threadpool_init": ([c_int], None),
+    "asm_threadpool_shutdown": ([], None),
+    "asm_threadpool_get_num_threads": ([], c_int),
+    "asm_threadpool_dispatch_q8": ([vp, vp, vp, vp, i64, i64], None),
+    # additions
+    "asm_matmul_q8q8": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_quantize_q8_0": ([vp, vp, vp, i64], None),
+    "asm_matmul_q4_f32": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_weights_register": ([vp, vp, i64, i64, c_int], c_int),
+    "asm_weights_unregister": ([vp], c_int),
+    "asm_weights_resident_bytes": ([ctypes.POINTER(c_int)], i64),
+    "asm_get_last_error": ([ctypes.c_char_p, ctypes.c_size_t], c_int),
+    "asm_matmul_q4_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matmul_q4_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matmul_q8q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matmul_q8q8_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matmul_q4_f32_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matmul_q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_quantize_q8_0_async": ([vp, vp, vp, i64, i64, vp], c_int),
+    "asm_block_sums_async": ([c_int, vp, vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_gguf_split_async": ([c_int, vp, vp, vp, c_int, i64, vp], c_int),
+    "asm_max_k": ([c_int, c_int], i64),
+    "asm_version": ([], ctypes.c_char_p),
+}
+
+
+class AsmError(RuntimeError):
+    """A libasmllm entry point reported an error through asm_get_last_error."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(f"asmllm error {code}: {message}")
+        self.code = code
+
+
+def library_path():
+    return _build.LIB_PATH
+
+
+def try_load_native_library() -> ctypes.CDLL:
+    """Returns the loaded library, building it first if needed; raises on failure."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = _build.build()
+            L = ctypes.CDLL(str(path))
+            for name, (argt, rest) in SIGNATURES.items():
+                f = getattr(L, name)
+                f.argtypes = argt
+                f.restype = rest
+            _lib = L
+    return _lib
+
+
+lib = try_load_native_library
+
+
+def last_error():
+    """(code, message) of the calling thread's last library error; clears it."""
+    buf = ctypes.create_string_buffer(1024)
+    code = lib().asm_get_last_error(buf, len(buf))
+    return code, buf.value.decode(errors="replace")
+
+
+def check(rc=None):
+    """Raises AsmError if the last call failed (rc != 0 or an error is pending)."""
+    code, msg = last_error()
+    if rc not in (None, 0) and code == 0:
+        code, msg = rc, "call failed"
+    if code != 0:
+        raise AsmError(code, msg)

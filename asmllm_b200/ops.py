@@ -1,0 +1,247 @@
+"""Python operator API over libasmllm.so.
+
+Two layers, both going through the C ABI (no Python or torch compute path):
+
+* Host layer -- numpy in, numpy out, through the reference's synchronous
+  entry points (`asm_matmul_q4`, `asm_matmul_q8`, ...), exactly as the
+  reference's ctypes callers use them (THRISHAL12345/asmllm
+  tests/correctness/test_runner.py:84-111, src/runtime/generate.py:255-259).
+* Device layer -- torch CUDA tensors, stream-ordered on torch's current
+  stream through the `*_async` entries; this is what the decode driver and
+  the benchmark use with weights resident in HBM.
+
+Argument meanings follow the reference: qweights Q4_0 uint8 [M, K/32, 16]
+(or flat), Q8_0 int8 [M, K/32, 32], scales [M, K/32], x fp32 [K], y fp32 [M].
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import native
+from .native import FMT_Q4_0, FMT_Q8_0, AsmError
+
+# --------------------------------------------------------------------------
+# Host (numpy) layer: the reference-facing synchronous ABI
+# --------------------------------------------------------------------------
+
+
+def _np(a, dtype):
+    return np.ascontiguousarray(a, dtype=dtype)
+
+
+def _mk(qw, scales, x, wdtype, bytes_per_block):
+    qw = _np(qw, wdtype)
+    scales = _np(scales, np.float32)
+    x = _np(x, np.float32)
+    K = x.shape[-1]
+    M = scales.shape[0] if scales.ndim >= 2 else (qw.size // max(1, (K // 32) * bytes_per_block) if K else 0)
+    return qw, scales, x, int(M), int(K)
+
+
+def _sync_call(name, qw, scales, x, wdtype, bpb, *extra):
+    qw, scales, x, M, K = _mk(qw, scales, x, wdtype, bpb)
+    y = np.zeros(M, dtype=np.float32)
+    getattr(native.lib(), name)(qw.ctypes.data, scales.ctypes.data, x.ctypes.data,
+                                y.ctypes.data, M, K, *extra)
+    native.check()
+    return y
+
+
+def matmul_q4(qweights, scales, x):
+    """asm_matmul_q4: Q4_0 x Q8_0 (x quantized inside, NEON semantics)."""
+    return _sync_call("asm_matmul_q4", qweights, scales, x, np.uint8, 16)
+
+
+def matmul_q4_mt(qweights, scales, x, num_threads=4):
+    return _sync_call("asm_matmul_q4_mt", qweights, scales, x, np.uint8, 16, int(num_threads))
+
+
+def matmul_q4_avx512(qweights, scales, x):
+    """asm_matmul_q4_avx512: Q4_0 x fp32 (x86 semantics)."""
+    return _sync_call("asm_matmul_q4_avx512", qweights, scales, x, np.uint8, 16)
+
+
+def matmul_q4_f32(qweights, scales, x):
+    return _sync_call("asm_matmul_q4_f32", qweights, scales, x, np.uint8, 16)
+
+
+def matmul_q8(qweights, scales, x):
+    """asm_matmul_q8: Q8_0 x fp32 (x86 / NEON-scalar semantics)."""
+    return _sync_call("asm_matmul_q8", qweights, scales, x, np.int8, 32)
+
+
+def matmul_q8_mt(qweights, scales, x, num_threads=4):
+    return _sync_call("asm_matmul_q8_mt", qweights, scales, x, np.int8, 32, int(num_threads))
+
+
+def matmul_q8q8(qweights, scales, x):
+    """asm_matmul_q8q8: Q8_0 x Q8_0."""
+    return _sync_call("asm_matmul_q8q8", qweights, scales, x, np.int8, 32)
+
+
+def quantize_q8_0(x):
+    """asm_quantize_q8_0: fp32[K] -> (int8[K], fp32[K/32])."""
+    x = _np(x, np.float32)
+    K = x.shape[-1]
+    xq = np.zeros(K, dtype=np.int8)
+    xd = np.zeros(K // 32, dtype=np.float32)
+    native.lib().asm_quantize_q8_0(x.ctypes.data, xq.ctypes.data, xd.ctypes.data, K)
+    native.check()
+    return xq, xd
+
+
+def register_weights(qweights: np.ndarray, scales: np.ndarray, fmt: int) -> None:
+    """asm_weights_register on host arrays (kept alive by the caller)."""
+    scales = np.asarray(scales)
+    if not (qweights.flags.c_contiguous and scales.flags.c_contiguous and scales.dtype == np.float32):
+        raise ValueError("register_weights needs C-contiguous arrays and fp32 scales")
+    M = scales.shape[0]
+    K = scales.size // M * 32
+    rc = native.lib().asm_weights_register(qweights.ctypes.data, scales.ctypes.data, M, K, fmt)
+    native.check(rc)
+
+
+def unregister_weights(qweights: np.ndarray) -> None:
+    native.check(native.lib().asm_weights_unregister(qweights.ctypes.data))
+
+
+def threadpool_init(num_threads: int) -> None:
+    native.lib().asm_threadpool_init(int(num_threads))
+    native.check()
+
+
+def threadpool_shutdown() -> None:
+    native.lib().asm_threadpool_shutdown()
+
+
+def threadpool_get_num_threads() -> int:
+    return int(native.lib().asm_threadpool_get_num_threads())
+
+
+def max_k(fmt: int, fp32_activations: bool) -> int:
+    return int(native.lib().asm_max_k(fmt, 1 if fp32_activations else 0))
+
+
+# --------------------------------------------------------------------------
+# Device (torch) layer
+# --------------------------------------------------------------------------
+
+
+def _torch():
+    import torch  # imported lazily: the host layer needs no torch
+
+    return torch
+
+
+def _stream_handle(stream=None):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _check_dev(t, dtypes, name):
+    torch = _torch()
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name}: expected a CUDA tensor")
+    if t.dtype not in dtypes:
+        raise TypeError(f"{name}: dtype {t.dtype} not in {dtypes}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: tensor must be contiguous")
+
+
+def matvec(fmt: int, qweights, scales, x, out=None, *, fp32_activations=False, stream=None):
+    """y = W x on device tensors.
+
+    fmt: FMT_Q4_0 (qweights uint8 [M, K/32, 16]) or FMT_Q8_0 (int8 [M, K/32, 32]).
+    scales: fp32 or fp16 [M, K/32].  fp32_activations selects the x86 (fp32-x)
+    semantics instead of Q8_0-quantized activations (fp32 scales only).
+    """
+    torch = _torch()
+    wdt = torch.uint8 if fmt == FMT_Q4_0 else torch.int8
+    _check_dev(qweights, (wdt,), "qweights")
+    _check_dev(scales, (torch.float32, torch.float16), "scales")
+    _check_dev(x, (torch.float32,), "x")
+    M = scales.shape[0]
+    K = x.shape[-1]
+    if scales.numel() != M * (K // 32) or qweights.numel() != M * (K // 32) * (16 if fmt == FMT_Q4_0 else 32):
+        raise ValueError(f"shape mismatch: qweights {tuple(qweights.shape)}, scales {tuple(scales.shape)}, K={K}")
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=x.device)
+    else:
+        _check_dev(out, (torch.float32,), "out")
+    L = native.lib()
+    f16 = scales.dtype == torch.float16
+    st = _stream_handle(stream)
+    args = (_ptr(qweights), _ptr(scales), _ptr(x), _ptr(out), M, K, st)
+    if fp32_activations:
+        if f16:
+            raise ValueError("fp32-activation kernels take fp32 scales")
+        rc = (L.asm_matmul_q4_f32_async if fmt == FMT_Q4_0 else L.asm_matmul_q8_async)(*args)
+    elif fmt == FMT_Q4_0:
+        rc = (L.asm_matmul_q4_f16s_async if f16 else L.asm_matmul_q4_async)(*args)
+    else:
+        rc = (L.asm_matmul_q8q8_f16s_async if f16 else L.asm_matmul_q8q8_async)(*args)
+    native.check(rc)
+    return out
+
+
+def quantize_q8_0_dev(x, xq=None, xd=None, stream=None):
+    """Device quantize of x fp32 [N, K] or [K] -> (int8 same shape, fp32 [..., K/32])."""
+    torch = _torch()
+    _check_dev(x, (torch.float32,), "x")
+    K = x.shape[-1]
+    N = x.numel() // K if K else 0
+    if xq is None:
+        xq = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    if xd is None:
+        xd = torch.empty((*x.shape[:-1], K // 32), dtype=torch.float32, device=x.device)
+    rc = native.lib().asm_quantize_q8_0_async(_ptr(x), _ptr(xq), _ptr(xd), N, K, _stream_handle(stream))
+    native.check(rc)
+    return xq, xd
+
+
+def block_sums_dev(fmt: int, qweights, scales, x, stream=None):
+    """(y, isums int32 [M, K/32]) from the matvec kernel's own debug instantiation."""
+    torch = _torch()
+    M = scales.shape[0]
+    K = x.shape[-1]
+    y = torch.empty(M, dtype=torch.float32, device=x.device)
+    isums = torch.empty((M, K // 32), dtype=torch.int32, device=x.device)
+    rc = native.lib().asm_block_sums_async(fmt, _ptr(qweights), _ptr(scales), _ptr(x), _ptr(y),
+                                           _ptr(isums), M, K, _stream_handle(stream))
+    native.check(rc)
+    return y, isums
+
+
+def gguf_split_dev(fmt: int, raw, nblocks: int, scales_f16: bool = True, stream=None):
+    """Split raw GGUF Q4_0 (18 B) / Q8_0 (34 B) blocks on the device.
+
+    Returns (qs uint8/int8 [nblocks, 16|32], scales fp16|fp32 [nblocks]).
+    Mirrors the reference's host split in src/runtime/generate.py:91-119.
+    """
+    torch = _torch()
+    _check_dev(raw, (torch.uint8,), "raw")
+    qb = 16 if fmt == FMT_Q4_0 else 32
+    if raw.numel() < nblocks * (qb + 2):
+        raise ValueError("raw buffer shorter than nblocks blocks")
+    qs = torch.empty((nblocks, qb), dtype=torch.uint8 if fmt == FMT_Q4_0 else torch.int8, device=raw.device)
+    scales = torch.empty(nblocks, dtype=torch.float16 if scales_f16 else torch.float32, device=raw.device)
+    rc = native.lib().asm_gguf_split_async(fmt, _ptr(raw), _ptr(qs), _ptr(scales), 1 if scales_f16 else 0,
+                                           nblocks, _stream_handle(stream))
+    native.check(rc)
+    return qs, scales
+
+
+__all__ = [
+    "AsmError", "FMT_Q4_0", "FMT_Q8_0",
+    "matmul_q4", "matmul_q4_mt", "matmul_q4_avx512", "matmul_q4_f32", "matmul_q8", "matmul_q8_mt",
+    "matmul_q8q8", "quantize_q8_0", "register_weights", "unregister_weights", "threadpool_init",
+    "threadpool_shutdown", "threadpool_get_num_threads", "max_k", "matvec", "quantize_q8_0_dev",
+    "block_sums_dev", "gguf_split_dev",
+]

@@ -1,0 +1,492 @@
+#!/usr/bin/env python3
+"""Benchmark of the Q4_0 x Q8_0 matvec hot path on B200 (one JSON line on rank 0).
+
+Workload (one "step"): one Q4_0 x Q8_0 matvec at each Llama-7B shape of the
+benchmark sweep -- 4096x4096, 11008x4096, 4096x11008, 32000x4096, batch 1 --
+on weights resident in HBM (GGUF Q4_0 blocks: 16 nibble bytes + fp16 scale),
+x fp32 N(0,1) quantized to Q8_0 inside the kernel.  Steps rotate over 3
+weight copies (402 MB working set, > 3x the 126 MB L2), so every launch
+streams its weights from HBM.  Synthetic seeded data, no model file.
+
+  value   = algorithmic bytes of all steps on all ranks / device time (max over
+            ranks), GB/s; bytes per matvec = M*K/32*18 (GGUF-native) + 4K + 4M.
+  e2e     = the same metric through the reference-facing C ABI
+            (asm_matmul_q4, host buffers: pinned x in, pinned y out, weights
+            registered once), host copies inside the timed region.
+  roofline, cpu_baseline, clocks: see DESIGN.md.
+
+Launch: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+(N > 1 under torch.distributed.run: one rank per GPU, weak scaling, no
+data-path collective; timing barrier and max-over-ranks use NCCL.)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+COPIES = 3
+L2_BYTES = 126 * 1024 * 1024
+METRIC = "Q4_0 matvec HBM GB/s (% roofline); 7B Q4_0 decode tokens/s at batch 1"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def q4_bytes(M, K):
+    return M * (K // 32) * 18 + 4 * K + 4 * M
+
+
+def q8_bytes(M, K):
+    return M * (K // 32) * 34 + 4 * K + 4 * M
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "roofline_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("sweep_avg_dram_bytes_per_launch="):
+            return float(line.split("=", 1)[1])
+    return None
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region (recipe's clocks line)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.gpus = set(gpu_indices)
+        self.proc = None
+        self.out = Path(os.environ.get("ASMLLM_CLOCKS_CSV", "/tmp/asmllm_clocks_%d.csv" % os.getpid()))
+
+    def start(self):
+        try:
+            self.fh = open(self.out, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.read_text().splitlines():
+            f = [t.strip() for t in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                idx = int(f[0])
+            except ValueError:
+                continue
+            if idx not in self.gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        try:
+            self.out.unlink()
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "power_w_max": max(power) if power else None}
+
+
+# --------------------------------------------------------------------------
+# CPU side: oracle port timed on the host cores (cpu_baseline and --impl reference)
+# --------------------------------------------------------------------------
+
+def cpu_sweep_gbs(budget_s, threads, copies=1):
+    """Times the oracle's multi-thread Q4_0 x Q8_0 (NEON semantics, threadpool
+    tiling) on the four sweep shapes; returns (GB/s, sweeps, seconds)."""
+    import numpy as np
+
+    from asmllm_b200 import synth
+    from oracle import oracle as O
+
+    data = []
+    for i, (M, K) in enumerate(SHAPES):
+        qs, s = synth.q4_0_weights(M, K, seed=100 + i)
+        data.append((qs, s, synth.activation(K, seed=200 + i), M, K))
+    sweep_bytes = sum(q4_bytes(M, K) for _, _, _, M, K in data)
+    # one untimed sweep (page-in)
+    for qs, s, x, M, K in data:
+        O.matmul_mt(O.K_Q4Q8, qs, s, x, M, K, threads)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        for qs, s, x, M, K in data:
+            O.matmul_mt(O.K_Q4Q8, qs, s, x, M, K, threads)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 10000:
+            break
+    return sweep_bytes * n / el / 1e9, n, el
+
+
+def run_reference(args, rank, world):
+    """The reference arm: the oracle port of the reference's CPU path, all host threads.
+
+    Each step is a bounded sample of the sweep: the first `rows` of every shape
+    (the same fraction for all four, whole 16-row tiles), sized from one
+    untimed full sweep so the --steps run stays near REF_BUDGET_S seconds."""
+    if rank != 0:
+        return
+    from asmllm_b200 import synth
+    from oracle import oracle as O
+
+    REF_BUDGET_S = 100.0
+    threads = O.host_threads()
+    data = []
+    for i, (M, K) in enumerate(SHAPES):
+        qs, s = synth.q4_0_weights(M, K, seed=100 + i)
+        data.append((qs, s, synth.activation(K, seed=200 + i), M, K))
+
+    def sweep(frac):
+        nbytes = 0
+        for qs, s, x, M, K in data:
+            rows = M if frac >= 1.0 else max(16, min(M, int(math.ceil(M * frac / 16.0)) * 16))
+            O.matmul_mt(O.K_Q4Q8, qs[:rows], s[:rows], x, rows, K, threads)
+            nbytes += q4_bytes(rows, K)
+        return nbytes
+
+    t0 = time.perf_counter()
+    sweep(1.0)
+    t_full = time.perf_counter() - t0
+    frac = min(1.0, REF_BUDGET_S / max(1e-9, args.steps * t_full))
+    for _ in range(max(1, args.warmup)):
+        sweep(frac)
+    nbytes = 0
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        nbytes += sweep(frac)
+    el = time.perf_counter() - t0
+    gbs = nbytes / el / 1e9
+    sample = (f"{args.steps} steps, each the first {frac * 100:.1f}% of the rows of each of the 4 shapes "
+              f"({nbytes / args.steps / 1e6:.1f} MB/step), after {max(1, args.warmup)} untimed; C restatement of "
+              "the NEON asm_matmul_q4 with the reference threadpool tiling (the reference NASM/GAS cannot be "
+              "assembled here: no nasm, no aarch64 toolchain)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "Q4_0xQ8_0 matvec sweep: 4096x4096, 11008x4096, 4096x11008, 32000x4096, batch 1",
+                   "weights": "fp32-scale ABI layout in host RAM", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+# GPU side
+# --------------------------------------------------------------------------
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30000)
+    ap.add_argument("--warmup", type=int, default=60)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--e2e-steps", type=int, default=2000)
+    ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--no-extras", action="store_true", help="skip per-shape / Q8 breakdown")
+    args = ap.parse_args()
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from asmllm_b200 import native, ops
+    from asmllm_b200.native import FMT_Q4_0, FMT_Q8_0
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    native.try_load_native_library()
+    dev = torch.device("cuda", local)
+    gen = torch.Generator(device=dev)
+
+    def make_q4(M, K, seed):
+        gen.manual_seed(seed)
+        qs = torch.randint(0, 256, (M, K // 32, 16), dtype=torch.uint8, device=dev, generator=gen)
+        d = torch.randn((M, K // 32), device=dev, generator=gen).mul_(0.02).abs_().half()
+        return qs, d
+
+    def make_q8(M, K, seed):
+        gen.manual_seed(seed)
+        qs = torch.randint(-127, 128, (M, K // 32, 32), dtype=torch.int8, device=dev, generator=gen)
+        d = torch.randn((M, K // 32), device=dev, generator=gen).mul_(0.002).abs_().half()
+        return qs, d
+
+    base = 1000 * rank
+    W4 = [[make_q4(M, K, base + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+    xs = {}
+    for K in sorted({K for _, K in SHAPES}):
+        gen.manual_seed(base + 500 + K)
+        xs[K] = torch.randn(K, device=dev, generator=gen)
+    ys = {M: torch.empty(M, device=dev) for M in sorted({M for M, _ in SHAPES})}
+    step_bytes = sum(q4_bytes(M, K) for M, K in SHAPES)
+
+    def step(c, W=W4, fmt=FMT_Q4_0, shapes=SHAPES):
+        for (qs, d), (M, K) in zip(W[c], shapes):
+            ops.matvec(fmt, qs, d, xs[K], out=ys[M])
+
+    # warm-up: eager steps (also primes the library's launch caches)
+    for i in range(max(3, args.warmup)):
+        step(i % COPIES)
+    torch.cuda.synchronize()
+
+    def capture(nsteps, fn):
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(nsteps):
+                    fn(i % COPIES)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        return g
+
+    K_steps = args.steps
+    G = min(K_steps, 300)
+    if G >= COPIES:
+        G -= G % COPIES
+    reps, rem = divmod(K_steps, G)
+    gA = capture(G, step)
+    gB = capture(rem, step) if rem else None
+    gA.replay()  # untimed
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    clocks = Clocks([local] if world == 1 else list(range(world))) if rank == 0 else None
+    barrier()
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)  # let nvidia-smi start sampling
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(reps):
+        gA.replay()
+    if gB is not None:
+        gB.replay()
+    ev1.record()
+    ev1.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop() if clocks else None
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total_bytes = step_bytes * K_steps * world
+    value = total_bytes / (ms / 1e3) / 1e9
+    launches = len(SHAPES) * K_steps
+    per_launch_ms = ms / launches
+    per_launch_bytes = step_bytes / len(SHAPES)
+    achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
+    del gA, gB
+
+    # ---- per-shape and Q8_0 x Q8_0 breakdown (not part of the timed value) ----
+    extras = {}
+    if not args.no_extras:
+        def time_graph(fn, n):
+            g = capture(n, fn)
+            g.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(5):
+                g.replay()
+            b.record()
+            b.synchronize()
+            return a.elapsed_time(b) / (5 * n)
+
+        per_shape = {}
+        for i, (M, K) in enumerate(SHAPES):
+            def one(c, i=i, M=M, K=K):
+                qs, d = W4[c][i]
+                ops.matvec(FMT_Q4_0, qs, d, xs[K], out=ys[M])
+            t = time_graph(one, 300)
+            per_shape[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q4_bytes(M, K) / (t / 1e3) / 1e9, 1)}
+        extras["q4q8_per_shape"] = per_shape
+        # Q8_0 x Q8_0 sweep on the same shapes
+        del W4
+        W8 = [[make_q8(M, K, base + 70 + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+        for i in range(COPIES):
+            step(i, W=W8, fmt=FMT_Q8_0)
+        t8 = time_graph(lambda c: step(c, W=W8, fmt=FMT_Q8_0), 60)
+        b8 = sum(q8_bytes(M, K) for M, K in SHAPES)
+        extras["q8q8_sweep"] = {"us_per_step": round(t8 * 1e3, 3), "GB/s": round(b8 / (t8 / 1e3) / 1e9, 1)}
+        per8 = {}
+        for i, (M, K) in enumerate(SHAPES):
+            def one8(c, i=i, M=M, K=K):
+                qs, d = W8[c][i]
+                ops.matvec(FMT_Q8_0, qs, d, xs[K], out=ys[M])
+            t = time_graph(one8, 300)
+            per8[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q8_bytes(M, K) / (t / 1e3) / 1e9, 1)}
+        extras["q8q8_per_shape"] = per8
+        del W8
+        torch.cuda.synchronize()
+        W4 = [[make_q4(M, K, base + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+
+    # ---- end to end through the reference-facing C ABI (host buffers) ----
+    L = native.lib()
+    host_w = []
+    for c in range(COPIES):
+        row = []
+        for (qs, d), (M, K) in zip(W4[c], SHAPES):
+            hq = qs.cpu().numpy()
+            hs = d.float().cpu().numpy()
+            ops.register_weights(hq, hs, FMT_Q4_0)
+            row.append((hq, hs, M, K))
+        host_w.append(row)
+    del W4
+    torch.cuda.empty_cache()
+    hx = {K: torch.from_numpy(xs[K].cpu().numpy()).pin_memory() for K in xs}
+    hy = {M: torch.empty(M, dtype=torch.float32).pin_memory() for M in ys}
+
+    def e2e_step(c):
+        for hq, hs, M, K in host_w[c]:
+            L.asm_matmul_q4(hq.ctypes.data, hs.ctypes.data, hx[K].data_ptr(), hy[M].data_ptr(), M, K)
+
+    for i in range(6):
+        e2e_step(i % COPIES)
+    native.check()
+    E = max(COPIES, min(args.e2e_steps, K_steps))
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(E):
+        e2e_step(i % COPIES)
+    el = time.perf_counter() - t0
+    native.check()
+    if world > 1:
+        t = torch.tensor([el], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        el = float(t.item())
+    e2e_val = step_bytes * E * world / el / 1e9
+    h2d = sum(4 * K for _, K in SHAPES)
+    d2h = sum(4 * M for M, _ in SHAPES)
+    for c in range(COPIES):
+        for hq, _, _, _ in host_w[c]:
+            ops.unregister_weights(hq)
+
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = load_peaks()
+    cpu = None
+    if world == 1:
+        from oracle import oracle as O
+
+        threads = O.host_threads()
+        gbs, n, sec = cpu_sweep_gbs(args.cpu_budget, threads)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": f"{n} sweeps of the 4 shapes in {sec:.1f} s; C restatement of the NEON asm_matmul_q4 "
+                         "with the reference threadpool row tiling (reference asm not assemblable here)"}
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": K_steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / K_steps, 6),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int8",
+        "data": "synthetic (seeded; GGUF Q4_0 d=fp16|N(0,0.02)|, nibbles U[0,15]; x N(0,1))",
+        "config": {
+            "workload": "Q4_0xQ8_0 matvec sweep: 4096x4096, 11008x4096, 4096x11008, 32000x4096, batch 1",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "weights_layout": "resident qs[M][K/32][16] + fp16 scales (18 B/block)",
+            "l2": f"rotating {COPIES} weight copies, {COPIES * step_bytes / 1e6:.0f} MB working set > 126 MB L2",
+            "launch": "CUDA graph replay of %d steps (%d kernels)" % (G, G * len(SHAPES)),
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "traffic": traffic,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback 6.65 TB/s",
+            "bytes_per_launch": round(per_launch_bytes),
+            "us_per_launch": round(per_launch_ms * 1e3, 3),
+        },
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "steps": E, "path": "asm_matmul_q4 (sync C ABI), registered host weights, pinned x/y"},
+        "gpu_launches": launches,
+        "clocks": clk,
+    }
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,194 @@
+/*
+ * include/asmllm.h -- C ABI of libasmllm.so, the B200 (sm_100a) implementation
+ * of asmllm's quantized matvec hot path.
+ *
+ * The first group keeps the exact names and signatures of the reference
+ * library's exports (THRISHAL12345/asmllm, exports list build_kernel.py:85-104,
+ * threadpool.h:37-102) so its ctypes callers load this library unchanged.
+ * The second group adds what the B200 path needs: stream-ordered entries on
+ * device pointers, Q8_0 x Q8_0, the standalone activation quantize, a
+ * block-sum probe, GGUF block splitting and an error channel.
+ *
+ * Conventions for every entry point:
+ *   - Q4_0 weights: uint8 [M][K/32][16]; byte j of a block holds element j in
+ *     its low nibble and element 16+j in its high nibble; value = nibble - 8
+ *     (reference tests/reference/ops.py:16-30).
+ *   - Q8_0 weights: int8 [M][K/32][32]; value = q.
+ *   - scales: one per (row, block), fp32 [M][K/32] (reference generate.py:91-119);
+ *     the *_f16s entries take fp16 scales instead (lossless for GGUF data).
+ *   - x: fp32 [K]; y: fp32 [M]; K must be a multiple of 32 (K = 0 gives y = 0).
+ *   - "Q4_0 x Q8_0" semantics = reference src/kernels/arm64/matmul_q4_neon.S:
+ *     x is quantized per 32-block with d = amax/127, q = sat8(RNE(x*127/amax)),
+ *     then y[r] = sum_b float(isum[r][b]) * (wd[r][b]*xd[b]).
+ *   - "fp32-x" semantics = reference src/kernels/x86_64/matmul_q{4,8}_avx2.asm:
+ *     y[r] = sum_b wd[r][b] * sum_i w[r][b][i]*x[b*32+i].
+ *
+ * Synchronous entries (the reference names) accept host or device pointers
+ * in any mix and return with y written, like the reference.  Host buffers are
+ * staged through device memory; weights registered with asm_weights_register
+ * stay resident in HBM and are not copied again.  They return void, like the
+ * reference; failures are reported on stderr and by asm_get_last_error().
+ *
+ * *_async entries take device pointers only, enqueue on `stream`
+ * (a cudaStream_t; NULL = legacy default stream) and return 0 or an ASM_E_*
+ * code.
+ */
+#ifndef ASMLLM_B200_H
+#define ASMLLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ASMLLM_API __attribute__((visibility("default")))
+
+/* Status codes of the int-returning entries. */
+#define ASM_OK 0
+#define ASM_E_INVALID 1     /* bad argument (negative size, K % 32 != 0, NULL) */
+#define ASM_E_UNSUPPORTED 2 /* size beyond what the kernel supports */
+#define ASM_E_CUDA 3        /* CUDA runtime error; text via asm_get_last_error */
+#define ASM_E_NOT_DEVICE 4  /* an *_async entry got a non-device pointer */
+
+/* ===================================================================== */
+/* 1. Reference ABI (drop-in)                                             */
+/* ===================================================================== */
+
+/* Q4_0 x Q8_0 matvec (quantizes x inside, NEON semantics).
+ * Replaces asm_matmul_q4: src/kernels/arm64/matmul_q4_neon.S:9-16,25-327
+ * (same symbol and signature as src/kernels/x86_64/matmul_q4_avx2.asm:12-19). */
+ASMLLM_API void asm_matmul_q4(const uint8_t* qweights, const float* scales,
+                              const float* x, float* y, int64_t M, int64_t K);
+
+/* Q4_0 x fp32 matvec (x86 semantics, no activation quantize).
+ * Replaces asm_matmul_q4_avx512: src/kernels/x86_64/matmul_q4_avx512.asm:57-279. */
+ASMLLM_API void asm_matmul_q4_avx512(const uint8_t* qweights, const float* scales,
+                                     const float* x, float* y, int64_t M, int64_t K);
+
+/* Q8_0 x fp32 matvec.
+ * Replaces asm_matmul_q8: src/kernels/x86_64/matmul_q8_avx2.asm:12-19,51-194
+ * and src/kernels/arm64/matmul_q8_neon.S:8-15,23-78. */
+ASMLLM_API void asm_matmul_q8(const int8_t* qweights, const float* scales,
+                              const float* x, float* y, int64_t M, int64_t K);
+
+/* Multi-thread entries: num_threads is accepted and ignored (one launch
+ * covers all rows).  Replace asm_matmul_q4_mt (src/runtime/threadpool.c:390-486,
+ * threadpool.h:49-57) and asm_matmul_q8_mt (threadpool.c:750-767,
+ * matmul_q8_avx2.asm:203-300, threadpool.h:59-67). */
+ASMLLM_API void asm_matmul_q4_mt(const uint8_t* qweights, const float* scales,
+                                 const float* x, float* y, int64_t M, int64_t K,
+                                 int num_threads);
+ASMLLM_API void asm_matmul_q8_mt(const int8_t* qweights, const float* scales,
+                                 const float* x, float* y, int64_t M, int64_t K,
+                                 int num_threads);
+/* Replaces asm_matmul_q4_avx512_mt (threadpool.c:489-586, built with AVX512_ENABLED):
+ * fp32-x semantics like asm_matmul_q4_avx512; num_threads ignored. */
+ASMLLM_API void asm_matmul_q4_avx512_mt(const uint8_t* qweights, const float* scales,
+                                        const float* x, float* y, int64_t M, int64_t K,
+                                        int num_threads);
+
+/* Pool management.  init records the thread count (returned by
+ * get_num_threads) and creates this device's stream and staging state;
+ * shutdown releases them and all registered weights.
+ * Replace threadpool.h:37,42,102 (threadpool.c:340-388). */
+ASMLLM_API void asm_threadpool_init(int num_threads);
+ASMLLM_API void asm_threadpool_shutdown(void);
+ASMLLM_API int asm_threadpool_get_num_threads(void);
+
+/* Q8_0 x fp32 dispatch with the current pool; same as asm_matmul_q8.
+ * Replaces asm_threadpool_dispatch_q8: threadpool.h:80-87, threadpool.c:588-665. */
+ASMLLM_API void asm_threadpool_dispatch_q8(const int8_t* qweights, const float* scales,
+                                           const float* x, float* y, int64_t M, int64_t K);
+
+/* ===================================================================== */
+/* 2. Additions for the B200 path                                         */
+/* ===================================================================== */
+
+/* Q8_0 x Q8_0 matvec (x quantized as in asm_matmul_q4, signed int8 block dot).
+ * No reference kernel: specified by composing matmul_q4_neon.S:57-143 with an
+ * int8 block dot and the combine of matmul_q4_neon.S:239-255. */
+ASMLLM_API void asm_matmul_q8q8(const int8_t* qweights, const float* scales,
+                                const float* x, float* y, int64_t M, int64_t K);
+
+/* fp32 -> Q8_0 activation quantize alone: xq int8[K], xd fp32[K/32].
+ * Exposes the quantize of matmul_q4_neon.S:57-143 (stack scratch :41-50)
+ * for bit-exact testing and for callers that quantize once for several matvecs. */
+ASMLLM_API void asm_quantize_q8_0(const float* x, int8_t* xq, float* xd, int64_t K);
+
+/* Q4_0 x fp32 matvec under an explicit name (same as asm_matmul_q4_avx512;
+ * the x86 AVX2 asm_matmul_q4 semantics, matmul_q4_avx2.asm:57-287). */
+ASMLLM_API void asm_matmul_q4_f32(const uint8_t* qweights, const float* scales,
+                                  const float* x, float* y, int64_t M, int64_t K);
+
+/* Keeps a copy of host weights resident in HBM.  Later synchronous calls that
+ * pass the same host `qweights` pointer (with the same scales pointer, M and
+ * K) use the resident copy instead of copying the weights again.  fmt: 2 =
+ * Q4_0, 8 = Q8_0 (GGUF type ids).  Scales are stored as fp16 when every
+ * scale converts to fp16 exactly, else as fp32.  The host buffers must not
+ * change while registered; register again after changing them.  This is the
+ * one-time "upload to HBM" of the reference's loader path
+ * (src/runtime/generate.py:169-180).  Returns ASM_OK or an ASM_E_* code. */
+ASMLLM_API int asm_weights_register(const void* qweights, const float* scales,
+                                    int64_t M, int64_t K, int fmt);
+ASMLLM_API int asm_weights_unregister(const void* qweights);
+/* Number of registered weight tensors and their resident bytes. */
+ASMLLM_API int64_t asm_weights_resident_bytes(int* count);
+
+/* Last error text of the calling thread (empty when none); returns its code
+ * and clears it.  The reference ABI returns void, so this is its error channel. */
+ASMLLM_API int asm_get_last_error(char* buf, size_t n);
+
+/* ---- Stream-ordered entries on device pointers ---------------------- */
+
+/* Q4_0 x Q8_0 (asm_matmul_q4 semantics).  scales fp32. */
+ASMLLM_API int asm_matmul_q4_async(const uint8_t* qweights, const float* scales,
+                                   const float* x, float* y, int64_t M, int64_t K,
+                                   void* stream);
+/* Same with fp16 scales (the resident/repacked layout: 18 bytes per block). */
+ASMLLM_API int asm_matmul_q4_f16s_async(const uint8_t* qweights, const uint16_t* scales_f16,
+                                        const float* x, float* y, int64_t M, int64_t K,
+                                        void* stream);
+ASMLLM_API int asm_matmul_q8q8_async(const int8_t* qweights, const float* scales,
+                                     const float* x, float* y, int64_t M, int64_t K,
+                                     void* stream);
+ASMLLM_API int asm_matmul_q8q8_f16s_async(const int8_t* qweights, const uint16_t* scales_f16,
+                                          const float* x, float* y, int64_t M, int64_t K,
+                                          void* stream);
+/* fp32-x semantics. */
+ASMLLM_API int asm_matmul_q4_f32_async(const uint8_t* qweights, const float* scales,
+                                       const float* x, float* y, int64_t M, int64_t K,
+                                       void* stream);
+ASMLLM_API int asm_matmul_q8_async(const int8_t* qweights, const float* scales,
+                                   const float* x, float* y, int64_t M, int64_t K,
+                                   void* stream);
+/* Batched quantize: N rows of x fp32[N][K] -> xq int8[N][K], xd fp32[N][K/32]. */
+ASMLLM_API int asm_quantize_q8_0_async(const float* x, int8_t* xq, float* xd,
+                                       int64_t N, int64_t K, void* stream);
+/* Per-block int32 sums of the Q4_0 x Q8_0 (fmt 2) or Q8_0 x Q8_0 (fmt 8)
+ * dot for every (row, block), written to isums int32[M][K/32], computed by
+ * the matvec kernel itself (its debug instantiation) so tests can check them
+ * bit for bit; y is written too. */
+ASMLLM_API int asm_block_sums_async(int fmt, const void* qweights, const float* scales,
+                                    const float* x, float* y, int32_t* isums,
+                                    int64_t M, int64_t K, void* stream);
+
+/* GGUF block split (reference generate.py:91-119): raw GGUF Q4_0 blocks
+ * (18 bytes: fp16 d + 16 nibble bytes) or Q8_0 blocks (34 bytes: fp16 d +
+ * 32 int8) for `nblocks` blocks -> qs plane (16 or 32 bytes per block) and a
+ * scale plane, fp32 (scales_are_f16 = 0) or fp16 (= 1). */
+ASMLLM_API int asm_gguf_split_async(int fmt, const uint8_t* raw, uint8_t* qs, void* scales,
+                                    int scales_are_f16, int64_t nblocks, void* stream);
+
+/* Largest K each matvec family supports (shared-memory staging of x). */
+ASMLLM_API int64_t asm_max_k(int fmt, int fp32_activations);
+
+/* Library version string. */
+ASMLLM_API const char* asm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASMLLM_B200_H */

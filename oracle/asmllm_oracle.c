@@ -1,0 +1,397 @@
+/*
+ * oracle/asmllm_oracle.c -- CPU restatement of asmllm's quantized matvec hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker, never the product:
+ * only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg and
+ * `--impl reference` arm may load it.  The shipped path (asmllm_b200/ and the
+ * C-ABI library build/libasmllm.so) never links, loads or calls it.
+ *
+ * What it restates (paths are inside the reference project THRISHAL12345/asmllm):
+ *   - fp32 -> Q8_0 activation quantize of the ARM64 NEON kernel
+ *       src/kernels/arm64/matmul_q4_neon.S:57-143
+ *   - Q4_0 x Q8_0 int8 block dot + fp32 combine of the same kernel
+ *       src/kernels/arm64/matmul_q4_neon.S:145-317
+ *   - Q8_0 x Q8_0: the same quantize and combine around a signed int8 block
+ *       dot (no reference kernel exists; composed as the north star specifies)
+ *   - Q4_0 x fp32 of the x86 AVX2 kernel, 8-lane FMA partials and its
+ *       horizontal-sum tree   src/kernels/x86_64/matmul_q4_avx2.asm:100-262
+ *   - the same with 16 lanes  src/kernels/x86_64/matmul_q4_avx512.asm:110-257
+ *   - Q8_0 x fp32, AVX2       src/kernels/x86_64/matmul_q8_avx2.asm:93-169
+ *   - Q8_0 x fp32, NEON scalar loop   src/kernels/arm64/matmul_q8_neon.S:30-72
+ *   - the threadpool's row tiling     src/runtime/threadpool.c:399-410
+ *
+ * Parity pinning: the fp32-x restatements are pinned to the reference's own
+ * golden generator (tools/reference_gen.py, seed 42) and to outputs of its
+ * numpy ops (tests/reference/ops.py) saved under tests/golden/.  The NEON
+ * Q8_0 activation bytes and per-block int32 sums are NOT pinned by any
+ * reference test or runnable reference build (no aarch64 toolchain exists
+ * here); they are pinned only by hand-derived known-answer vectors written
+ * from the ARMv8 instruction semantics (tests/test_oracle.py).
+ *
+ * Compile with -ffp-contract=off: every multiply/add below is rounded exactly
+ * where the reference instruction rounds; fused steps call fmaf explicitly.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#include <pthread.h>
+
+#define QK 32
+
+/* ------------------------------------------------------------------------ */
+/* Instruction-level helpers (ARMv8 semantics)                               */
+/* ------------------------------------------------------------------------ */
+
+/* FMAX / FMAXV: a NaN operand yields NaN (matmul_q4_neon.S:69-86). */
+static inline float arm_fmax(float a, float b) {
+    if (isnan(a)) return a;
+    if (isnan(b)) return b;
+    return a > b ? a : b;
+}
+
+/* FCVTNS: round to nearest, ties to even; NaN -> 0; saturates to int32. */
+static inline int32_t arm_fcvtns(float t) {
+    if (isnan(t)) return 0;
+    if (t >= 2147483648.0f) return INT32_MAX;
+    if (t <= -2147483648.0f) return INT32_MIN;
+    return (int32_t)nearbyintf(t); /* default rounding mode is ties-to-even */
+}
+
+/* SQXTN to int16 then SQXTN to int8 (matmul_q4_neon.S:122-135). */
+static inline int8_t arm_sqxtn_s8(int32_t v) {
+    if (v > 32767) v = 32767;
+    if (v < -32768) v = -32768;
+    if (v > 127) v = 127;
+    if (v < -128) v = -128;
+    return (int8_t)v;
+}
+
+/* ------------------------------------------------------------------------ */
+/* a1: fp32 -> Q8_0 activation quantize (matmul_q4_neon.S:57-143)           */
+/* ------------------------------------------------------------------------ */
+
+/* Quantizes K/32 blocks of x.  xq[K] int8, xd[K/32] fp32 (the kernel stores
+ * d as fp32, :92).  K % 32 elements at the end are ignored, as the kernel's
+ * `lsr x19, x5, #5` block count ignores them (:36). */
+void ref_quantize_q8_0(const float* x, int64_t K, int8_t* xq, float* xd) {
+    const int64_t nb = K / QK;
+    for (int64_t b = 0; b < nb; ++b) {
+        const float* xb = x + b * QK;
+        float amax = fabsf(xb[0]);
+        for (int i = 1; i < QK; ++i) amax = arm_fmax(amax, fabsf(xb[i]));
+        const float d = amax / 127.0f;                       /* fdiv :91 */
+        const float inv = (amax == 0.0f) ? 0.0f : 127.0f / amax; /* :95-101 */
+        xd[b] = d;
+        for (int i = 0; i < QK; ++i) {
+            const float t = xb[i] * inv;                     /* fmul :104 */
+            xq[b * QK + i] = arm_sqxtn_s8(arm_fcvtns(t));    /* fcvtns+sqxtn */
+        }
+    }
+}
+
+/* Sum of the 32 quantized values of each block (not stored by the
+ * reference; exposed so tests can check the GPU's bias identity). */
+void ref_q8_0_block_qsum(const int8_t* xq, int64_t K, int32_t* qsum) {
+    const int64_t nb = K / QK;
+    for (int64_t b = 0; b < nb; ++b) {
+        int32_t s = 0;
+        for (int i = 0; i < QK; ++i) s += xq[b * QK + i];
+        qsum[b] = s;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* a2: Q4_0 x Q8_0 int8 block dot (matmul_q4_neon.S:190-200)                 */
+/* ------------------------------------------------------------------------ */
+
+/* Block b of a row: byte j holds element j in its low nibble and element
+ * 16+j in its high nibble (tests/reference/ops.py:24-28); value = nibble-8. */
+static inline int32_t q4q8_block_dot(const uint8_t* qb, const int8_t* xqb) {
+    int32_t s = 0;
+    for (int j = 0; j < 16; ++j) {
+        const int32_t lo = (int32_t)(qb[j] & 0x0F) - 8;
+        const int32_t hi = (int32_t)(qb[j] >> 4) - 8;
+        s += lo * (int32_t)xqb[j] + hi * (int32_t)xqb[16 + j];
+    }
+    return s;
+}
+
+static inline int32_t q8q8_block_dot(const int8_t* wb, const int8_t* xqb) {
+    int32_t s = 0;
+    for (int j = 0; j < QK; ++j) s += (int32_t)wb[j] * (int32_t)xqb[j];
+    return s;
+}
+
+void ref_q4q8_block_sums(const uint8_t* qs, const int8_t* xq, int32_t* isums,
+                         int64_t M, int64_t K) {
+    const int64_t nb = K / QK;
+    for (int64_t r = 0; r < M; ++r)
+        for (int64_t b = 0; b < nb; ++b)
+            isums[r * nb + b] = q4q8_block_dot(qs + (r * nb + b) * 16, xq + b * QK);
+}
+
+void ref_q8q8_block_sums(const int8_t* qw, const int8_t* xq, int32_t* isums,
+                         int64_t M, int64_t K) {
+    const int64_t nb = K / QK;
+    for (int64_t r = 0; r < M; ++r)
+        for (int64_t b = 0; b < nb; ++b)
+            isums[r * nb + b] = q8q8_block_dot(qw + (r * nb + b) * QK, xq + b * QK);
+}
+
+/* Combine (matmul_q4_neon.S:239-255): s = wd*xd (fmul), acc = fma(float(isum), s, acc),
+ * sequentially over the blocks of a row, acc starting at +0. */
+static void q4q8_rows(const uint8_t* qs, const float* scales, const int8_t* xq,
+                      const float* xd, float* y, int64_t r0, int64_t r1, int64_t nb) {
+    for (int64_t r = r0; r < r1; ++r) {
+        float acc = 0.0f;
+        const uint8_t* qrow = qs + r * nb * 16;
+        const float* srow = scales + r * nb;
+        for (int64_t b = 0; b < nb; ++b) {
+            const float fi = (float)q4q8_block_dot(qrow + b * 16, xq + b * QK); /* scvtf */
+            const float s = srow[b] * xd[b];
+            acc = fmaf(fi, s, acc);
+        }
+        y[r] = acc;
+    }
+}
+
+static void q8q8_rows(const int8_t* qw, const float* scales, const int8_t* xq,
+                      const float* xd, float* y, int64_t r0, int64_t r1, int64_t nb) {
+    for (int64_t r = r0; r < r1; ++r) {
+        float acc = 0.0f;
+        const int8_t* wrow = qw + r * nb * QK;
+        const float* srow = scales + r * nb;
+        for (int64_t b = 0; b < nb; ++b) {
+            const float fi = (float)q8q8_block_dot(wrow + b * QK, xq + b * QK);
+            const float s = srow[b] * xd[b];
+            acc = fmaf(fi, s, acc);
+        }
+        y[r] = acc;
+    }
+}
+
+/* asm_matmul_q4, NEON semantics: quantize x, then block dots + combine. */
+void ref_matmul_q4q8(const uint8_t* qs, const float* scales, const float* x, float* y,
+                     int64_t M, int64_t K) {
+    const int64_t nb = K / QK;
+    int8_t* xq = (int8_t*)malloc((size_t)(nb * QK) + 1);
+    float* xd = (float*)malloc((size_t)nb * sizeof(float) + 4);
+    ref_quantize_q8_0(x, K, xq, xd);
+    q4q8_rows(qs, scales, xq, xd, y, 0, M, nb);
+    free(xq);
+    free(xd);
+}
+
+/* asm_matmul_q8q8: Q8_0 weights x Q8_0 activations, same quantize/combine. */
+void ref_matmul_q8q8(const int8_t* qw, const float* scales, const float* x, float* y,
+                     int64_t M, int64_t K) {
+    const int64_t nb = K / QK;
+    int8_t* xq = (int8_t*)malloc((size_t)(nb * QK) + 1);
+    float* xd = (float*)malloc((size_t)nb * sizeof(float) + 4);
+    ref_quantize_q8_0(x, K, xq, xd);
+    q8q8_rows(qw, scales, xq, xd, y, 0, M, nb);
+    free(xq);
+    free(xd);
+}
+
+/* ------------------------------------------------------------------------ */
+/* a3/a4/a5: fp32-activation kernels (x86 lane structure)                    */
+/* ------------------------------------------------------------------------ */
+
+/* 8 lanes: ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7))  (matmul_q4_avx2.asm:251-256,
+ * matmul_q8_avx2.asm:159-164 give the same tree). */
+static inline float hsum8(const float a[8]) {
+    const float t0 = a[0] + a[4], t1 = a[1] + a[5], t2 = a[2] + a[6], t3 = a[3] + a[7];
+    return (t0 + t2) + (t1 + t3);
+}
+
+/* 16 lanes: fold upper 8 onto lower 8, then the 8-lane tree
+ * (matmul_q4_avx512.asm:249-256). */
+static inline float hsum16(const float a[16]) {
+    float t[8];
+    for (int j = 0; j < 8; ++j) t[j] = a[8 + j] + a[j];
+    return hsum8(t);
+}
+
+/* Q4_0 x fp32, AVX2 (matmul_q4_avx2.asm:100-178): per block four 8-wide
+ * slices (low nibbles 0-7, 8-15, high nibbles 0-7, 8-15 -> elements 0-7,
+ * 8-15, 16-23, 24-31) are FMA'd into a fresh block accumulator, which is
+ * FMA'd with the broadcast block scale into the row accumulator. */
+static void q4f32_avx2_rows(const uint8_t* qs, const float* scales, const float* x,
+                            float* y, int64_t r0, int64_t r1, int64_t nb) {
+    for (int64_t r = r0; r < r1; ++r) {
+        float acc[8] = {0};
+        for (int64_t b = 0; b < nb; ++b) {
+            const uint8_t* qb = qs + (r * nb + b) * 16;
+            const float* xb = x + b * QK;
+            float w[QK];
+            for (int j = 0; j < 16; ++j) {
+                w[j] = (float)(qb[j] & 0x0F) - 8.0f;
+                w[16 + j] = (float)(qb[j] >> 4) - 8.0f;
+            }
+            float blk[8] = {0};
+            for (int s = 0; s < 4; ++s)
+                for (int j = 0; j < 8; ++j) blk[j] = fmaf(w[8 * s + j], xb[8 * s + j], blk[j]);
+            const float sc = scales[r * nb + b];
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(blk[j], sc, acc[j]);
+        }
+        y[r] = hsum8(acc);
+    }
+}
+
+/* Q4_0 x fp32, AVX-512 (matmul_q4_avx512.asm:110-175): two 16-wide slices. */
+static void q4f32_avx512_rows(const uint8_t* qs, const float* scales, const float* x,
+                              float* y, int64_t r0, int64_t r1, int64_t nb) {
+    for (int64_t r = r0; r < r1; ++r) {
+        float acc[16] = {0};
+        for (int64_t b = 0; b < nb; ++b) {
+            const uint8_t* qb = qs + (r * nb + b) * 16;
+            const float* xb = x + b * QK;
+            float blk[16];
+            for (int j = 0; j < 16; ++j) {
+                const float lo = (float)(qb[j] & 0x0F) - 8.0f;
+                const float hi = (float)(qb[j] >> 4) - 8.0f;
+                blk[j] = fmaf(lo, xb[j], 0.0f);
+                blk[j] = fmaf(hi, xb[16 + j], blk[j]);
+            }
+            const float sc = scales[r * nb + b];
+            for (int j = 0; j < 16; ++j) acc[j] = fmaf(blk[j], sc, acc[j]);
+        }
+        y[r] = hsum16(acc);
+    }
+}
+
+/* Q8_0 x fp32, AVX2 (matmul_q8_avx2.asm:103-164). */
+static void q8f32_avx2_rows(const int8_t* qw, const float* scales, const float* x,
+                            float* y, int64_t r0, int64_t r1, int64_t nb) {
+    for (int64_t r = r0; r < r1; ++r) {
+        float acc[8] = {0};
+        for (int64_t b = 0; b < nb; ++b) {
+            const int8_t* wb = qw + (r * nb + b) * QK;
+            const float* xb = x + b * QK;
+            float blk[8] = {0};
+            for (int s = 0; s < 4; ++s)
+                for (int j = 0; j < 8; ++j)
+                    blk[j] = fmaf((float)wb[8 * s + j], xb[8 * s + j], blk[j]);
+            const float sc = scales[r * nb + b];
+            for (int j = 0; j < 8; ++j) acc[j] = fmaf(blk[j], sc, acc[j]);
+        }
+        y[r] = hsum8(acc);
+    }
+}
+
+void ref_matmul_q4f32_avx2(const uint8_t* qs, const float* scales, const float* x, float* y,
+                           int64_t M, int64_t K) {
+    q4f32_avx2_rows(qs, scales, x, y, 0, M, K / QK);
+}
+
+void ref_matmul_q4f32_avx512(const uint8_t* qs, const float* scales, const float* x, float* y,
+                             int64_t M, int64_t K) {
+    q4f32_avx512_rows(qs, scales, x, y, 0, M, K / QK);
+}
+
+void ref_matmul_q8f32_avx2(const int8_t* qw, const float* scales, const float* x, float* y,
+                           int64_t M, int64_t K) {
+    q8f32_avx2_rows(qw, scales, x, y, 0, M, K / QK);
+}
+
+/* Q8_0 x fp32, NEON scalar loop (matmul_q8_neon.S:45-60): per element
+ * t = float(q)*scale (fmul), acc = fma(t, x, acc), sequential. */
+void ref_matmul_q8f32_neon(const int8_t* qw, const float* scales, const float* x, float* y,
+                           int64_t M, int64_t K) {
+    const int64_t nb = K / QK;
+    for (int64_t r = 0; r < M; ++r) {
+        float acc = 0.0f;
+        for (int64_t b = 0; b < nb; ++b) {
+            const float sc = scales[r * nb + b];
+            for (int j = 0; j < QK; ++j) {
+                const float t = (float)qw[(r * nb + b) * QK + j] * sc;
+                acc = fmaf(t, x[b * QK + j], acc);
+            }
+        }
+        y[r] = acc;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* a7: multi-thread row tiling (threadpool.c:399-410, :596-598)              */
+/* ------------------------------------------------------------------------ */
+
+/* Rows per worker: ceil(M/T) rounded up to a multiple of 16.  Returns 0 when
+ * the reference falls back to one thread (T <= 1 or M < 32). */
+int64_t ref_mt_tile_rows(int64_t M, int nthreads) {
+    if (nthreads <= 1 || M < 32) return 0;
+    int64_t t = (M + nthreads - 1) / nthreads;
+    return ((t + 15) / 16) * 16;
+}
+
+enum { K_Q4Q8 = 0, K_Q8Q8 = 1, K_Q4F32 = 2, K_Q8F32 = 3, K_Q4F32_512 = 4 };
+
+typedef struct {
+    int kind;
+    const void* w;
+    const float* scales;
+    const float* x;
+    float* y;
+    int64_t M, K, r0, r1;
+} mt_task;
+
+/* One worker runs the single-thread kernel on its row tile; the NEON
+ * kernel re-quantizes x inside every call, so each worker does too. */
+static void* mt_worker(void* arg) {
+    mt_task* t = (mt_task*)arg;
+    const int64_t nb = t->K / QK;
+    const int64_t rows = t->r1 - t->r0;
+    if (rows <= 0) return NULL;
+    switch (t->kind) {
+    case K_Q4Q8:
+        ref_matmul_q4q8((const uint8_t*)t->w + t->r0 * nb * 16, t->scales + t->r0 * nb,
+                        t->x, t->y + t->r0, rows, t->K);
+        break;
+    case K_Q8Q8:
+        ref_matmul_q8q8((const int8_t*)t->w + t->r0 * nb * QK, t->scales + t->r0 * nb,
+                        t->x, t->y + t->r0, rows, t->K);
+        break;
+    case K_Q4F32:
+        q4f32_avx2_rows((const uint8_t*)t->w, t->scales, t->x, t->y, t->r0, t->r1, nb);
+        break;
+    case K_Q4F32_512:
+        q4f32_avx512_rows((const uint8_t*)t->w, t->scales, t->x, t->y, t->r0, t->r1, nb);
+        break;
+    case K_Q8F32:
+        q8f32_avx2_rows((const int8_t*)t->w, t->scales, t->x, t->y, t->r0, t->r1, nb);
+        break;
+    }
+    return NULL;
+}
+
+/* Row-split dispatch with pthreads.  Unlike the reference pool the workers
+ * are created per call and joined (no spin waits); the tiling is the same.
+ * Returns 0 on success, -1 if a thread could not be created. */
+int ref_matmul_mt(int kind, const void* w, const float* scales, const float* x, float* y,
+                  int64_t M, int64_t K, int nthreads) {
+    int64_t tile = ref_mt_tile_rows(M, nthreads);
+    if (tile == 0) {
+        mt_task t = {kind, w, scales, x, y, M, K, 0, M};
+        mt_worker(&t);
+        return 0;
+    }
+    if (nthreads > 1024) nthreads = 1024;
+    pthread_t* th = (pthread_t*)calloc((size_t)nthreads, sizeof(pthread_t));
+    mt_task* tasks = (mt_task*)calloc((size_t)nthreads, sizeof(mt_task));
+    int rc = 0, started = 0;
+    for (int i = 0; i < nthreads; ++i) {
+        int64_t r0 = (int64_t)i * tile, r1 = r0 + tile;
+        if (r0 > M) r0 = M;
+        if (r1 > M) r1 = M;
+        mt_task t = {kind, w, scales, x, y, M, K, r0, r1};
+        tasks[i] = t;
+        if (pthread_create(&th[i], NULL, mt_worker, &tasks[i]) != 0) { rc = -1; break; }
+        ++started;
+    }
+    for (int i = 0; i < started; ++i) pthread_join(th[i], NULL);
+    free(th);
+    free(tasks);
+    return rc;
+}

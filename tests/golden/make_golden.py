@@ -1,0 +1,97 @@
+#!/usr/bin/env python3
+"""Regenerates the golden fixtures in this folder from the reference itself.
+
+Run in a container where the reference project (THRISHAL12345/asmllm) is
+checked out; pass its root as the first argument or via ASMLLM_REFERENCE_ROOT.
+It imports the reference's own Python (no copy of it lives in this repo):
+
+  * tools/reference_gen.py:31-112  generate_reference_data(seed=42) -- the
+    fixture tests/correctness/test_runner.py feeds every kernel;
+  * tests/reference/ops.py:33-64   ref_q4_matmul / ref_q8_matmul -- the numpy
+    fp32 expectations the reference harness compares against;
+  * the input recipes of bench/harness/bench_matmul_q4.py:76-80,
+    bench_mt_throughput.py:54-58 and bench_quant_formats.py:68-80 (numpy
+    RandomState(42)), whose numpy outputs are stored as expectations.  Inputs
+    of the large recipes are not stored: tests regenerate them from the same
+    legacy RandomState stream and check the stored SHA-256 of the bytes.
+
+Outputs: reference_seed42.npz (small fixture, all arrays) and
+bench_recipes.npz (expected y vectors + input digests).
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+
+
+def _sha(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def bench_matmul_q4_inputs(M=4096, K=4096):
+    """Input recipe of bench/harness/bench_matmul_q4.py:76-80."""
+    rng = np.random.RandomState(42)
+    nb = K // 32
+    q = rng.randint(0, 256, size=(M, nb, 16), dtype=np.uint8)
+    s = rng.uniform(0.5, 1.5, size=(M, nb)).astype(np.float32)
+    x = rng.randn(K).astype(np.float32)
+    return q, s, x
+
+
+def bench_mt_inputs(M=4096, K=4096):
+    """Input recipe of bench/harness/bench_mt_throughput.py:54-58."""
+    rng = np.random.RandomState(42)
+    nb = K // 32
+    q = rng.randint(0, 256, size=(M, nb, 16), dtype=np.uint8)
+    s = rng.uniform(0.05, 0.25, size=(M, nb)).astype(np.float32)
+    x = rng.randn(K).astype(np.float32)
+    return q, s, x
+
+
+def bench_quant_formats_inputs(M=1024, K=4096):
+    """Input recipe of bench/harness/bench_quant_formats.py:68-80 (Q4 and Q8 parts)."""
+    rng = np.random.RandomState(42)
+    nb = K // 32
+    x = rng.randn(K).astype(np.float32)
+    q4 = rng.randint(0, 256, size=(M, nb, 16), dtype=np.uint8)
+    s4 = rng.uniform(0.5, 1.5, size=(M, nb)).astype(np.float32)
+    q8 = rng.randint(-127, 128, size=(M, nb, 32), dtype=np.int8)
+    s8 = rng.uniform(0.1, 0.9, size=(M, nb)).astype(np.float32)
+    return x, q4, s4, q8, s8
+
+
+def main() -> None:
+    root = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ASMLLM_REFERENCE_ROOT", ""))
+    if not (root / "tools" / "reference_gen.py").exists():
+        raise SystemExit("usage: make_golden.py <reference project root>")
+    sys.path.insert(0, str(root))
+    from tools.reference_gen import generate_reference_data  # noqa: E402
+    from tests.reference.ops import ref_q4_matmul, ref_q8_matmul  # noqa: E402
+
+    data = generate_reference_data(seed=42)
+    keep = {k: v for k, v in data.items() if k.startswith(("q4_matmul", "q8_matmul", "q5_matmul"))}
+    np.savez_compressed(HERE / "reference_seed42.npz", **keep)
+
+    out = {}
+    q, s, x = bench_matmul_q4_inputs()
+    out["bench_q4_y"] = ref_q4_matmul(q, s, x).astype(np.float32)
+    out["bench_q4_sha"] = np.array([_sha(q), _sha(s), _sha(x)])
+    q, s, x = bench_mt_inputs()
+    out["bench_mt_y"] = ref_q4_matmul(q, s, x).astype(np.float32)
+    out["bench_mt_sha"] = np.array([_sha(q), _sha(s), _sha(x)])
+    x, q4, s4, q8, s8 = bench_quant_formats_inputs()
+    out["bench_qf_q4_y"] = ref_q4_matmul(q4, s4, x).astype(np.float32)
+    out["bench_qf_q8_y"] = ref_q8_matmul(q8, s8, x).astype(np.float32)
+    out["bench_qf_sha"] = np.array([_sha(x), _sha(q4), _sha(s4), _sha(q8), _sha(s8)])
+    np.savez_compressed(HERE / "bench_recipes.npz", **out)
+    print("wrote", HERE / "reference_seed42.npz", "and", HERE / "bench_recipes.npz")
+
+
+if __name__ == "__main__":
+    main()

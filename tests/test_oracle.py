@@ -1,0 +1,210 @@
+"""Pins the CPU oracle (oracle/asmllm_oracle.c) before it is trusted as the checker.
+
+1. Against the reference's own golden data: the seed-42 fixture of
+   tools/reference_gen.py and numpy outputs of tests/reference/ops.py on the
+   bench harness input recipes (tests/golden/make_golden.py made both).
+2. Against known-answer vectors derived by hand from the ARMv8 semantics of
+   the instructions src/kernels/arm64/matmul_q4_neon.S uses (FMAXV, FDIV,
+   FMUL, FCVTNS round-half-even, SQXTN saturation, SDOT) -- independent of the
+   oracle's code.
+3. The multi-thread row tiling of src/runtime/threadpool.c:399-410.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+import make_golden as G
+
+F = np.float32
+
+
+def f32(bits: int) -> np.float32:
+    return np.array([bits], dtype=np.uint32).view(np.float32)[0]
+
+
+def block(vals):
+    x = np.zeros(32, dtype=np.float32)
+    x[: len(vals)] = vals
+    return x
+
+
+# --------------------------------------------------------------------------
+# 1. golden data from the reference
+# --------------------------------------------------------------------------
+
+def test_seed42_q4_fp32x_matches_reference_numpy(oracle, golden):
+    q, s, x, e = (golden[k] for k in ("q4_matmul_qweights", "q4_matmul_scales", "q4_matmul_x", "q4_matmul_expected"))
+    np.testing.assert_allclose(oracle.matmul_q4f32_avx2(q, s, x), e, rtol=0, atol=1e-5)
+    np.testing.assert_allclose(oracle.matmul_q4f32_avx512(q, s, x), e, rtol=0, atol=1e-5)
+
+
+def test_seed42_q4q8_within_reference_harness_tolerance(oracle, golden):
+    # tests/correctness/test_runner.py:33 TOLERANCE_Q4 = 0.5 covers the Q8_0
+    # activation noise of the NEON kernel.
+    q, s, x, e = (golden[k] for k in ("q4_matmul_qweights", "q4_matmul_scales", "q4_matmul_x", "q4_matmul_expected"))
+    err = np.abs(oracle.matmul_q4q8(q, s, x) - e).max()
+    assert 0.3 < err <= 0.5
+
+
+def test_seed42_q8_fp32x_matches_reference_numpy(oracle, golden):
+    q, s, x, e = (golden[k] for k in ("q8_matmul_qweights", "q8_matmul_scales", "q8_matmul_x", "q8_matmul_expected"))
+    # tests/correctness/test_runner.py:34 TOLERANCE_Q8 = 1e-2
+    assert np.abs(oracle.matmul_q8f32_avx2(q, s, x) - e).max() <= 1e-4
+    assert np.abs(oracle.matmul_q8f32_neon(q, s, x) - e).max() <= 1e-4
+
+
+def test_seed42_q8q8_would_fail_reference_q8_tolerance(oracle, golden):
+    # Why asm_matmul_q8 keeps fp32-x semantics: Q8_0 activations miss 1e-2 by far.
+    q, s, x, e = (golden[k] for k in ("q8_matmul_qweights", "q8_matmul_scales", "q8_matmul_x", "q8_matmul_expected"))
+    assert np.abs(oracle.matmul_q8q8(q, s, x) - e).max() > 1.0
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_bench_matmul_q4_recipe(oracle, bench_recipes):
+    q, s, x = G.bench_matmul_q4_inputs()
+    assert [_sha(q), _sha(s), _sha(x)] == list(bench_recipes["bench_q4_sha"])
+    ref = bench_recipes["bench_q4_y"]
+    y = oracle.matmul_q4f32_avx2(q, s, x)
+    assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+    # NEON Q4 x Q8 semantics stays within the harness bench bound (err < 10.0,
+    # bench_matmul_q4.py:125) and ~0.5% of ||y||.
+    yq = oracle.matmul_q4q8(q, s, x)
+    assert np.abs(yq - ref).max() < 10.0
+
+
+def test_bench_mt_recipe(oracle, bench_recipes):
+    q, s, x = G.bench_mt_inputs()
+    assert [_sha(q), _sha(s), _sha(x)] == list(bench_recipes["bench_mt_sha"])
+    ref = bench_recipes["bench_mt_y"]
+    y = oracle.matmul_mt(oracle.K_Q4F32, q, s, x, 4096, 4096, 4)
+    assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_bench_quant_formats_recipe(oracle, bench_recipes):
+    x, q4, s4, q8, s8 = G.bench_quant_formats_inputs()
+    assert [_sha(a) for a in (x, q4, s4, q8, s8)] == list(bench_recipes["bench_qf_sha"])
+    r4, r8 = bench_recipes["bench_qf_q4_y"], bench_recipes["bench_qf_q8_y"]
+    assert np.abs(oracle.matmul_q4f32_avx512(q4, s4, x) - r4).max() <= 1e-5 * np.abs(r4).max()
+    assert np.abs(oracle.matmul_q8f32_avx2(q8, s8, x) - r8).max() <= 1e-5 * np.abs(r8).max()
+
+
+# --------------------------------------------------------------------------
+# 2. known-answer vectors from the instruction semantics
+# --------------------------------------------------------------------------
+
+def test_kat_round_half_even_and_scale(oracle):
+    # amax = 127 -> d = 127/127 = 1, inv = 127/127 = 1, q = FCVTNS(x) (ties to even).
+    x = block([127.0, -127.0, 62.5, 63.5, -2.5, 0.5, 1.5, 126.5, -0.5, 3.0])
+    xq, xd = oracle.quantize_q8_0(x)
+    assert xd[0] == F(1.0)
+    assert list(xq[:10]) == [127, -127, 62, 64, -2, 0, 2, 126, 0, 3]
+    assert not xq[10:].any()
+
+
+def test_kat_unit_amax(oracle):
+    # amax = 1 -> inv = 127 exactly; d = fl(1/127) = 0x3c010204.
+    x = block([1.0, -1.0, 0.5, -0.5, 0.25])
+    xq, xd = oracle.quantize_q8_0(x)
+    assert xd.view(np.uint32)[0] == 0x3C010204
+    assert list(xq[:5]) == [127, -127, 64, -64, 32]  # 63.5 -> 64, 31.75 -> 32
+
+
+def test_kat_multiply_not_divide(oracle):
+    # The kernel multiplies by inv = 127/amax (matmul_q4_neon.S:97,104), not
+    # x / (amax/127): here x*inv = 27.499998 -> 27 while x/d = 27.5 -> 28.
+    amax, v = f32(0x40350F9D), f32(0x3F1CD311)
+    xq, _ = oracle.quantize_q8_0(block([amax, v]))
+    assert xq[0] == 127 and xq[1] == 27
+    amax, v = f32(0x3FDE5292), f32(0x3FCBF109)  # 116.49999 -> 116 (divide form: 117)
+    xq, _ = oracle.quantize_q8_0(block([amax, v]))
+    assert xq[1] == 116
+
+
+def test_kat_zero_block(oracle):
+    xq, xd = oracle.quantize_q8_0(np.zeros(64, dtype=np.float32))
+    assert not xq.any() and (xd == 0).all() and not np.signbit(xd).any()
+
+
+def test_kat_nan_block(oracle):
+    # FMAX propagates NaN -> d = NaN, inv = 127/NaN = NaN, FCVTNS(NaN) = 0.
+    x = np.concatenate([block([1.0, np.nan, 5.0]), block([2.0, -4.0])])
+    xq, xd = oracle.quantize_q8_0(x)
+    assert np.isnan(xd[0]) and not xq[:32].any()
+    assert xd[1] == F(4.0) / F(127.0) and list(xq[32:34]) == [64, -127]  # 63.5 -> 64
+
+
+def test_kat_inf_block(oracle):
+    # amax = inf -> d = inf, inv = 127/inf = 0 -> finite*0 = 0, inf*0 = NaN -> 0.
+    xq, xd = oracle.quantize_q8_0(block([np.inf, 3.0, -7.0, -np.inf]))
+    assert np.isinf(xd[0]) and not xq.any()
+
+
+def test_kat_inverse_overflow_saturates(oracle):
+    # amax = 2^-127 (subnormal): 127/amax overflows to +inf, so x*inv is
+    # +inf (FCVTNS -> INT32_MAX -> SQXTN 127), -inf (-> -128) or NaN (0*inf -> 0).
+    a = F(2.0) ** -127
+    xq, xd = oracle.quantize_q8_0(block([a, -a, a / 2, 0.0]))
+    assert list(xq[:4]) == [127, -128, 127, 0]
+    assert xd.view(np.uint32)[0] == 0x8102  # 2^-127/127 rounded to a subnormal
+
+
+def test_kat_block_sums(oracle):
+    # Byte j: element j = low nibble - 8, element 16+j = high nibble - 8
+    # (tests/reference/ops.py:24-28; NEON and/ushr/sub at :192-195).
+    xq = np.arange(32, dtype=np.int8) - 16  # -16 .. 15
+    qs = np.zeros((3, 1, 16), dtype=np.uint8)
+    qs[0] = 0x00  # all elements -8
+    qs[1] = 0xFF  # all elements +7
+    qs[2] = 0x8F  # elements 0..15 -> +7, elements 16..31 -> 0
+    got = oracle.q4q8_block_sums(qs, xq, 3, 32)[:, 0]
+    s_all = int(xq.astype(np.int64).sum())
+    s_lo = int(xq[:16].astype(np.int64).sum())
+    assert list(got) == [-8 * s_all, 7 * s_all, 7 * s_lo]
+    w8 = np.tile(np.array([1, -2, 3, -128, 127, 0, 5, -1] * 4, dtype=np.int8), (1, 1))
+    got8 = oracle.q8q8_block_sums(w8.reshape(1, 1, 32), xq, 1, 32)[0, 0]
+    assert got8 == int((w8.astype(np.int64).ravel() * xq.astype(np.int64)).sum())
+
+
+def test_kat_combine_is_sequential_fma(oracle):
+    # y = fma(f(isum_b), wd_b*xd_b, acc) over b in order (matmul_q4_neon.S:239-255).
+    rng = np.random.default_rng(5)
+    K = 32 * 6
+    qs = rng.integers(0, 256, size=(1, 6, 16), dtype=np.uint8)
+    sc = rng.uniform(0.01, 0.05, size=(1, 6)).astype(np.float32)
+    x = rng.standard_normal(K).astype(np.float32)
+    xq, xd = oracle.quantize_q8_0(x)
+    isums = oracle.q4q8_block_sums(qs, xq, 1, K)[0]
+    acc = F(0.0)
+    import math
+    for b in range(6):
+        s = F(sc[0, b] * xd[b])
+        # exact fma in float64 then one rounding to fp32 is the IEEE fmaf result
+        acc = F(math.fsum([float(F(isums[b])) * float(s), float(acc)]))
+    assert oracle.matmul_q4q8(qs, sc, x)[0] == acc
+
+
+# --------------------------------------------------------------------------
+# 3. threadpool tiling
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M,T,tile", [(4096, 4, 1024), (4096, 3, 1376), (100, 3, 48), (31, 8, 0), (64, 1, 0), (4096, 8, 512)])
+def test_mt_tile_rows(oracle, M, T, tile):
+    assert oracle.mt_tile_rows(M, T) == tile
+
+
+def test_mt_equals_single_thread(oracle):
+    rng = np.random.default_rng(1)
+    M, K = 257, 128
+    q4 = rng.integers(0, 256, size=(M, K // 32, 16), dtype=np.uint8)
+    q8 = rng.integers(-127, 128, size=(M, K // 32, 32), dtype=np.int8)
+    s = rng.uniform(0.01, 0.1, size=(M, K // 32)).astype(np.float32)
+    x = rng.standard_normal(K).astype(np.float32)
+    for kind, w, single in ((oracle.K_Q4Q8, q4, oracle.matmul_q4q8), (oracle.K_Q8Q8, q8, oracle.matmul_q8q8),
+                            (oracle.K_Q4F32, q4, oracle.matmul_q4f32_avx2), (oracle.K_Q8F32, q8, oracle.matmul_q8f32_avx2)):
+        assert np.array_equal(oracle.matmul_mt(kind, w, s, x, M, K, 5), single(w, s, x))

@@ -1,0 +1,284 @@
+"""GPU parity: the sm_100a kernels against the CPU oracle, through the C ABI.
+
+Bars (from the task's north star):
+  * Q8_0 activation bytes and scales: bit-exact.
+  * per-(row, block) int32 dot sums: bit-exact.
+  * y: max |y - y_oracle| <= 1e-4 * ||y_oracle||_inf  (YTOL in conftest).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import refharness
+from asmllm_b200 import native, ops, synth
+from asmllm_b200.native import FMT_Q4_0, FMT_Q8_0
+from conftest import YTOL, rel_err
+
+pytestmark = pytest.mark.gpu
+
+SHAPES_SMALL = [(1, 32), (5, 64), (7, 96), (33, 4096), (129, 4096), (257, 1024), (1000, 11008)]
+SHAPES_7B = list(synth.SHAPES_7B.values())
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def special_x(K):
+    """Activation with every edge case of the quantize in some block."""
+    x = synth.activation(K, seed=3).copy()
+    nb = K // 32
+    if nb >= 8:
+        x[0:32] = 0.0                                     # zero block
+        x[32:64] *= 1e-30                                 # tiny but normal
+        x[64] = np.nan                                    # NaN block
+        x[96] = np.inf                                    # inf block
+        x[128:160] = np.float32(2.0) ** -127              # 127/amax overflows
+        x[129] = -x[129]
+        x[160:192] = np.linspace(-127, 127, 32).astype(np.float32)
+        x[192:224] = np.array([62.5, 63.5, -2.5, 0.5, 1.5, 126.5, -0.5, 127.0] * 4, dtype=np.float32)
+    return x
+
+
+def assert_quant_equal(xq, xd, rq, rd):
+    assert np.array_equal(xq, rq), f"{np.count_nonzero(xq != rq)} int8 values differ"
+    nan_a, nan_b = np.isnan(xd), np.isnan(rd)
+    assert np.array_equal(nan_a, nan_b)
+    assert np.array_equal(xd[~nan_a].view(np.uint32), rd[~nan_b].view(np.uint32))
+
+
+# --------------------------------------------------------------------------
+# Drop-in contract: the reference harness's own checks on its fixture
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("kernel,tol", refharness.KERNELS)
+def test_reference_harness(cuda, golden, kernel, tol):
+    status, err = refharness.run_kernel_test(kernel, tol, golden, native.lib())
+    assert status == "PASS", (kernel, err)
+
+
+def test_reference_harness_fixture_matches_oracle(cuda, golden, oracle):
+    # The drop-in asm_matmul_q4 is the NEON Q4_0 x Q8_0 semantics, not numpy's fp32-x.
+    q, s, x = golden["q4_matmul_qweights"], golden["q4_matmul_scales"], golden["q4_matmul_x"]
+    assert rel_err(ops.matmul_q4(q, s, x), oracle.matmul_q4q8(q, s, x)) <= YTOL
+    assert rel_err(ops.matmul_q4_avx512(q, s, x), oracle.matmul_q4f32_avx512(q, s, x)) <= YTOL
+    q8, s8 = golden["q8_matmul_qweights"], golden["q8_matmul_scales"]
+    assert rel_err(ops.matmul_q8(q8, s8, x), oracle.matmul_q8f32_avx2(q8, s8, x)) <= YTOL
+    assert rel_err(ops.matmul_q8q8(q8, s8, x), oracle.matmul_q8q8(q8, s8, x)) <= YTOL
+
+
+# --------------------------------------------------------------------------
+# Activation quantize: bit-exact
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("K", [32, 64, 256, 4096, 11008, 28672])
+def test_quantize_bit_exact_device(cuda, oracle, K):
+    x = special_x(K)
+    rq, rd = oracle.quantize_q8_0(x)
+    xq, xd = ops.quantize_q8_0_dev(dev(cuda, x))
+    assert_quant_equal(xq.cpu().numpy(), xd.cpu().numpy(), rq, rd)
+
+
+def test_quantize_bit_exact_host_abi(cuda, oracle):
+    x = special_x(4096)
+    rq, rd = oracle.quantize_q8_0(x)
+    xq, xd = ops.quantize_q8_0(x)
+    assert_quant_equal(xq, xd, rq, rd)
+
+
+def test_quantize_batched_rows(cuda, oracle):
+    X = synth.activation(4096, seed=7, n=8)
+    X[3, :32] = 0.0
+    xq, xd = ops.quantize_q8_0_dev(dev(cuda, X))
+    for n in range(8):
+        rq, rd = oracle.quantize_q8_0(X[n])
+        assert_quant_equal(xq[n].cpu().numpy(), xd[n].cpu().numpy(), rq, rd)
+
+
+def test_quantize_random_bulk(cuda, oracle):
+    # 2^22 values from several scales: the quantize is exact on all of them.
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal(1 << 22) * np.exp(rng.uniform(-30, 30, 1 << 22))).astype(np.float32)
+    rq, rd = oracle.quantize_q8_0(x)
+    xq, xd = ops.quantize_q8_0_dev(dev(cuda, x))
+    assert_quant_equal(xq.cpu().numpy(), xd.cpu().numpy(), rq, rd)
+
+
+# --------------------------------------------------------------------------
+# Block sums: bit-exact (the matvec kernel's own debug instantiation)
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("M,K", SHAPES_SMALL + [(4096, 4096)])
+@pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
+def test_block_sums_bit_exact(cuda, oracle, fmt, M, K):
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=M + K)
+    x = special_x(K) if K >= 256 else synth.activation(K, seed=2)
+    xq, _ = oracle.quantize_q8_0(x)
+    ref = (oracle.q4q8_block_sums if fmt == FMT_Q4_0 else oracle.q8q8_block_sums)(w, xq, M, K)
+    _, isums = ops.block_sums_dev(fmt, dev(cuda, w), dev(cuda, s), dev(cuda, x))
+    assert np.array_equal(isums.cpu().numpy(), ref)
+
+
+# --------------------------------------------------------------------------
+# Matvec outputs within 1e-4 * ||y||_inf
+# --------------------------------------------------------------------------
+
+def _oracle_y(oracle, fmt, fp32_act, w, s, x):
+    if fmt == FMT_Q4_0:
+        return (oracle.matmul_q4f32_avx2 if fp32_act else oracle.matmul_q4q8)(w, s, x)
+    return (oracle.matmul_q8f32_avx2 if fp32_act else oracle.matmul_q8q8)(w, s, x)
+
+
+@pytest.mark.parametrize("M,K", SHAPES_SMALL + SHAPES_7B)
+@pytest.mark.parametrize("fmt,fp32_act", [(FMT_Q4_0, False), (FMT_Q8_0, False), (FMT_Q4_0, True), (FMT_Q8_0, True)])
+def test_matvec_parity(cuda, oracle, fmt, fp32_act, M, K):
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=M * 7 + K)
+    x = synth.activation(K, seed=K)
+    ref = _oracle_y(oracle, fmt, fp32_act, w, s, x)
+    dw, ds, dx = dev(cuda, w), dev(cuda, s), dev(cuda, x)
+    y = ops.matvec(fmt, dw, ds, dx, fp32_activations=fp32_act).cpu().numpy()
+    assert rel_err(y, ref) <= YTOL
+    if not fp32_act:  # fp16 scale plane: same values, same result
+        y16 = ops.matvec(fmt, dw, ds.half(), dx).cpu().numpy()
+        assert np.array_equal(y16, y)
+
+
+@pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
+def test_matvec_edge_activations(cuda, oracle, fmt):
+    M, K = 300, 4096
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=9)
+    x = special_x(K)
+    x[64] = 0.0  # drop the NaN block so y stays finite
+    x[96] = 1.0  # and the inf block
+    ref = _oracle_y(oracle, fmt, False, w, s, x)
+    y = ops.matvec(fmt, dev(cuda, w), dev(cuda, s), dev(cuda, x)).cpu().numpy()
+    assert rel_err(y, ref) <= YTOL
+
+
+def test_nan_activation_propagates(cuda, oracle):
+    M, K = 64, 128
+    w, s = synth.q4_0_weights(M, K, seed=4)
+    x = synth.activation(K)
+    x[5] = np.nan
+    ref = oracle.matmul_q4q8(w, s, x)
+    y = ops.matvec(FMT_Q4_0, dev(cuda, w), dev(cuda, s), dev(cuda, x)).cpu().numpy()
+    assert np.isnan(ref).all() and np.isnan(y).all()
+
+
+def test_zero_k_gives_zero(cuda):
+    y = ops.matmul_q4(np.zeros((3, 0, 16), np.uint8), np.zeros((3, 0), np.float32), np.zeros(0, np.float32))
+    assert y.shape == (3,) and not y.any()
+
+
+# --------------------------------------------------------------------------
+# The synchronous ABI: host, device and registered pointers agree
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("fmt,name", [(FMT_Q4_0, "asm_matmul_q4"), (FMT_Q8_0, "asm_matmul_q8q8"),
+                                      (FMT_Q4_0, "asm_matmul_q4_avx512"), (FMT_Q8_0, "asm_matmul_q8")])
+def test_sync_abi_pointer_kinds(cuda, oracle, fmt, name):
+    M, K = 4096, 4096
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=21)
+    x = synth.activation(K, seed=22)
+    L = native.lib()
+    f = getattr(L, name)
+
+    def call(pw, ps, px, py):
+        f(pw, ps, px, py, M, K)
+        native.check()
+
+    y_host = np.zeros(M, np.float32)
+    call(w.ctypes.data, s.ctypes.data, x.ctypes.data, y_host.ctypes.data)
+    dw, ds, dx = dev(cuda, w), dev(cuda, s), dev(cuda, x)
+    dy = cuda.zeros(M, dtype=cuda.float32, device="cuda")
+    call(dw.data_ptr(), ds.data_ptr(), dx.data_ptr(), dy.data_ptr())
+    assert np.array_equal(dy.cpu().numpy(), y_host)
+    # pinned host x / y (the end-to-end path of the benchmark)
+    px = cuda.from_numpy(x).pin_memory()
+    py = cuda.zeros(M, dtype=cuda.float32).pin_memory()
+    call(w.ctypes.data, s.ctypes.data, px.data_ptr(), py.data_ptr())
+    assert np.array_equal(py.numpy(), y_host)
+    # registered (resident) weights, fp16 scale plane
+    ops.register_weights(w, s, fmt)
+    try:
+        y_reg = np.zeros(M, np.float32)
+        call(w.ctypes.data, s.ctypes.data, x.ctypes.data, y_reg.ctypes.data)
+        cnt = ctypes.c_int(0)
+        assert L.asm_weights_resident_bytes(ctypes.byref(cnt)) > 0 and cnt.value == 1
+        assert np.array_equal(y_reg, y_host)
+    finally:
+        ops.unregister_weights(w)
+    fp32_act = name in ("asm_matmul_q4_avx512", "asm_matmul_q8")
+    assert rel_err(y_host, _oracle_y(oracle, fmt, fp32_act, w, s, x)) <= YTOL
+
+
+def test_mt_entries_and_threadpool(cuda, golden):
+    ops.threadpool_init(8)
+    assert ops.threadpool_get_num_threads() == 8
+    q, s, x = golden["q4_matmul_qweights"], golden["q4_matmul_scales"], golden["q4_matmul_x"]
+    assert np.array_equal(ops.matmul_q4_mt(q, s, x, 8), ops.matmul_q4(q, s, x))
+    q8, s8 = golden["q8_matmul_qweights"], golden["q8_matmul_scales"]
+    y8 = ops.matmul_q8(q8, s8, x)
+    assert np.array_equal(ops.matmul_q8_mt(q8, s8, x, 3), y8)
+    yd = np.zeros(4, np.float32)
+    native.lib().asm_threadpool_dispatch_q8(q8.ctypes.data, s8.ctypes.data, x.ctypes.data, yd.ctypes.data, 4, 64)
+    native.check()
+    assert np.array_equal(yd, y8)
+    ops.threadpool_shutdown()
+    assert ops.threadpool_get_num_threads() == 0
+    # usable again after shutdown
+    assert np.array_equal(ops.matmul_q4(q, s, x), ops.matmul_q4_mt(q, s, x, 2))
+
+
+def test_deterministic(cuda):
+    M, K = 11008, 4096
+    w, s = synth.q4_0_weights(M, K)
+    x = synth.activation(K)
+    dw, ds, dx = dev(cuda, w), dev(cuda, s), dev(cuda, x)
+    a = ops.matvec(FMT_Q4_0, dw, ds, dx)
+    b = ops.matvec(FMT_Q4_0, dw, ds, dx)
+    assert cuda.equal(a, b)
+
+
+# --------------------------------------------------------------------------
+# Errors are reported, never launched
+# --------------------------------------------------------------------------
+
+def test_async_rejects_host_pointers(cuda):
+    w, s = synth.q4_0_weights(8, 64)
+    x = synth.activation(64)
+    y = np.zeros(8, np.float32)
+    rc = native.lib().asm_matmul_q4_async(w.ctypes.data, s.ctypes.data, x.ctypes.data, y.ctypes.data, 8, 64, None)
+    assert rc == native.ASM_E_NOT_DEVICE
+    native.last_error()
+
+
+def test_k_beyond_maximum_is_rejected(cuda):
+    kmax = ops.max_k(FMT_Q4_0, False)
+    assert kmax >= 131072 - 32
+    K = kmax + 32
+    dw = cuda.zeros((1, K // 32, 16), dtype=cuda.uint8, device="cuda")
+    ds = cuda.zeros((1, K // 32), dtype=cuda.float32, device="cuda")
+    dx = cuda.zeros(K, dtype=cuda.float32, device="cuda")
+    with pytest.raises(native.AsmError) as e:
+        ops.matvec(FMT_Q4_0, dw, ds, dx)
+    assert e.value.code == native.ASM_E_UNSUPPORTED
+
+
+# --------------------------------------------------------------------------
+# GGUF block split (reference generate.py:91-119)
+# --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
+@pytest.mark.parametrize("f16", [True, False])
+def test_gguf_split(cuda, fmt, f16):
+    M, K = 77, 4096
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=5)
+    raw = synth.gguf_blocks(w, s)
+    nblk = M * (K // 32)
+    qs, sc = ops.gguf_split_dev(fmt, dev(cuda, raw), nblk, scales_f16=f16)
+    assert np.array_equal(qs.cpu().numpy().reshape(w.shape), w)
+    assert np.array_equal(sc.float().cpu().numpy().reshape(s.shape), s)

@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -106,6 +107,8 @@ struct DeviceState {
   cudaStream_t stream = nullptr;
   Buf dev[4];   // device staging: weights, scales, x, y
   Buf host[2];  // pinned host staging: x, y
+  Buf image;    // Q8_0 activation image of the synchronous calls
+  unsigned* err_word = nullptr;  // pinned copy of the device error word
   std::mutex mu;
 };
 
@@ -124,6 +127,9 @@ int get_state(DeviceState** out, int* dev_out) {
   if (!st.init) {
     e = cudaStreamCreateWithFlags(&st.stream, cudaStreamDefault);
     if (e != cudaSuccess) return cuda_error(e, "cudaStreamCreate");
+    e = cudaHostAlloc(&st.err_word, sizeof(unsigned), cudaHostAllocDefault);
+    if (e != cudaSuccess) return cuda_error(e, "cudaHostAlloc (error word)");
+    *st.err_word = 0;
     st.init = true;
   }
   *out = &st;
@@ -153,6 +159,23 @@ int ensure_host(Buf& b, size_t bytes) {
   if (e != cudaSuccess) return cuda_error(e, "cudaHostAlloc (staging)");
   b.cap = cap;
   return ASM_OK;
+}
+
+// --------------------------------------------------------------------------
+// Device ranges declared static by the caller (asm_weights_mark_static): the
+// kernel that precedes a matvec never writes them, so the matvec may stream
+// them before waiting for that kernel (programmatic dependent launch).
+// --------------------------------------------------------------------------
+std::mutex g_static_mu;
+std::map<uintptr_t, uintptr_t> g_static;  // begin -> end
+
+bool is_static(const void* p, size_t bytes) {
+  const uintptr_t b = (uintptr_t)p, e = b + bytes;
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  auto it = g_static.upper_bound(b);
+  if (it == g_static.begin()) return false;
+  --it;
+  return b >= it->first && e <= it->second;
 }
 
 // --------------------------------------------------------------------------
@@ -199,6 +222,18 @@ int validate(const char* name, const void* w, const void* s, const void* x, cons
   return ASM_OK;
 }
 
+// The kernels read weights and x with 16-byte vector loads and scales with
+// naturally aligned loads; device buffers must be aligned accordingly.
+int check_align(const char* name, const void* w, const void* s, size_t s_align, const void* x) {
+  if ((uintptr_t)w % 16 != 0)
+    return set_error(ASM_E_INVALID, "%s: qweights device pointer is not 16-byte aligned", name);
+  if ((uintptr_t)s % s_align != 0)
+    return set_error(ASM_E_INVALID, "%s: scales device pointer is not %zu-byte aligned", name, s_align);
+  if ((uintptr_t)x % 16 != 0)
+    return set_error(ASM_E_INVALID, "%s: x device pointer is not 16-byte aligned", name);
+  return ASM_OK;
+}
+
 int check_max_k(const char* name, int fmt, bool fp32_act, int64_t K, int dev) {
   const int64_t mk = max_k(fmt, fp32_act, dev);
   if (K > mk)
@@ -235,6 +270,16 @@ int device_in(DeviceState& st, int dev, const void* p, size_t bytes, int slot, c
   return ASM_OK;
 }
 
+// Synchronous Q8_0-activation calls quantize x with a separate pre-pass into a
+// per-device image (default) or inside the matvec (ASMLLM_SYNC_FUSED=1).
+bool sync_fused() {
+  static const bool v = [] {
+    const char* e = getenv("ASMLLM_SYNC_FUSED");
+    return e && e[0] == '1';
+  }();
+  return v;
+}
+
 void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const float* s,
                  const float* x, float* y, int64_t M, int64_t K) {
   if (validate(name, w, s, x, y, M, K)) return;
@@ -269,10 +314,16 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
     if (device_in(st, dev, w, weight_bytes(fmt, M, K), 0, &a.w, name)) return;
     if (device_in(st, dev, s, (size_t)M * (K / 32) * sizeof(float), 1, &a.scales, name)) return;
   }
+  // Library-owned copies (registered or staged) are never written by a kernel;
+  // caller device buffers only when declared static.
+  a.weights_static = K > 0 && ((a.w != (const void*)w) ||
+                               (is_static(w, weight_bytes(fmt, M, K)) &&
+                                is_static(s, (size_t)M * (K / 32) * sizeof(float))));
   if (K > 0) {
     const void* dx = nullptr;
     if (device_in(st, dev, x, (size_t)K * sizeof(float), 2, &dx, name)) return;
     a.x = static_cast<const float*>(dx);
+    if (check_align(name, a.w, a.scales, a.scales_f16 ? 2 : 4, a.x)) return;
   }
 
   int ydev = -1;
@@ -289,7 +340,15 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
     a.y = static_cast<float*>(st.dev[3].p);
   }
 
-  cudaError_t e = launch_matvec(a, st.stream);
+  cudaError_t e = cudaSuccess;
+  if (!fp32_act && K > 0 && !sync_fused()) {
+    // Quantize x once into the device's activation image, then the matvec reads it.
+    if (ensure_dev(st.image, act_image_bytes(K / 32))) return;
+    e = launch_act_image(a.x, st.image.p, 1, K, st.stream, a.w, weight_bytes(fmt, M, K), a.scales,
+                         (size_t)M * (K / 32) * (a.scales_f16 ? 2 : 4));
+    a.image = st.image.p;
+  }
+  if (e == cudaSuccess) e = launch_matvec(a, st.stream);
   if (e != cudaSuccess) {
     cuda_error(e, name);
     return;
@@ -306,9 +365,17 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
     cuda_error(e, "cudaMemcpyAsync D2H");
     return;
   }
-  e = cudaStreamSynchronize(st.stream);
+  e = read_device_error_async(st.err_word, st.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st.stream);
   if (e != cudaSuccess) {
     cuda_error(e, name);
+    return;
+  }
+  if (*st.err_word) {
+    unsigned v = 0;
+    read_device_error(&v, true);
+    *st.err_word = 0;
+    set_error(ASM_E_CUDA, "%s: a device-side bounded wait timed out (error bits 0x%x); y is not valid", name, v);
     return;
   }
   if (ybounce) memcpy(y, ybounce, ybytes);
@@ -344,6 +411,8 @@ int async_matvec(const char* name, int fmt, bool fp32_act, bool f16s, const void
     if ((rc = require_device(name, x, "x"))) return rc;
   }
   if (isums && (rc = require_device(name, isums, "isums"))) return rc;
+  if (K > 0 && (rc = check_align(name, w, s, f16s ? 2 : 4, x))) return rc;
+  if (isums && (uintptr_t)isums % 4 != 0) return set_error(ASM_E_INVALID, "%s: isums is not 4-byte aligned", name);
   MatvecArgs a;
   a.fmt = fmt;
   a.fp32_act = fp32_act;
@@ -355,6 +424,8 @@ int async_matvec(const char* name, int fmt, bool fp32_act, bool f16s, const void
   a.isums = isums;
   a.M = M;
   a.K = K;
+  a.weights_static = K > 0 && is_static(w, weight_bytes(fmt, M, K)) &&
+                     is_static(s, (size_t)M * (K / 32) * (f16s ? 2 : 4));
   e = launch_matvec(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
@@ -444,8 +515,12 @@ ASMLLM_API void asm_threadpool_shutdown(void) {
       if (b.p) cudaFreeHost(b.p);
       b = Buf();
     }
+    if (st.image.p) cudaFree(st.image.p);
+    st.image = Buf();
     cudaStreamDestroy(st.stream);
     st.stream = nullptr;
+    if (st.err_word) cudaFreeHost(st.err_word);
+    st.err_word = nullptr;
     st.init = false;
   }
   cudaSetDevice(cur);
@@ -654,6 +729,83 @@ ASMLLM_API int asm_quantize_q8_0_async(const float* x, int8_t* xq, float* xd, in
   return ASM_OK;
 }
 
+ASMLLM_API int64_t asm_act_image_bytes(int64_t K) {
+  if (K < 0 || K % 32 != 0) return -1;
+  return (int64_t)act_image_bytes(K / 32);
+}
+
+ASMLLM_API int asm_act_image_q8_0_async(const float* x, void* image, int64_t N, int64_t K,
+                                        void* stream) {
+  const char* name = "asm_act_image_q8_0_async";
+  if (N < 0 || K < 0 || K % 32 != 0)
+    return set_error(ASM_E_INVALID, "%s: N=%lld K=%lld (K must be a multiple of 32)", name,
+                     (long long)N, (long long)K);
+  if (N == 0 || K == 0) return ASM_OK;
+  int rc;
+  if ((rc = require_device(name, x, "x")) || (rc = require_device(name, image, "image"))) return rc;
+  if ((uintptr_t)x % 16 != 0 || (uintptr_t)image % 16 != 0)
+    return set_error(ASM_E_INVALID, "%s: x and image must be 16-byte aligned", name);
+  cudaError_t e = launch_act_image(x, image, N, K, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_act_image_q8_0_prefetch_async(const float* x, void* image, int64_t N, int64_t K,
+                                                 const void* next_w, int64_t next_w_bytes,
+                                                 const void* next_s, int64_t next_s_bytes,
+                                                 void* stream) {
+  const char* name = "asm_act_image_q8_0_prefetch_async";
+  if (N < 0 || K < 0 || K % 32 != 0 || next_w_bytes < 0 || next_s_bytes < 0)
+    return set_error(ASM_E_INVALID, "%s: bad sizes N=%lld K=%lld", name, (long long)N, (long long)K);
+  if (N == 0 || K == 0) return ASM_OK;
+  int rc;
+  if ((rc = require_device(name, x, "x")) || (rc = require_device(name, image, "image"))) return rc;
+  if (next_w && next_w_bytes && (rc = require_device(name, next_w, "next_w"))) return rc;
+  if (next_s && next_s_bytes && (rc = require_device(name, next_s, "next_s"))) return rc;
+  if ((uintptr_t)x % 16 != 0 || (uintptr_t)image % 16 != 0)
+    return set_error(ASM_E_INVALID, "%s: x and image must be 16-byte aligned", name);
+  cudaError_t e = launch_act_image(x, image, N, K, static_cast<cudaStream_t>(stream), next_w,
+                                   (size_t)next_w_bytes, next_s, (size_t)next_s_bytes);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_matmul_image_async(int fmt, const void* qweights, const void* scales,
+                                      int scales_are_f16, const void* image, float* y, int64_t M,
+                                      int64_t K, void* stream) {
+  const char* name = "asm_matmul_image_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0)
+    return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  int rc = validate(name, qweights, scales, image, y, M, K);
+  if (rc) return rc;
+  if (M == 0) return ASM_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if ((rc = check_max_k(name, fmt, false, K, dev))) return rc;
+  if ((rc = require_device(name, y, "y"))) return rc;
+  if (K > 0) {
+    if ((rc = require_device(name, qweights, "qweights")) || (rc = require_device(name, scales, "scales")) ||
+        (rc = require_device(name, image, "image")))
+      return rc;
+    if ((rc = check_align(name, qweights, scales, scales_are_f16 ? 2 : 4, image))) return rc;
+  }
+  MatvecArgs a;
+  a.fmt = fmt;
+  a.scales_f16 = scales_are_f16 != 0;
+  a.w = qweights;
+  a.scales = scales;
+  a.image = image;
+  a.y = y;
+  a.M = M;
+  a.K = K;
+  a.weights_static = K > 0 && is_static(qweights, weight_bytes(fmt, M, K)) &&
+                     is_static(scales, (size_t)M * (K / 32) * (scales_are_f16 ? 2 : 4));
+  e = launch_matvec(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
 ASMLLM_API int asm_gguf_split_async(int fmt, const uint8_t* raw, uint8_t* qs, void* scales,
                                     int scales_are_f16, int64_t nblocks, void* stream) {
   const char* name = "asm_gguf_split_async";
@@ -671,6 +823,37 @@ ASMLLM_API int asm_gguf_split_async(int fmt, const uint8_t* raw, uint8_t* qs, vo
                                     static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
+}
+
+ASMLLM_API int asm_weights_mark_static(const void* ptr, int64_t bytes) {
+  if (!ptr || bytes <= 0) return set_error(ASM_E_INVALID, "asm_weights_mark_static: empty range");
+  if (classify(ptr, nullptr) != kDevice)
+    return set_error(ASM_E_NOT_DEVICE, "asm_weights_mark_static: not a device pointer");
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  g_static[(uintptr_t)ptr] = (uintptr_t)ptr + (uintptr_t)bytes;
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_weights_unmark_static(const void* ptr) {
+  std::lock_guard<std::mutex> lk(g_static_mu);
+  g_static.erase((uintptr_t)ptr);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_device_error(unsigned* flags) {
+  unsigned v = 0;
+  cudaError_t e = read_device_error(&v, true);
+  if (e != cudaSuccess) return cuda_error(e, "asm_device_error");
+  if (flags) *flags = v;
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_set_option(const char* name, int value) {
+  if (!name) return -1;
+  if (strcmp(name, "tma") == 0) return g_opt_tma.exchange(value ? 1 : 0);
+  if (strcmp(name, "pdl") == 0) return g_opt_pdl.exchange(value ? 1 : 0);
+  set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
+  return -1;
 }
 
 ASMLLM_API int64_t asm_max_k(int fmt, int fp32_activations) {

@@ -43,6 +43,89 @@ __device__ __forceinline__ int quantize_block_lane(float v, float& d, int& qsum)
   return q;
 }
 
+// Quantizes one 32-element block held by a single thread (xb: 16-byte aligned
+// global pointer).  Same formulas as quantize_block_lane; writes the 32 int8
+// values packed little-endian into q[8], returns d and the block's q-sum.
+__device__ __forceinline__ void quantize_block_thread(const float* __restrict__ xb, unsigned q[8],
+                                                      float& d, int& qsum) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 t = reinterpret_cast<const float4*>(xb)[i];
+    v[4 * i] = t.x;
+    v[4 * i + 1] = t.y;
+    v[4 * i + 2] = t.z;
+    v[4 * i + 3] = t.w;
+  }
+  float a = fabsf(v[0]);
+#pragma unroll
+  for (int i = 1; i < 32; ++i) a = arm_fmax(a, fabsf(v[i]));
+  d = __fdiv_rn(a, 127.0f);
+  const float inv = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
+  int s = 0;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    int b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float t = __fmul_rn(v[4 * w + j], inv);
+      b[j] = (t != t) ? 0 : __float2int_rn(fminf(fmaxf(t, -128.0f), 127.0f));
+      s += b[j];
+    }
+    q[w] = __byte_perm(__byte_perm((unsigned)b[0], (unsigned)b[1], 0x0040u),
+                       __byte_perm((unsigned)b[2], (unsigned)b[3], 0x0040u), 0x5410u);
+  }
+  qsum = s;
+}
+
+// Quantizes one 32-element block spread over 8 consecutive lanes (lane group
+// of 8 aligned in the warp; this lane holds elements 4j..4j+3, j = lane & 7).
+// All 32 lanes of the warp must call it.  Same formulas as above; returns the
+// 4 int8 values packed little-endian, and d and the block q-sum to all 8 lanes.
+__device__ __forceinline__ unsigned quantize_quad(float4 v, float& d, int& qsum) {
+  float a = arm_fmax(arm_fmax(fabsf(v.x), fabsf(v.y)), arm_fmax(fabsf(v.z), fabsf(v.w)));
+  a = arm_fmax(a, __shfl_xor_sync(kFull, a, 1));
+  a = arm_fmax(a, __shfl_xor_sync(kFull, a, 2));
+  a = arm_fmax(a, __shfl_xor_sync(kFull, a, 4));
+  d = __fdiv_rn(a, 127.0f);
+  const float inv = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
+  int q[4];
+  const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float t = __fmul_rn(e[j], inv);
+    q[j] = (t != t) ? 0 : __float2int_rn(fminf(fmaxf(t, -128.0f), 127.0f));
+  }
+  int s = q[0] + q[1] + q[2] + q[3];
+  s += __shfl_xor_sync(kFull, s, 1);
+  s += __shfl_xor_sync(kFull, s, 2);
+  s += __shfl_xor_sync(kFull, s, 4);
+  qsum = s;
+  return __byte_perm(__byte_perm((unsigned)q[0], (unsigned)q[1], 0x0040u),
+                     __byte_perm((unsigned)q[2], (unsigned)q[3], 0x0040u), 0x5410u);
+}
+
+// Bulk prefetch of [p, p + bytes) into L2 (sm_90+ bulk-copy unit).  Fire and
+// forget: nothing waits on it; p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// 16-byte asynchronous global -> shared copy (Ampere-style cp.async; the
+// wait below is a hardware wait on the copies this thread issued, no spin).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Programmatic dependent launch (sm_90+): `pdl_trigger` lets the next kernel
+// in the stream start launching; `pdl_wait` blocks until the previous kernel
+// has completed and its writes are visible.  Both are no-ops for a kernel
+// launched without the programmatic-serialization attribute.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // dp4a with unsigned bytes in `a` and signed bytes in `b`.
 __device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
   int d;

@@ -1,38 +1,46 @@
 // asmllm_b200/csrc/matvec.cu -- batch-1 quantized matvec kernels for sm_100a.
 //
-// Four kernel families, one per semantics of the reference library
-// (THRISHAL12345/asmllm):
-//   q4q8   Q4_0 weights x Q8_0 activations   src/kernels/arm64/matmul_q4_neon.S:38-317
-//   q8q8   Q8_0 weights x Q8_0 activations   (composed: same quantize/combine, s8 dot)
-//   q4f32  Q4_0 weights x fp32 activations   src/kernels/x86_64/matmul_q4_avx2.asm:100-262
-//   q8f32  Q8_0 weights x fp32 activations   src/kernels/x86_64/matmul_q8_avx2.asm:93-169
+// Semantics (reference THRISHAL12345/asmllm):
+//   Q4_0 x Q8_0   src/kernels/arm64/matmul_q4_neon.S:38-317   (asm_matmul_q4)
+//   Q8_0 x Q8_0   the same quantize and combine around an s8 dot (no reference kernel)
+//   Q4_0 x fp32   src/kernels/x86_64/matmul_q4_avx2.asm:100-262 (asm_matmul_q4_avx512 / _f32)
+//   Q8_0 x fp32   src/kernels/x86_64/matmul_q8_avx2.asm:93-169  (asm_matmul_q8)
 //
-// Design (all four are HBM-bound streams over the weights):
-//   * One CTA = 8 warps; the grid is persistent (at most the resident CTAs of
-//     all SMs) and the row groups are split evenly and contiguously over all
-//     warps.  A warp owns ROWS rows at a time and walks their blocks with its
-//     32 lanes; every weight byte is loaded once with 16-byte streaming loads
-//     (ld.global.nc.L1::no_allocate.L2::256B), ROWS*U of them in flight per
-//     lane.
-//   * The activation is staged in shared memory once per CTA.  For the Q8_0
-//     families each CTA quantizes x itself in its prologue (bit-exact with the
-//     reference, see common.cuh), so a matvec is one launch and needs no
-//     scratch memory.  The first weight tile is issued before the prologue so
-//     the quantize overlaps the HBM latency.
-//   * Shared layouts are padded per family so each lane's 16-byte reads of
-//     its block fall in distinct banks (48 B per Q8_0 block, 144 B per fp32
-//     block, 80 B per fp32 half block).
-//   * Q4 x Q8 block dot: isum = dp4a(lo_nibbles, xq[0:16]) + dp4a(hi_nibbles*16,
-//     xq[16:32])/16 - 8*sum(xq), exactly the reference's sum of (n-8)*q.
-//   * Combine per block: acc = fma(float(isum), wd*xd, acc) as the reference
-//     (matmul_q4_neon.S:241-243); the per-lane partial sums are then added
-//     with a warp butterfly, so y differs from the reference only by fp32
-//     summation order.
+// Design.  Every kernel here is an HBM-bound stream over the weights.
+//   * Unit of work: 16 weight bytes per lane -- one Q4_0 block (32 nibbles) or
+//     one half of a Q8_0 block.  A row is NU = K/32 (Q4) or K/16 (Q8) units at
+//     16-byte stride, so both formats share the addressing
+//     w + (row*NU + unit)*16 and every load is a coalesced 16-byte
+//     ld.global.nc.L1::no_allocate.L2::256B (each weight byte is read once).
+//   * A warp owns ROWS rows at a time; a "tile" is U units per lane for those
+//     rows.  Tiles are double-buffered in registers: the next tile's loads are
+//     in flight while the current one is consumed, so each warp keeps up to
+//     2*ROWS*U 16-byte loads outstanding.
+//   * The grid is persistent (at most the co-resident CTAs of all SMs) and the
+//     row groups are split evenly and contiguously over all warps.
+//   * The activation sits in shared memory, in a layout padded so each lane's
+//     16-byte reads hit distinct banks.  For the Q8_0 families it is the
+//     "activation image": per 32-block a 48-byte slot (32 int8 + 16 pad) and
+//     then (d, qsum) pairs -- written either by act_image_kernel (a pre-pass,
+//     once per x, shareable by several matvecs) or by the matvec's own
+//     prologue (FUSED: one launch, no scratch).  Both use quantize_quad, the
+//     bit-exact restatement of matmul_q4_neon.S:57-143.
+//   * Programmatic dependent launch: each kernel issues its first weight tile,
+//     lets the next kernel launch, then waits for the previous kernel before
+//     touching x / the image or writing y.  Consecutive matvecs overlap their
+//     ramp-up and tail; stream semantics are unchanged.
+//   * Q4 x Q8 block dot: isum = dp4a(lo nibbles, xq[0:16]) + dp4a(hi nibbles*16,
+//     xq[16:32])/16 - 8*sum(xq) == sum((n-8)*q), exact.  Combine per block:
+//     acc = fma(float(isum), wd*xd, acc) as the reference (matmul_q4_neon.S:241-243);
+//     lane partials are then added by a warp butterfly, so y differs from the
+//     reference only in fp32 summation order.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
+
 #include <cstdio>
 #include <cstdlib>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -44,11 +52,10 @@ namespace asmllm {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
+constexpr int kImgSlot = 48;  // bytes per 32-block of int8 in the activation image
 
-// Shared-memory bytes per block of K for each family.
-constexpr int kQ4Q8SmemPerBlock = 48 + 8;   // padded xq + (xd, qsum)
-constexpr int kQ8Q8SmemPerBlock = 32 + 4;   // xq + xd
-constexpr int kQ4F32SmemPerBlock = 36 * 4;  // 32 floats + 4 pad
+// Shared-memory bytes per 32-block of K for the fp32-activation families.
+constexpr int kQ4F32SmemPerBlock = 36 * 4;      // 32 floats + 4 pad
 constexpr int kQ8F32SmemPerBlock = 2 * 20 * 4;  // two half blocks of 16 floats + 4 pad
 
 __device__ __forceinline__ void group_range(int ngroups, int& g0, int& g1) {
@@ -58,77 +65,183 @@ __device__ __forceinline__ void group_range(int ngroups, int& g0, int& g1) {
   g1 = (int)(((long long)ngroups * (gw + 1)) / nw);
 }
 
+template <int ROWS, int U>
+struct Tile {
+  uint4 w[ROWS][U];
+  float sc[ROWS][U];
+};
+
+// Loads tile (group g, chunk c): units c*32*U + k*32 + lane, rows g*ROWS + r.
+template <int FMT, int ROWS, int U, bool F16S>
+__device__ __forceinline__ void load_tile(Tile<ROWS, U>& t, const uint8_t* __restrict__ w,
+                                          const void* __restrict__ scales, int M, int NU, int nb,
+                                          int g, int c, int lane) {
+#pragma unroll
+  for (int k = 0; k < U; ++k) {
+    const int u = c * 32 * U + k * 32 + lane;
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      const int row = g * ROWS + r;
+      if (u < NU && row < M) {
+        t.w[r][k] = ld_stream_v4(w + ((size_t)row * NU + u) * 16);
+        const int b = FMT == kFmtQ4_0 ? u : (u >> 1);
+        t.sc[r][k] = ScaleLoad<F16S>::load(scales, (size_t)row * nb + b);
+      } else {
+        t.w[r][k] = make_uint4(0u, 0u, 0u, 0u);
+        t.sc[r][k] = 0.0f;
+      }
+    }
+  }
+}
+
+// Bulk-prefetches the weight rows (and, when 16-byte aligned, the scales) of
+// row group g into L2; lanes 0..ROWS-1 each issue one row.
+template <int ROWS, bool F16S>
+__device__ __forceinline__ void prefetch_group(const uint8_t* __restrict__ w, const void* __restrict__ scales,
+                                               int M, int NU, int nb, int g, int lane) {
+  const int row = g * ROWS + lane;
+  if (lane < ROWS && row < M) {
+    prefetch_l2_bulk(w + (size_t)row * NU * 16, (unsigned)NU * 16u);
+    const size_t sb = (size_t)nb * (F16S ? 2 : 4);
+    if (sb % 16 == 0) prefetch_l2_bulk(static_cast<const unsigned char*>(scales) + (size_t)row * sb, (unsigned)sb);
+  }
+}
+
+// Sums each row's lane partials and stores y (lane r stores row r).
+template <int ROWS>
+__device__ __forceinline__ void finalize_rows(float (&acc)[ROWS], float* __restrict__ y, int g,
+                                              int M, int lane) {
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    const float v = warp_sum(acc[r]);
+    const int row = g * ROWS + r;
+    if (lane == r && row < M) y[row] = v;
+    acc[r] = 0.0f;
+  }
+}
+
 // --------------------------------------------------------------------------
-// Q4_0 x Q8_0
+// Activation image pre-pass: x fp32 [nrows][K] -> image [nrows][img_bytes(nb)]
 // --------------------------------------------------------------------------
-template <int ROWS, int U, bool F16S, bool DBG>
+// Before waiting for the previous kernel it bulk-prefetches into L2 the first
+// pf_bytes of the weights (and scales) of the matvec that will read this
+// image: this small kernel becomes resident while the previous kernel drains,
+// so HBM keeps streaming across the quantize -> matvec dependency chain.
+__device__ __forceinline__ void prefetch_range(const unsigned char* p, unsigned long long bytes) {
+  if (!p || bytes < 16) return;
+  const unsigned long long nthr = (unsigned long long)gridDim.x * blockDim.x;
+  const unsigned long long t = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x;
+  unsigned long long chunk = ((bytes + nthr - 1) / nthr + 4095) & ~4095ull;  // >= 4 KB per request
+  const unsigned long long beg = t * chunk;
+  if (beg >= bytes) return;
+  unsigned long long n = bytes - beg < chunk ? bytes - beg : chunk;
+  n &= ~15ull;
+  if (n) prefetch_l2_bulk(p + beg, (unsigned)n);
+}
+
 __global__ void __launch_bounds__(kThreads)
-q4q8_matvec_kernel(const uint8_t* __restrict__ qs, const void* __restrict__ scales,
-                   const float* __restrict__ x, float* __restrict__ y, int M, int nb,
-                   int32_t* __restrict__ isums) {
+act_image_kernel(const float* __restrict__ x, unsigned char* __restrict__ img, int nb,
+                 long long nrows, long long row_stride, const unsigned char* __restrict__ pf_w,
+                 unsigned long long pf_w_bytes, const unsigned char* __restrict__ pf_s,
+                 unsigned long long pf_s_bytes) {
+  pdl_trigger();
+  prefetch_range(pf_w, pf_w_bytes);
+  prefetch_range(pf_s, pf_s_bytes);
+  pdl_wait();  // x may come from the previous kernel; the image may still be read by it
+  const int lane8 = threadIdx.x & 7;
+  const long long total = nrows * nb;
+  const long long nw = (long long)gridDim.x * kWarps;
+  for (long long wb = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5); wb * 4 < total; wb += nw) {
+    const long long gb = wb * 4 + ((threadIdx.x & 31) >> 3);  // warp-uniform loop, 4 blocks per warp
+    const bool valid = gb < total;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid) v = reinterpret_cast<const float4*>(x + gb * QK)[lane8];
+    float d;
+    int qsum;
+    const unsigned q = quantize_quad(v, d, qsum);
+    if (valid) {
+      const long long n = gb / nb, b = gb - n * nb;
+      unsigned char* row = img + n * row_stride;
+      reinterpret_cast<unsigned*>(row + b * kImgSlot)[lane8] = q;
+      if (lane8 == 0) reinterpret_cast<float2*>(row + (size_t)nb * kImgSlot)[b] = make_float2(d, __int_as_float(qsum));
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Q8_0-activation matvec: Q4_0 (FMT 2) or Q8_0 (FMT 8) weights
+// --------------------------------------------------------------------------
+template <int FMT, int ROWS, int U, bool F16S, bool DBG, bool FUSED>
+__global__ void __launch_bounds__(kThreads, 2)
+q8act_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales,
+                    const void* __restrict__ act, float* __restrict__ y, int M, int nb,
+                    int32_t* __restrict__ isums, int pf, int pre) {
   extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* sxq = smem;                                    // nb * 48
-  float2* sdq = reinterpret_cast<float2*>(smem + (size_t)nb * 48);  // nb * 8
+  const float2* sdq = reinterpret_cast<const float2*>(smem + (size_t)nb * kImgSlot);
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  constexpr int UPB = FMT == kFmtQ4_0 ? 1 : 2;  // units per block
+  const int NU = nb * UPB;
   const int ngroups = (M + ROWS - 1) / ROWS;
   int g0, g1;
   group_range(ngroups, g0, g1);
-  constexpr int CH = 32 * U;  // blocks per chunk
-  const int nchunks = (nb + CH - 1) / CH;
+  constexpr int CH = 32 * U;
+  const int nchunks = (NU + CH - 1) / CH;
+  const int T = (g1 - g0) * nchunks;
 
-  uint4 w[ROWS][U];
-  float sc[ROWS][U];
+  // Weights are read before waiting for the previous kernel only when the
+  // caller declared them static (pre != 0); L2 prefetches are always safe
+  // (L2 is coherent, a prefetch never returns data to the SM).
+  Tile<ROWS, U> A, B;
+  if (pre && T > 0) load_tile<FMT, ROWS, U, F16S>(A, w, scales, M, NU, nb, g0, 0, lane);
+  for (int gp = g0 + 1; gp < g1 && gp <= g0 + pf; ++gp) prefetch_group<ROWS, F16S>(w, scales, M, NU, nb, gp, lane);
+  pdl_trigger();
+  pdl_wait();
+  if (!pre && T > 0) load_tile<FMT, ROWS, U, F16S>(A, w, scales, M, NU, nb, g0, 0, lane);
 
-  auto load_tile = [&](int g, int c) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int b = c * CH + u * 32 + lane;
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        const int row = g * ROWS + r;
-        if (b < nb && row < M) {
-          const size_t blk = (size_t)row * nb + b;
-          w[r][u] = ld_stream_v4(qs + blk * 16);
-          sc[r][u] = ScaleLoad<F16S>::load(scales, blk);
-        } else {
-          w[r][u] = make_uint4(0u, 0u, 0u, 0u);
-          sc[r][u] = 0.0f;
-        }
+  if (FUSED) {
+    // Quantize x into the shared image: 8 lanes per block, 32 blocks per pass.
+    const float* x = static_cast<const float*>(act);
+    const int lane8 = threadIdx.x & 7;
+#pragma unroll 2
+    for (int base = 0; base < nb; base += kThreads / 8) {
+      const int b = base + (threadIdx.x >> 3);
+      const bool valid = b < nb;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid) v = reinterpret_cast<const float4*>(x + (size_t)b * QK)[lane8];
+      float d;
+      int qsum;
+      const unsigned q = quantize_quad(v, d, qsum);
+      if (valid) {
+        reinterpret_cast<unsigned*>(smem + b * kImgSlot)[lane8] = q;
+        if (lane8 == 0) reinterpret_cast<float2*>(smem + (size_t)nb * kImgSlot)[b] = make_float2(d, __int_as_float(qsum));
       }
     }
-  };
-
-  if (g0 < g1) load_tile(g0, 0);
-
-  // Prologue: quantize x (fp32[K]) into shared memory, one warp per block.
-  for (int b = warp; b < nb; b += kWarps) {
-    float d;
-    int qsum;
-    const int q = quantize_block_lane(x[(size_t)b * QK + lane], d, qsum);
-    sxq[b * 48 + lane] = (unsigned char)(q & 0xff);
-    if (lane == 0) sdq[b] = make_float2(d, __int_as_float(qsum));
+  } else {
+    const unsigned char* img = static_cast<const unsigned char*>(act);
+    const int n16 = (int)(act_image_bytes(nb) / 16);
+    for (int i = threadIdx.x; i < n16; i += kThreads) cp_async16(smem + 16 * i, img + 16 * i);
+    cp_async_wait_all();
   }
   __syncthreads();
 
-  for (int g = g0; g < g1; ++g) {
-    float acc[ROWS];
+  float acc[ROWS];
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-    for (int c = 0; c < nchunks; ++c) {
-      if (g != g0 || c != 0) load_tile(g, c);
+  for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+
+  auto compute = [&](const Tile<ROWS, U>& t, int g, int c) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int b = c * CH + u * 32 + lane;
-        if (b < nb) {
-          const uint4* xp = reinterpret_cast<const uint4*>(sxq + b * 48);
-          const uint4 xa = xp[0];  // xq[0..15]  (pairs with low nibbles)
-          const uint4 xb = xp[1];  // xq[16..31] (pairs with high nibbles)
-          const float2 dq = sdq[b];
+    for (int k = 0; k < U; ++k) {
+      const int u = c * CH + k * 32 + lane;
+      if (FMT == kFmtQ4_0) {
+        if (u < NU) {
+          const uint4* xp = reinterpret_cast<const uint4*>(smem + u * kImgSlot);
+          const uint4 xa = xp[0];  // xq[0..15]  with the low nibbles
+          const uint4 xb = xp[1];  // xq[16..31] with the high nibbles
+          const float2 dq = sdq[u];
           const int qsum8 = __float_as_int(dq.y) * 8;
 #pragma unroll
           for (int r = 0; r < ROWS; ++r) {
-            const uint4 q = w[r][u];
+            const uint4 q = t.w[r][k];
             int lo = 0, hi = 0;
             lo = dp4a_us(q.x & 0x0F0F0F0Fu, (int)xa.x, lo);
             hi = dp4a_us(q.x & 0xF0F0F0F0u, (int)xb.x, hi);
@@ -141,93 +254,23 @@ q4q8_matvec_kernel(const uint8_t* __restrict__ qs, const void* __restrict__ scal
             const int isum = lo + (hi >> 4) - qsum8;
             if (DBG) {
               const int row = g * ROWS + r;
-              if (row < M) isums[(size_t)row * nb + b] = isum;
+              if (row < M) isums[(size_t)row * nb + u] = isum;
             }
-            acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc[r][u], dq.x), acc[r]);
+            acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(t.sc[r][k], dq.x), acc[r]);
           }
         }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      const float v = warp_sum(acc[r]);
-      const int row = g * ROWS + r;
-      if (lane == r && row < M) y[row] = v;
-    }
-  }
-}
-
-// --------------------------------------------------------------------------
-// Q8_0 x Q8_0 (lane pairs share a block: each lane loads one 16-byte half)
-// --------------------------------------------------------------------------
-template <int ROWS, int U, bool F16S, bool DBG>
-__global__ void __launch_bounds__(kThreads)
-q8q8_matvec_kernel(const int8_t* __restrict__ qw, const void* __restrict__ scales,
-                   const float* __restrict__ x, float* __restrict__ y, int M, int nb,
-                   int32_t* __restrict__ isums) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  unsigned char* sxq = smem;                                  // nb * 32
-  float* sd = reinterpret_cast<float*>(smem + (size_t)nb * 32);  // nb * 4
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int ngroups = (M + ROWS - 1) / ROWS;
-  int g0, g1;
-  group_range(ngroups, g0, g1);
-  const int nhb = 2 * nb;
-  constexpr int CH = 32 * U;  // half blocks per chunk
-  const int nchunks = (nhb + CH - 1) / CH;
-
-  uint4 w[ROWS][U];
-  float sc[ROWS][U];
-
-  auto load_tile = [&](int g, int c) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int hb = c * CH + u * 32 + lane;
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        const int row = g * ROWS + r;
-        if (hb < nhb && row < M) {
-          w[r][u] = ld_stream_v4(qw + ((size_t)row * nb * 32 + (size_t)hb * 16));
-          sc[r][u] = ScaleLoad<F16S>::load(scales, (size_t)row * nb + (hb >> 1));
-        } else {
-          w[r][u] = make_uint4(0u, 0u, 0u, 0u);
-          sc[r][u] = 0.0f;
-        }
-      }
-    }
-  };
-
-  if (g0 < g1) load_tile(g0, 0);
-
-  for (int b = warp; b < nb; b += kWarps) {
-    float d;
-    int qsum;
-    const int q = quantize_block_lane(x[(size_t)b * QK + lane], d, qsum);
-    sxq[b * 32 + lane] = (unsigned char)(q & 0xff);
-    if (lane == 0) sd[b] = d;
-  }
-  __syncthreads();
-
-  for (int g = g0; g < g1; ++g) {
-    float acc[ROWS];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-    for (int c = 0; c < nchunks; ++c) {
-      if (g != g0 || c != 0) load_tile(g, c);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int hb = c * CH + u * 32 + lane;
-        const bool valid = hb < nhb;  // same for both lanes of a pair
+      } else {
+        const bool valid = u < NU;  // same for both lanes of a pair (NU even, chunks of 32)
+        const int b = u >> 1;
         uint4 xa = make_uint4(0u, 0u, 0u, 0u);
         float xd = 0.0f;
         if (valid) {
-          xa = reinterpret_cast<const uint4*>(sxq)[hb];
-          xd = sd[hb >> 1];
+          xa = *reinterpret_cast<const uint4*>(smem + b * kImgSlot + (u & 1) * 16);
+          xd = sdq[b].x;
         }
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) {
-          const uint4 q = w[r][u];
+          const uint4 q = t.w[r][k];
           int part = 0;
           part = dp4a_ss((int)q.x, (int)xa.x, part);
           part = dp4a_ss((int)q.y, (int)xa.y, part);
@@ -237,215 +280,170 @@ q8q8_matvec_kernel(const int8_t* __restrict__ qw, const void* __restrict__ scale
           if (valid && !(lane & 1)) {
             if (DBG) {
               const int row = g * ROWS + r;
-              if (row < M) isums[(size_t)row * nb + (hb >> 1)] = isum;
+              if (row < M) isums[(size_t)row * nb + b] = isum;
             }
-            acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc[r][u], xd), acc[r]);
+            acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(t.sc[r][k], xd), acc[r]);
           }
         }
       }
     }
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      const float v = warp_sum(acc[r]);
-      const int row = g * ROWS + r;
-      if (lane == r && row < M) y[row] = v;
+    if (c == nchunks - 1) {
+      finalize_rows<ROWS>(acc, y, g, M, lane);
+      if (pf > 0 && g + pf + 1 < g1) prefetch_group<ROWS, F16S>(w, scales, M, NU, nb, g + pf + 1, lane);
     }
+  };
+
+  int g = g0, c = 0;
+  for (int t = 0; t < T; t += 2) {
+    int gb = g, cb = c + 1;
+    if (cb == nchunks) { cb = 0; ++gb; }
+    if (t + 1 < T) load_tile<FMT, ROWS, U, F16S>(B, w, scales, M, NU, nb, gb, cb, lane);
+    compute(A, g, c);
+    int ga = gb, ca = cb + 1;
+    if (ca == nchunks) { ca = 0; ++ga; }
+    if (t + 2 < T) load_tile<FMT, ROWS, U, F16S>(A, w, scales, M, NU, nb, ga, ca, lane);
+    if (t + 1 < T) compute(B, gb, cb);
+    g = ga;
+    c = ca;
   }
 }
 
 // --------------------------------------------------------------------------
-// Q4_0 x fp32 (x86 semantics)
+// fp32-activation matvec (x86 semantics): Q4_0 (FMT 2) or Q8_0 (FMT 8)
 // --------------------------------------------------------------------------
-template <int ROWS, int U, bool F16S>
-__global__ void __launch_bounds__(kThreads)
-q4f32_matvec_kernel(const uint8_t* __restrict__ qs, const void* __restrict__ scales,
-                    const float* __restrict__ x, float* __restrict__ y, int M, int nb) {
+template <int FMT, int ROWS, int U, bool F16S>
+__global__ void __launch_bounds__(kThreads, 2)
+f32act_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales,
+                     const float* __restrict__ x, float* __restrict__ y, int M, int nb, int pf, int pre) {
   extern __shared__ __align__(16) unsigned char smem[];
-  float* sx = reinterpret_cast<float*>(smem);  // nb * 36 floats
+  float* sx = reinterpret_cast<float*>(smem);
   const int lane = threadIdx.x & 31;
+  constexpr int UPB = FMT == kFmtQ4_0 ? 1 : 2;
+  const int NU = nb * UPB;
   const int ngroups = (M + ROWS - 1) / ROWS;
   int g0, g1;
   group_range(ngroups, g0, g1);
   constexpr int CH = 32 * U;
-  const int nchunks = (nb + CH - 1) / CH;
+  const int nchunks = (NU + CH - 1) / CH;
+  const int T = (g1 - g0) * nchunks;
 
-  uint4 w[ROWS][U];
-  float sc[ROWS][U];
-
-  auto load_tile = [&](int g, int c) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int b = c * CH + u * 32 + lane;
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        const int row = g * ROWS + r;
-        if (b < nb && row < M) {
-          const size_t blk = (size_t)row * nb + b;
-          w[r][u] = ld_stream_v4(qs + blk * 16);
-          sc[r][u] = ScaleLoad<F16S>::load(scales, blk);
-        } else {
-          w[r][u] = make_uint4(0u, 0u, 0u, 0u);
-          sc[r][u] = 0.0f;
-        }
-      }
-    }
-  };
-
-  if (g0 < g1) load_tile(g0, 0);
+  // Weights are read before waiting for the previous kernel only when the
+  // caller declared them static (pre != 0); L2 prefetches are always safe
+  // (L2 is coherent, a prefetch never returns data to the SM).
+  Tile<ROWS, U> A, B;
+  if (pre && T > 0) load_tile<FMT, ROWS, U, F16S>(A, w, scales, M, NU, nb, g0, 0, lane);
+  for (int gp = g0 + 1; gp < g1 && gp <= g0 + pf; ++gp) prefetch_group<ROWS, F16S>(w, scales, M, NU, nb, gp, lane);
+  pdl_trigger();
+  pdl_wait();
+  if (!pre && T > 0) load_tile<FMT, ROWS, U, F16S>(A, w, scales, M, NU, nb, g0, 0, lane);
 
   const int K = nb * QK;
-  for (int i = threadIdx.x; i < K; i += kThreads) sx[(i >> 5) * 36 + (i & 31)] = x[i];
+  if (FMT == kFmtQ4_0) {
+    for (int i = threadIdx.x; i < K; i += kThreads) sx[(i >> 5) * 36 + (i & 31)] = x[i];
+  } else {
+    for (int i = threadIdx.x; i < K; i += kThreads) sx[(i >> 4) * 20 + (i & 15)] = x[i];
+  }
   __syncthreads();
 
-  for (int g = g0; g < g1; ++g) {
-    float acc[ROWS];
+  float acc[ROWS];
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-    for (int c = 0; c < nchunks; ++c) {
-      if (g != g0 || c != 0) load_tile(g, c);
+  for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+
+  auto compute = [&](const Tile<ROWS, U>& t, int g, int c) {
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int b = c * CH + u * 32 + lane;
-        if (b < nb) {
-          const float4* xp = reinterpret_cast<const float4*>(sx + b * 36);
-          float blk[ROWS];
+    for (int k = 0; k < U; ++k) {
+      const int u = c * CH + k * 32 + lane;
+      if (u < NU) {
+        float blk[ROWS];
 #pragma unroll
-          for (int r = 0; r < ROWS; ++r) blk[r] = 0.0f;
+        for (int r = 0; r < ROWS; ++r) blk[r] = 0.0f;
+        if (FMT == kFmtQ4_0) {
+          const float4* xp = reinterpret_cast<const float4*>(sx + u * 36);
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float4 xl = xp[k];      // elements 4k .. 4k+3
-            const float4 xh = xp[4 + k];  // elements 16+4k .. 16+4k+3
+          for (int j = 0; j < 4; ++j) {
+            const float4 xl = xp[j];      // elements 4j .. 4j+3 (low nibbles of bytes 4j..)
+            const float4 xh = xp[4 + j];  // elements 16+4j .. (high nibbles)
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) {
-              const unsigned word = k == 0 ? w[r][u].x : k == 1 ? w[r][u].y : k == 2 ? w[r][u].z : w[r][u].w;
+              const unsigned word = j == 0 ? t.w[r][k].x : j == 1 ? t.w[r][k].y : j == 2 ? t.w[r][k].z : t.w[r][k].w;
               const unsigned lo = word & 0x0F0F0F0Fu;
               const unsigned hi = (word >> 4) & 0x0F0F0F0Fu;
-              float t = blk[r];
-              t = __fmaf_rn(u4_to_f32_minus8(lo, 0), xl.x, t);
-              t = __fmaf_rn(u4_to_f32_minus8(lo, 1), xl.y, t);
-              t = __fmaf_rn(u4_to_f32_minus8(lo, 2), xl.z, t);
-              t = __fmaf_rn(u4_to_f32_minus8(lo, 3), xl.w, t);
-              t = __fmaf_rn(u4_to_f32_minus8(hi, 0), xh.x, t);
-              t = __fmaf_rn(u4_to_f32_minus8(hi, 1), xh.y, t);
-              t = __fmaf_rn(u4_to_f32_minus8(hi, 2), xh.z, t);
-              t = __fmaf_rn(u4_to_f32_minus8(hi, 3), xh.w, t);
-              blk[r] = t;
+              float s = blk[r];
+              s = __fmaf_rn(u4_to_f32_minus8(lo, 0), xl.x, s);
+              s = __fmaf_rn(u4_to_f32_minus8(lo, 1), xl.y, s);
+              s = __fmaf_rn(u4_to_f32_minus8(lo, 2), xl.z, s);
+              s = __fmaf_rn(u4_to_f32_minus8(lo, 3), xl.w, s);
+              s = __fmaf_rn(u4_to_f32_minus8(hi, 0), xh.x, s);
+              s = __fmaf_rn(u4_to_f32_minus8(hi, 1), xh.y, s);
+              s = __fmaf_rn(u4_to_f32_minus8(hi, 2), xh.z, s);
+              s = __fmaf_rn(u4_to_f32_minus8(hi, 3), xh.w, s);
+              blk[r] = s;
             }
           }
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(blk[r], sc[r][u], acc[r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      const float v = warp_sum(acc[r]);
-      const int row = g * ROWS + r;
-      if (lane == r && row < M) y[row] = v;
-    }
-  }
-}
-
-// --------------------------------------------------------------------------
-// Q8_0 x fp32 (x86 semantics); each lane takes one 16-element half block
-// --------------------------------------------------------------------------
-template <int ROWS, int U, bool F16S>
-__global__ void __launch_bounds__(kThreads)
-q8f32_matvec_kernel(const int8_t* __restrict__ qw, const void* __restrict__ scales,
-                    const float* __restrict__ x, float* __restrict__ y, int M, int nb) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* sx = reinterpret_cast<float*>(smem);  // 2*nb half blocks * 20 floats
-  const int lane = threadIdx.x & 31;
-  const int ngroups = (M + ROWS - 1) / ROWS;
-  int g0, g1;
-  group_range(ngroups, g0, g1);
-  const int nhb = 2 * nb;
-  constexpr int CH = 32 * U;
-  const int nchunks = (nhb + CH - 1) / CH;
-
-  uint4 w[ROWS][U];
-  float sc[ROWS][U];
-
-  auto load_tile = [&](int g, int c) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int hb = c * CH + u * 32 + lane;
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r) {
-        const int row = g * ROWS + r;
-        if (hb < nhb && row < M) {
-          w[r][u] = ld_stream_v4(qw + ((size_t)row * nb * 32 + (size_t)hb * 16));
-          sc[r][u] = ScaleLoad<F16S>::load(scales, (size_t)row * nb + (hb >> 1));
         } else {
-          w[r][u] = make_uint4(0u, 0u, 0u, 0u);
-          sc[r][u] = 0.0f;
+          const float4* xp = reinterpret_cast<const float4*>(sx + u * 20);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 xv = xp[j];
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) {
+              const unsigned word = (j == 0 ? t.w[r][k].x : j == 1 ? t.w[r][k].y : j == 2 ? t.w[r][k].z : t.w[r][k].w) ^ 0x80808080u;
+              float s = blk[r];
+              s = __fmaf_rn(s8_biased_to_f32(word, 0), xv.x, s);
+              s = __fmaf_rn(s8_biased_to_f32(word, 1), xv.y, s);
+              s = __fmaf_rn(s8_biased_to_f32(word, 2), xv.z, s);
+              s = __fmaf_rn(s8_biased_to_f32(word, 3), xv.w, s);
+              blk[r] = s;
+            }
+          }
         }
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(blk[r], t.sc[r][k], acc[r]);
       }
+    }
+    if (c == nchunks - 1) {
+      finalize_rows<ROWS>(acc, y, g, M, lane);
+      if (pf > 0 && g + pf + 1 < g1) prefetch_group<ROWS, F16S>(w, scales, M, NU, nb, g + pf + 1, lane);
     }
   };
 
-  if (g0 < g1) load_tile(g0, 0);
-
-  const int K = nb * QK;
-  for (int i = threadIdx.x; i < K; i += kThreads) sx[(i >> 4) * 20 + (i & 15)] = x[i];
-  __syncthreads();
-
-  for (int g = g0; g < g1; ++g) {
-    float acc[ROWS];
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-    for (int c = 0; c < nchunks; ++c) {
-      if (g != g0 || c != 0) load_tile(g, c);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int hb = c * CH + u * 32 + lane;
-        if (hb < nhb) {
-          const float4* xp = reinterpret_cast<const float4*>(sx + hb * 20);
-          float blk[ROWS];
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) blk[r] = 0.0f;
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const float4 xv = xp[k];
-#pragma unroll
-            for (int r = 0; r < ROWS; ++r) {
-              const unsigned word = (k == 0 ? w[r][u].x : k == 1 ? w[r][u].y : k == 2 ? w[r][u].z : w[r][u].w) ^ 0x80808080u;
-              float t = blk[r];
-              t = __fmaf_rn(s8_biased_to_f32(word, 0), xv.x, t);
-              t = __fmaf_rn(s8_biased_to_f32(word, 1), xv.y, t);
-              t = __fmaf_rn(s8_biased_to_f32(word, 2), xv.z, t);
-              t = __fmaf_rn(s8_biased_to_f32(word, 3), xv.w, t);
-              blk[r] = t;
-            }
-          }
-#pragma unroll
-          for (int r = 0; r < ROWS; ++r) acc[r] = __fmaf_rn(blk[r], sc[r][u], acc[r]);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      const float v = warp_sum(acc[r]);
-      const int row = g * ROWS + r;
-      if (lane == r && row < M) y[row] = v;
-    }
+  int g = g0, c = 0;
+  for (int t = 0; t < T; t += 2) {
+    int gb = g, cb = c + 1;
+    if (cb == nchunks) { cb = 0; ++gb; }
+    if (t + 1 < T) load_tile<FMT, ROWS, U, F16S>(B, w, scales, M, NU, nb, gb, cb, lane);
+    compute(A, g, c);
+    int ga = gb, ca = cb + 1;
+    if (ca == nchunks) { ca = 0; ++ga; }
+    if (t + 2 < T) load_tile<FMT, ROWS, U, F16S>(A, w, scales, M, NU, nb, ga, ca, lane);
+    if (t + 1 < T) compute(B, gb, cb);
+    g = ga;
+    c = ca;
   }
 }
 
 // --------------------------------------------------------------------------
-// Standalone / batched activation quantize: one warp per 32-block.
+// Standalone / batched activation quantize to separate xq / xd arrays.
 // --------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads)
 quantize_q8_0_kernel(const float* __restrict__ x, int8_t* __restrict__ xq,
                      float* __restrict__ xd, long long nblocks) {
-  const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
+  const int lane8 = threadIdx.x & 7;
   const long long nw = (long long)gridDim.x * kWarps;
-  for (long long b = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5); b < nblocks; b += nw) {
+  for (long long wb = (long long)blockIdx.x * kWarps + (threadIdx.x >> 5); wb * 4 < nblocks; wb += nw) {
+    const long long gb = wb * 4 + ((threadIdx.x & 31) >> 3);
+    const bool valid = gb < nblocks;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (valid) v = reinterpret_cast<const float4*>(x + gb * QK)[lane8];
     float d;
     int qsum;
-    const int q = quantize_block_lane(x[b * QK + lane], d, qsum);
-    xq[b * QK + lane] = (int8_t)q;
-    if (lane == 0) xd[b] = d;
+    const unsigned q = quantize_quad(v, d, qsum);
+    if (valid) {
+      reinterpret_cast<unsigned*>(xq + gb * QK)[lane8] = q;
+      if (lane8 == 0) xd[gb] = d;
+    }
   }
 }
 
@@ -485,7 +483,6 @@ struct DevInfo {
   bool init = false;
 };
 DevInfo g_dev[64];
-
 std::mutex g_dev_mu;
 
 const DevInfo& dev_info(int dev) {
@@ -499,14 +496,59 @@ const DevInfo& dev_info(int dev) {
   return d;
 }
 
+}  // namespace
+
+std::atomic<int> g_opt_pdl{[] {
+  const char* e = getenv("ASMLLM_PDL");
+  return (e && e[0] == '0') ? 0 : 1;
+}()};
+
+namespace {
+
+}  // namespace
+
+// Runtime switches (asm_set_option): bulk-copy pipeline kernel for the Q8_0
+// families (else the register-streaming kernels) and programmatic dependent
+// launch.  Initial values from ASMLLM_TMA / ASMLLM_PDL (default on).
+std::atomic<int> g_opt_tma{[] {
+  const char* e = getenv("ASMLLM_TMA");
+  return (e && e[0] == '0') ? 0 : 1;
+}()};
+
+namespace {
+
 // Occupancy of each (kernel, shared bytes, device), computed once: later
 // launches (including ones recorded into a CUDA graph) only do the launch.
 std::mutex g_occ_mu;
 std::map<std::tuple<const void*, size_t, int>, int> g_occ;
 
+cudaError_t launch_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       void** args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_opt_pdl.load() ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, kernel, args);
+}
+
+// Tunables (environment, read once): CTAs per SM cap and L2 prefetch budget.
+int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : dflt;
+}
+const int g_cta_cap = env_int("ASMLLM_CTAS_PER_SM", 0);      // 0: heuristic
+const int g_pf_budget_kb = env_int("ASMLLM_PF_KB", 24);       // per-warp L2 prefetch window
+const int g_img_pf_mb = env_int("ASMLLM_IMG_PF_MB", 0);       // quantize-kernel prefetch of the next weights (MB)
+
 template <typename KernelT>
 cudaError_t launch_persistent(KernelT kernel, int ngroups, size_t smem, cudaStream_t stream,
-                              int dev, void** args) {
+                              int dev, void** args, int* pf_arg = nullptr, size_t group_bytes = 0) {
   const DevInfo& di = dev_info(dev);
   const auto key = std::make_tuple((const void*)kernel, smem, dev);
   int per_sm = 0;
@@ -526,51 +568,89 @@ cudaError_t launch_persistent(KernelT kernel, int ngroups, size_t smem, cudaStre
     std::lock_guard<std::mutex> lk(g_occ_mu);
     g_occ[key] = per_sm;
   }
+  // All co-resident CTAs by default (ASMLLM_CTAS_PER_SM caps it for experiments).
+  int cap = g_cta_cap > 0 ? g_cta_cap : per_sm;
+  if (cap > per_sm) cap = per_sm;
   const long long needed = ((long long)ngroups + kWarps - 1) / kWarps;
-  long long grid = (long long)per_sm * di.sms;
+  long long grid = (long long)cap * di.sms;
   if (needed < grid) grid = needed;
   if (grid < 1) grid = 1;
-  return cudaLaunchKernel((const void*)kernel, dim3((unsigned)grid), dim3(kThreads), args, smem, stream);
+  if (pf_arg) {
+    const long long groups_per_warp = ((long long)ngroups + grid * kWarps - 1) / (grid * kWarps);
+    long long pf = group_bytes ? ((long long)g_pf_budget_kb * 1024) / (long long)group_bytes : 0;
+    if (pf > groups_per_warp) pf = groups_per_warp;
+    *pf_arg = (int)pf;
+  }
+  return launch_pdl((const void*)kernel, dim3((unsigned)grid), dim3(kThreads), smem, stream, args);
+}
+
+// Kernel configuration: rows per warp x units per lane per tile.
+struct Cfg {
+  int rows, u;
+};
+
+Cfg pick_cfg(int M, int NU, int sms, bool fp32_act) {
+  (void)NU;
+  if (fp32_act) return {2, 2};
+  if ((long long)M < (long long)sms * kWarps * 4) return {1, 4};
+  return {2, 2};
+}
+
+Cfg cfg_override(Cfg c) {
+  static int forced_rows = -1, forced_u = -1;
+  if (forced_rows < 0) {
+    forced_rows = 0;
+    const char* s = getenv("ASMLLM_MATVEC_CFG");
+    int r = 0, u = 0;
+    if (s && sscanf(s, "%dx%d", &r, &u) == 2) {
+      forced_rows = r;
+      forced_u = u;
+    }
+  }
+  if (forced_rows > 0) return {forced_rows, forced_u};
+  return c;
+}
+
+template <int FMT, int R, int U>
+cudaError_t launch_q8act_cfg(const MatvecArgs& a, int ngroups, size_t smem, cudaStream_t stream, int dev,
+                             void** args) {
+  const bool fused = a.image == nullptr;
+  int* pf = static_cast<int*>(args[7]);
+  const size_t gb = (size_t)R * (size_t)(a.K / QK) * ((FMT == kFmtQ4_0 ? 16 : 32) + (a.scales_f16 ? 2 : 4));
+  if (a.isums) {
+    if (fused)
+      return launch_persistent(q8act_matvec_kernel<FMT, R, U, false, true, true>, ngroups, smem, stream, dev, args, pf, gb);
+    return launch_persistent(q8act_matvec_kernel<FMT, R, U, false, true, false>, ngroups, smem, stream, dev, args, pf, gb);
+  }
+  if (a.scales_f16) {
+    if (fused)
+      return launch_persistent(q8act_matvec_kernel<FMT, R, U, true, false, true>, ngroups, smem, stream, dev, args, pf, gb);
+    return launch_persistent(q8act_matvec_kernel<FMT, R, U, true, false, false>, ngroups, smem, stream, dev, args, pf, gb);
+  }
+  if (fused)
+    return launch_persistent(q8act_matvec_kernel<FMT, R, U, false, false, true>, ngroups, smem, stream, dev, args, pf, gb);
+  return launch_persistent(q8act_matvec_kernel<FMT, R, U, false, false, false>, ngroups, smem, stream, dev, args, pf, gb);
+}
+
+template <int FMT>
+cudaError_t launch_q8act(const MatvecArgs& a, Cfg c, int M, int nb, cudaStream_t stream, int dev, void** args) {
+  const int ngroups = (M + c.rows - 1) / c.rows;
+  const size_t smem = act_image_bytes(nb);
+  if (c.rows == 1 && c.u == 2) return launch_q8act_cfg<FMT, 1, 2>(a, ngroups, smem, stream, dev, args);
+  if (c.rows == 1 && c.u == 4) return launch_q8act_cfg<FMT, 1, 4>(a, ngroups, smem, stream, dev, args);
+  if (c.rows == 2 && c.u == 4) return launch_q8act_cfg<FMT, 2, 4>(a, ngroups, smem, stream, dev, args);
+  const int ng2 = (M + 1) / 2;
+  return launch_q8act_cfg<FMT, 2, 2>(a, ng2, smem, stream, dev, args);
 }
 
 }  // namespace
 
 int64_t max_k(int fmt, bool fp32_act, int dev) {
   const DevInfo& di = dev_info(dev);
-  const int per_block = fmt == kFmtQ4_0 ? (fp32_act ? kQ4F32SmemPerBlock : kQ4Q8SmemPerBlock)
-                                        : (fp32_act ? kQ8F32SmemPerBlock : kQ8Q8SmemPerBlock);
-  const int64_t nb = di.smem_optin / per_block;
-  int64_t k = nb * QK;
-  if (k > (int64_t)1 << 30) k = (int64_t)1 << 30;
-  return k;
+  const int per_block = fp32_act ? (fmt == kFmtQ4_0 ? kQ4F32SmemPerBlock : kQ8F32SmemPerBlock) : (kImgSlot + 8);
+  const int64_t nb = (di.smem_optin - 16) / per_block;
+  return nb * QK;
 }
-
-// Kernel configuration: rows per warp x 32-block iterations per load batch.
-// Chosen from the shape; ASMLLM_MATVEC_CFG=<rows>x<u> forces one for sweeps.
-struct Cfg { int rows, u; };
-
-static Cfg pick_cfg(int M, int nb, int sms) {
-  (void)nb;
-  // Two rows per warp keeps 8 x 16-byte loads in flight per lane at K=4096;
-  // small M drops to one row so every SM gets several warps.
-  if ((long long)M < (long long)sms * kWarps * 4) return {1, 4};
-  return {2, 4};
-}
-
-static Cfg cfg_override(Cfg c) {
-  static int forced_rows = -1, forced_u = -1;
-  if (forced_rows < 0) {
-    forced_rows = 0;
-    const char* s = getenv("ASMLLM_MATVEC_CFG");
-    int r = 0, u = 0;
-    if (s && sscanf(s, "%dx%d", &r, &u) == 2) { forced_rows = r; forced_u = u; }
-  }
-  if (forced_rows > 0) return {forced_rows, forced_u};
-  return c;
-}
-
-#define ASMLLM_DISPATCH_RU(ROWS_, U_, CALL)                                    \
-  if (c.rows == ROWS_ && c.u == U_) { CALL(ROWS_, U_); }
 
 cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
   int dev = 0;
@@ -581,63 +661,69 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
   const int nb = (int)(a.K / QK);
   if (nb == 0) return cudaMemsetAsync(a.y, 0, (size_t)a.M * sizeof(float), stream);
   const DevInfo& di = dev_info(dev);
-  Cfg c = cfg_override(pick_cfg(M, nb, di.sms));
-  if (!((c.rows == 1 || c.rows == 2 || c.rows == 4) && (c.u == 2 || c.u == 4))) c = {2, 4};
+  const int NU = a.fmt == kFmtQ4_0 ? nb : 2 * nb;
+  const Cfg c = cfg_override(pick_cfg(M, NU, di.sms, a.fp32_act));
 
   const void* w = a.w;
   const void* s = a.scales;
-  const float* x = a.x;
+  const void* act = a.image ? a.image : (const void*)a.x;
   float* y = a.y;
   int32_t* isums = a.isums;
   int Mi = M, nbi = nb;
-  void* args7[] = {(void*)&w, (void*)&s, (void*)&x, (void*)&y, (void*)&Mi, (void*)&nbi, (void*)&isums};
-  void* args6[] = {(void*)&w, (void*)&s, (void*)&x, (void*)&y, (void*)&Mi, (void*)&nbi};
 
+  int pf = 0;
+  int pre = a.weights_static ? 1 : 0;
+  if (!a.fp32_act && g_opt_tma.load() && !a.isums_force_ldg && tma_matvec_supported(a, di.smem_optin))
+    return launch_tma_matvec(a, di.sms, di.smem_optin, stream, g_opt_pdl.load() != 0);
   if (!a.fp32_act) {
-    const bool q4 = a.fmt == kFmtQ4_0;
-    const int rows_for_groups = c.rows;
-    const int ngroups = (M + rows_for_groups - 1) / rows_for_groups;
-    const size_t smem = (size_t)nb * (q4 ? kQ4Q8SmemPerBlock : kQ8Q8SmemPerBlock);
-    if (smem > (size_t)di.smem_optin) return cudaErrorInvalidValue;
-#define CALL_Q8ACT(R, U)                                                                      \
-  {                                                                                           \
-    if (q4) {                                                                                 \
-      if (a.isums) {                                                                          \
-        return a.scales_f16 ? launch_persistent(q4q8_matvec_kernel<R, U, true, true>, ngroups, smem, stream, dev, args7)   \
-                            : launch_persistent(q4q8_matvec_kernel<R, U, false, true>, ngroups, smem, stream, dev, args7); \
-      }                                                                                       \
-      return a.scales_f16 ? launch_persistent(q4q8_matvec_kernel<R, U, true, false>, ngroups, smem, stream, dev, args7)    \
-                          : launch_persistent(q4q8_matvec_kernel<R, U, false, false>, ngroups, smem, stream, dev, args7);  \
-    }                                                                                         \
-    if (a.isums) {                                                                            \
-      return a.scales_f16 ? launch_persistent(q8q8_matvec_kernel<R, U, true, true>, ngroups, smem, stream, dev, args7)     \
-                          : launch_persistent(q8q8_matvec_kernel<R, U, false, true>, ngroups, smem, stream, dev, args7);   \
-    }                                                                                         \
-    return a.scales_f16 ? launch_persistent(q8q8_matvec_kernel<R, U, true, false>, ngroups, smem, stream, dev, args7)      \
-                        : launch_persistent(q8q8_matvec_kernel<R, U, false, false>, ngroups, smem, stream, dev, args7);    \
+    if (act_image_bytes(nb) > (size_t)di.smem_optin) return cudaErrorInvalidValue;
+    void* args[] = {(void*)&w, (void*)&s, (void*)&act, (void*)&y, (void*)&Mi, (void*)&nbi, (void*)&isums, (void*)&pf, (void*)&pre};
+    return a.fmt == kFmtQ4_0 ? launch_q8act<kFmtQ4_0>(a, c, M, nb, stream, dev, args)
+                             : launch_q8act<kFmtQ8_0>(a, c, M, nb, stream, dev, args);
   }
-    ASMLLM_DISPATCH_RU(1, 4, CALL_Q8ACT)
-    ASMLLM_DISPATCH_RU(2, 4, CALL_Q8ACT)
-    ASMLLM_DISPATCH_RU(4, 4, CALL_Q8ACT)
-    ASMLLM_DISPATCH_RU(1, 2, CALL_Q8ACT)
-    ASMLLM_DISPATCH_RU(2, 2, CALL_Q8ACT)
-    ASMLLM_DISPATCH_RU(4, 2, CALL_Q8ACT)
-#undef CALL_Q8ACT
-    return cudaErrorInvalidValue;
-  }
-
-  // fp32 activations: four rows per warp share each lane's x reads.
+  void* args[] = {(void*)&w, (void*)&s, (void*)&act, (void*)&y, (void*)&Mi, (void*)&nbi, (void*)&pf, (void*)&pre};
   const bool q4 = a.fmt == kFmtQ4_0;
-  constexpr int R = 4, U = 2;
-  const int ngroups = (M + R - 1) / R;
   const size_t smem = (size_t)nb * (q4 ? kQ4F32SmemPerBlock : kQ8F32SmemPerBlock);
   if (smem > (size_t)di.smem_optin) return cudaErrorInvalidValue;
+  constexpr int R = 2, U = 2;
+  const int ngroups = (M + R - 1) / R;
+  const size_t gb = (size_t)R * nb * ((q4 ? 16 : 32) + (a.scales_f16 ? 2 : 4));
   if (q4) {
-    return a.scales_f16 ? launch_persistent(q4f32_matvec_kernel<R, U, true>, ngroups, smem, stream, dev, args6)
-                        : launch_persistent(q4f32_matvec_kernel<R, U, false>, ngroups, smem, stream, dev, args6);
+    return a.scales_f16 ? launch_persistent(f32act_matvec_kernel<kFmtQ4_0, R, U, true>, ngroups, smem, stream, dev, args, &pf, gb)
+                        : launch_persistent(f32act_matvec_kernel<kFmtQ4_0, R, U, false>, ngroups, smem, stream, dev, args, &pf, gb);
   }
-  return a.scales_f16 ? launch_persistent(q8f32_matvec_kernel<R, U, true>, ngroups, smem, stream, dev, args6)
-                      : launch_persistent(q8f32_matvec_kernel<R, U, false>, ngroups, smem, stream, dev, args6);
+  return a.scales_f16 ? launch_persistent(f32act_matvec_kernel<kFmtQ8_0, R, U, true>, ngroups, smem, stream, dev, args, &pf, gb)
+                      : launch_persistent(f32act_matvec_kernel<kFmtQ8_0, R, U, false>, ngroups, smem, stream, dev, args, &pf, gb);
+}
+
+cudaError_t launch_act_image(const float* x, void* image, long long nrows, int64_t K, cudaStream_t stream,
+                             const void* pf_w, size_t pf_w_bytes, const void* pf_s, size_t pf_s_bytes) {
+  if (nrows <= 0 || K <= 0) return cudaSuccess;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const DevInfo& di = dev_info(dev);
+  int nb = (int)(K / QK);
+  const long long total = nrows * nb;
+  long long grid = (total + 4 * kWarps - 1) / (4 * kWarps);
+  const long long cap = (long long)di.sms * 8;
+  if (grid > cap) grid = cap;
+  unsigned char* img = static_cast<unsigned char*>(image);
+  long long stride = (long long)act_image_bytes(nb);
+  // Prefetch at most ASMLLM_IMG_PF_MB (default 32) MB of the following matvec's weights,
+  // in proportion between the weight and scale planes; 16-byte aligned starts only.
+  const size_t pf_cap = (size_t)g_img_pf_mb << 20;
+  const size_t tot = pf_w_bytes + pf_s_bytes;
+  if (tot > pf_cap && tot > 0) {
+    pf_w_bytes = (size_t)((double)pf_w_bytes * pf_cap / tot);
+    pf_s_bytes = (size_t)((double)pf_s_bytes * pf_cap / tot);
+  }
+  const unsigned char* pw = ((uintptr_t)pf_w % 16 == 0) ? static_cast<const unsigned char*>(pf_w) : nullptr;
+  const unsigned char* ps = ((uintptr_t)pf_s % 16 == 0) ? static_cast<const unsigned char*>(pf_s) : nullptr;
+  unsigned long long bw = pw ? pf_w_bytes : 0, bs = ps ? pf_s_bytes : 0;
+  void* args[] = {(void*)&x, (void*)&img, (void*)&nb, (void*)&nrows, (void*)&stride,
+                  (void*)&pw, (void*)&bw, (void*)&ps, (void*)&bs};
+  return launch_pdl((const void*)act_image_kernel, dim3((unsigned)grid), dim3(kThreads), 0, stream, args);
 }
 
 cudaError_t launch_quantize(const float* x, int8_t* xq, float* xd, long long nblocks,
@@ -647,11 +733,11 @@ cudaError_t launch_quantize(const float* x, int8_t* xq, float* xd, long long nbl
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const DevInfo& di = dev_info(dev);
-  long long grid = (nblocks + kWarps - 1) / kWarps;
+  long long grid = (nblocks + 4 * kWarps - 1) / (4 * kWarps);
   const long long cap = (long long)di.sms * 8;
   if (grid > cap) grid = cap;
-  quantize_q8_0_kernel<<<(unsigned)grid, kThreads, 0, stream>>>(x, xq, xd, nblocks);
-  return cudaGetLastError();
+  void* args[] = {(void*)&x, (void*)&xq, (void*)&xd, (void*)&nblocks};
+  return launch_pdl((const void*)quantize_q8_0_kernel, dim3((unsigned)grid), dim3(kThreads), 0, stream, args);
 }
 
 cudaError_t launch_gguf_split(int fmt, const uint8_t* raw, uint8_t* qs, void* scales, int f16,

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace asmllm {
 
 // GGUF tensor type ids of the two weight formats.
@@ -16,17 +18,47 @@ struct MatvecArgs {
   bool scales_f16 = false;  // scale plane dtype
   const void* w = nullptr;  // device: Q4_0 [M][K/32][16] or Q8_0 [M][K/32][32]
   const void* scales = nullptr;
-  const float* x = nullptr;
+  const float* x = nullptr;     // fp32 activation (used when image is null)
+  const void* image = nullptr;  // Q8_0 activation image from launch_act_image (Q8_0 families)
   float* y = nullptr;
   int32_t* isums = nullptr;  // optional: per-(row, block) int32 sums (Q8_0 activations only)
+  // The weights are not written by the kernel that precedes this launch in the
+  // stream, so the kernel may start reading them before that kernel completes.
+  bool weights_static = false;
+  // Use the register-streaming (LDG) kernel even where the bulk-copy one applies.
+  bool isums_force_ldg = false;
   int64_t M = 0, K = 0;
 };
 
+// Bytes of one row of the Q8_0 activation image for nb = K/32 blocks:
+// nb 48-byte slots (32 int8 + 16 pad) then nb (d, qsum) float pairs, rounded to 16.
+__host__ __device__ inline size_t act_image_bytes(int64_t nb) {
+  return ((size_t)nb * 56 + 15) & ~(size_t)15;
+}
+
 cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream);
+// pf_w / pf_s: optional weight and scale planes of the matvec that will read
+// this image; their first bytes are prefetched into L2 while the kernel waits
+// for its predecessor (pass nullptr / 0 for none).
+cudaError_t launch_act_image(const float* x, void* image, long long nrows, int64_t K,
+                             cudaStream_t stream, const void* pf_w = nullptr, size_t pf_w_bytes = 0,
+                             const void* pf_s = nullptr, size_t pf_s_bytes = 0);
 cudaError_t launch_quantize(const float* x, int8_t* xq, float* xd, long long nblocks,
                             cudaStream_t stream);
 cudaError_t launch_gguf_split(int fmt, const uint8_t* raw, uint8_t* qs, void* scales, int f16,
                               long long nblocks, cudaStream_t stream);
 int64_t max_k(int fmt, bool fp32_act, int dev);
+
+// Bulk-copy (TMA) pipeline kernel for the Q8_0-activation families
+// (tma_matvec.cu); launch_matvec uses it when the shape allows.
+bool tma_matvec_supported(const MatvecArgs& a, int smem_optin);
+cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl);
+// Reads (and optionally clears) the device error word the kernels set when a
+// bounded wait gives up (bit 0: a shared-memory ring barrier timed out).
+cudaError_t read_device_error(unsigned* out, bool clear);
+cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream);
+
+extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
+extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch
 
 }  // namespace asmllm

@@ -1,0 +1,477 @@
+// asmllm_b200/csrc/tma_matvec.cu -- Q4_0/Q8_0 x Q8_0 matvec streamed by the
+// bulk-copy (TMA) engine through a shared-memory ring (sm_100a).
+//
+// Same semantics as q8act_matvec_kernel in matvec.cu (reference
+// THRISHAL12345/asmllm src/kernels/arm64/matmul_q4_neon.S:38-317): the
+// activation is quantized to Q8_0 bit-exactly, each (row, block) int32 dot is
+// exact, and y[r] = sum_b fma(float(isum), wd*xd) differs from the reference
+// only in fp32 summation order.
+//
+// Structure of one CTA (persistent, one per SM by default, ~110 KB of shared
+// memory so the NEXT matvec's CTA fits beside it):
+//   * The CTA owns a contiguous range of rows, cut into stages of R whole rows
+//     (R in {8,4,2,1}, ~16 KB of weights).  Rows are contiguous in memory, so
+//     a stage is exactly two cp.async.bulk copies: the R rows' weights and
+//     their scales.
+//   * 1 producer warp: one lane issues the stages into per-warpgroup rings of
+//     shared-memory slots (full/empty mbarriers, expect_tx).  Weights do not
+//     depend on the previous kernel, so when the caller declares them static
+//     the producer starts before griddepcontrol.wait: under programmatic
+//     dependent launch the rings fill while the previous matvec still runs.
+//   * NWG warpgroups of 8 consumer warps own alternate stages.  After
+//     griddepcontrol.wait they build the Q8_0 activation image in shared
+//     memory (quantizing x, 8 lanes per block, or copying a prepared image).
+//     Per stage, 8/R warps share a row: each takes a strided subset of its
+//     16-byte units, reduces across lanes, and (when R < 8) the row's partials
+//     are summed in fixed order through shared memory -- y is deterministic.
+//   * Every mbarrier wait is bounded (about a second of clock cycles); on
+//     timeout the kernel sets bit 0 of g_device_error, stops, lets the copies
+//     it issued land, and returns.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "common.cuh"
+#include "matvec.cuh"
+
+namespace asmllm {
+
+__device__ unsigned int g_device_error;
+
+namespace {
+
+constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200 SM clock
+constexpr int kBarBytes = 256;                   // room for 2 x 8 mbarriers + abort flag
+constexpr int kPartBytes = 2 * 2 * 8 * 4;        // row partials [2 stage parities][2 warpgroups][8]
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity; false after kWaitCycles.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void consumer_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Barrier over the 256 threads of warpgroup wg (named barrier 2 + wg) that
+// also ORs a flag across them: every warp gets the same answer.
+__device__ __forceinline__ bool wg_bar_or(int wg, bool v) {
+  unsigned r;
+  if (wg == 0)
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, 2, 256, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((unsigned)v)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, 3, 256, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(r)
+        : "r"((unsigned)v)
+        : "memory");
+  return r != 0;
+}
+
+}  // namespace
+
+template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG>
+__global__ void __launch_bounds__((NWG * 8 + 1) * 32, 2)
+tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales,
+                  const void* __restrict__ act, float* __restrict__ y, int M, int nb,
+                  int32_t* __restrict__ isums, int R, int NS, int pre) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;  // weight bytes per block
+  constexpr int SS = F16S ? 2 : 4;               // scale bytes per block
+  constexpr int UPB = FMT == kFmtQ4_0 ? 1 : 2;   // 16-byte units per block
+  constexpr int NCW = NWG * 8;                   // consumer warps
+  constexpr int NCT = NCW * 32;                  // consumer threads
+
+  // Shared layout: [barriers + abort flag | row partials | activation image | ring]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // full[0..NS), empty[NS..2NS)
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kBarBytes - 4);
+  float* part = reinterpret_cast<float*>(smem + kBarBytes);  // [2][NWG][8] partial row sums
+  unsigned char* img = smem + kBarBytes + kPartBytes;
+  const size_t img_bytes = (act_image_bytes(nb) + 127) & ~(size_t)127;
+  unsigned char* stages = img + img_bytes;
+  const size_t row_w = (size_t)nb * UB, row_s = (size_t)nb * SS;
+  const size_t stage_bytes = (size_t)R * (row_w + row_s);  // R whole rows, then their scales
+  const int WPR = 8 / R;                                   // warps per row
+  const int NU = nb * UPB;                                 // units per row
+  const int NSW = NS / NWG;                                // ring slots per warpgroup
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = (int)((long long)M * blockIdx.x / gridDim.x);
+  const int r1 = (int)((long long)M * (blockIdx.x + 1) / gridDim.x);
+  const int S = (r1 - r0 + R - 1) / R;  // stages; stage s owned by warpgroup s % NWG
+
+  pdl_trigger();
+  if (S == 0) return;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSW * NWG; ++i) {
+      mbar_init(smem_u32(&bars[i]), 1);       // full: producer arrive + tx bytes
+      mbar_init(smem_u32(&bars[NS + i]), 8);  // empty: the 8 warps of the owning warpgroup
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ producer
+  if (warp == NCW) {
+    if (lane == 0) {
+      if (!pre) pdl_wait();  // weights may be written by the previous kernel
+      int s = 0;
+      for (; s < S && !*s_abort; ++s) {
+        const int g = s % NWG, k = s / NWG;  // k-th stage of warpgroup g
+        const int slot = g * NSW + k % NSW, round = k / NSW;
+        if (round > 0 && !mbar_wait_bounded(smem_u32(&bars[NS + slot]), (round - 1) & 1)) {
+          atomicOr(&g_device_error, 1u);
+          *s_abort = 1;
+          break;
+        }
+        const int row0 = r0 + s * R;
+        const int nrows = min(R, r1 - row0);
+        const uint32_t full = smem_u32(&bars[slot]);
+        mbar_arrive_expect_tx(full, (uint32_t)((size_t)nrows * (row_w + row_s)));
+        const uint32_t st = smem_u32(stages + (size_t)slot * stage_bytes);
+        bulk_g2s(st, w + (size_t)row0 * row_w, (uint32_t)((size_t)nrows * row_w), full);
+        bulk_g2s(st + (uint32_t)((size_t)R * row_w), static_cast<const unsigned char*>(scales) + (size_t)row0 * row_s,
+                 (uint32_t)((size_t)nrows * row_s), full);
+      }
+      if (*s_abort) {  // let the copies already issued land before the CTA exits
+        for (int t = (s > NS ? s - NS : 0); t < s; ++t) {
+          const int g = t % NWG, k = t / NWG;
+          mbar_wait_bounded(smem_u32(&bars[g * NSW + k % NSW]), (k / NSW) & 1);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------ consumers
+  const int wg = warp >> 3, wi = warp & 7;
+  const int rr = wi / WPR, sg = wi - rr * WPR;  // this warp's row in a stage and its segment
+  pdl_wait();  // x / the image may come from the previous kernel; y may still be in use
+  if (FUSED) {
+    const float* x = static_cast<const float*>(act);
+    const int lane8 = threadIdx.x & 7;
+    constexpr int BPP = NCT / 8;  // blocks per pass
+    for (int base = 0; base < nb; base += 4 * BPP) {
+      float4 v[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {  // issue the loads of 4 passes before any use
+        const int b = base + p * BPP + (threadIdx.x >> 3);
+        v[p] = b < nb ? reinterpret_cast<const float4*>(x + (size_t)b * QK)[lane8] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int b = base + p * BPP + (threadIdx.x >> 3);
+        if (base + p * BPP >= nb) break;  // uniform across the consumers
+        float d;
+        int qsum;
+        const unsigned q = quantize_quad(v[p], d, qsum);
+        if (b < nb) {
+          reinterpret_cast<unsigned*>(img + b * 48)[lane8] = q;
+          if (lane8 == 0) reinterpret_cast<float2*>(img + (size_t)nb * 48)[b] = make_float2(d, __int_as_float(qsum));
+        }
+      }
+    }
+  } else {
+    const unsigned char* src = static_cast<const unsigned char*>(act);
+    const int n16 = (int)(act_image_bytes(nb) / 16);
+    for (int i = threadIdx.x; i < n16; i += NCT) cp_async16(img + 16 * i, src + 16 * i);
+    cp_async_wait_all();
+  }
+  consumer_bar_sync(NCT);
+
+  const float2* sdq = reinterpret_cast<const float2*>(img + (size_t)nb * 48);
+  for (int s = wg, k = 0; s < S; s += NWG, ++k) {
+    const int slot = wg * NSW + k % NSW;
+    const bool ok = mbar_wait_bounded(smem_u32(&bars[slot]), (k / NSW) & 1);
+    if (!ok) atomicOr(&g_device_error, 1u);
+    const int row0 = r0 + s * R;
+    const int nrows = min(R, r1 - row0);
+    const unsigned char* st = stages + (size_t)slot * stage_bytes;
+    float acc = 0.0f;
+    if (ok && rr < nrows) {
+      const unsigned char* wrow = st + (size_t)rr * row_w;
+      const unsigned char* srow = st + (size_t)R * row_w + (size_t)rr * row_s;
+      const int row = row0 + rr;
+      if (FMT == kFmtQ4_0) {
+#pragma unroll 4
+        for (int b = sg * 32 + lane; b < nb; b += 32 * WPR) {
+          const uint4 q = *reinterpret_cast<const uint4*>(wrow + b * 16);
+          const float sc = F16S ? __half2float(*reinterpret_cast<const __half*>(srow + b * 2))
+                                : *reinterpret_cast<const float*>(srow + b * 4);
+          const uint4* xp = reinterpret_cast<const uint4*>(img + b * 48);
+          const uint4 xa = xp[0], xb = xp[1];
+          const float2 dq = sdq[b];
+          int lo = 0, hi = 0;
+          lo = dp4a_us(q.x & 0x0F0F0F0Fu, (int)xa.x, lo);
+          hi = dp4a_us(q.x & 0xF0F0F0F0u, (int)xb.x, hi);
+          lo = dp4a_us(q.y & 0x0F0F0F0Fu, (int)xa.y, lo);
+          hi = dp4a_us(q.y & 0xF0F0F0F0u, (int)xb.y, hi);
+          lo = dp4a_us(q.z & 0x0F0F0F0Fu, (int)xa.z, lo);
+          hi = dp4a_us(q.z & 0xF0F0F0F0u, (int)xb.z, hi);
+          lo = dp4a_us(q.w & 0x0F0F0F0Fu, (int)xa.w, lo);
+          hi = dp4a_us(q.w & 0xF0F0F0F0u, (int)xb.w, hi);
+          const int isum = lo + (hi >> 4) - __float_as_int(dq.y) * 8;
+          if (DBG) isums[(size_t)row * nb + b] = isum;
+          acc = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, dq.x), acc);
+        }
+      } else {
+#pragma unroll 4
+        for (int u0 = sg * 32; u0 < NU; u0 += 32 * WPR) {
+          const int u = u0 + lane;
+          const bool valid = u < NU;  // same for both lanes of a pair
+          const int b = u >> 1;
+          uint4 q = make_uint4(0u, 0u, 0u, 0u), xa = make_uint4(0u, 0u, 0u, 0u);
+          float sc = 0.0f, xd = 0.0f;
+          if (valid) {
+            q = *reinterpret_cast<const uint4*>(wrow + u * 16);
+            xa = *reinterpret_cast<const uint4*>(img + b * 48 + (u & 1) * 16);
+            sc = F16S ? __half2float(*reinterpret_cast<const __half*>(srow + b * 2))
+                      : *reinterpret_cast<const float*>(srow + b * 4);
+            xd = sdq[b].x;
+          }
+          int p = 0;
+          p = dp4a_ss((int)q.x, (int)xa.x, p);
+          p = dp4a_ss((int)q.y, (int)xa.y, p);
+          p = dp4a_ss((int)q.z, (int)xa.z, p);
+          p = dp4a_ss((int)q.w, (int)xa.w, p);
+          const int isum = p + __shfl_xor_sync(kFull, p, 1);
+          if (valid && !(lane & 1)) {
+            if (DBG) isums[(size_t)row * nb + b] = isum;
+            acc = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, xd), acc);
+          }
+        }
+      }
+      acc = warp_sum(acc);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&bars[NS + slot]));  // this warp is done with the slot
+    // Rows split over WPR warps: partials through shared memory, summed in
+    // segment order (deterministic); double-buffered by stage parity.
+    float* pb = part + ((k & 1) * NWG + wg) * 8;
+    if (WPR == 1) {
+      if (ok && rr < nrows && lane == 0) y[row0 + rr] = acc;
+    } else if (lane == 0) {
+      pb[wi] = acc;
+    }
+    // One decision per warpgroup: stop together if any warp timed out or the
+    // producer gave up (no warp can be left waiting at this barrier).
+    const bool stop = wg_bar_or(wg, !ok || *s_abort);
+    if (stop) {
+      *s_abort = 1;
+      break;
+    }
+    if (WPR > 1 && sg == 0 && rr < nrows && lane == 0) {
+      float v = pb[rr * WPR];
+      for (int t = 1; t < WPR; ++t) v += pb[rr * WPR + t];
+      y[row0 + rr] = v;
+    }
+  }
+}
+
+// ==========================================================================
+// Host side
+// ==========================================================================
+namespace {
+
+std::mutex g_tma_mu;
+std::map<std::tuple<const void*, int>, bool> g_tma_attr;  // (kernel, device) -> smem opt-in done
+
+int env_int2(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : dflt;
+}
+const int g_tma_ctas = env_int2("ASMLLM_TMA_CTAS_PER_SM", 1);
+const int g_tma_smem_kb = env_int2("ASMLLM_TMA_SMEM_KB", 110);
+const int g_tma_nwg = env_int2("ASMLLM_TMA_NWG", 2);
+const int g_tma_carveout = env_int2("ASMLLM_TMA_CARVEOUT", 100);  // percent of the unified L1/shared
+
+struct TmaPlan {
+  int R = 0, NS = 0;
+  size_t smem = 0;
+};
+
+// Stage = R whole consecutive rows (contiguous in memory: one bulk copy for
+// their weights and one for their scales), R in {8, 4, 2, 1}, the largest
+// whose weights fit in the stage target (16 KB); rows above 24 KB are left
+// to the register-streaming kernel.
+bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
+  const int ub = fmt == kFmtQ4_0 ? 16 : 32, ss = f16s ? 2 : 4;
+  if (nb % (f16s ? 8 : 4) != 0) return false;  // 16-byte aligned scale rows
+  const size_t row_w = (size_t)nb * ub, row_s = (size_t)nb * ss;
+  if (row_w > 24 * 1024) return false;
+  int R = 8;
+  while (R > 1 && (size_t)R * row_w > 16 * 1024) R /= 2;
+  const size_t stage = (size_t)R * (row_w + row_s);
+  const size_t img = (act_image_bytes(nb) + 127) & ~(size_t)127;
+  size_t budget = (size_t)g_tma_smem_kb * 1024;
+  if (budget > (size_t)smem_optin) budget = smem_optin;
+  const size_t fixed = kBarBytes + kPartBytes + img;
+  if (budget < fixed) return false;
+  size_t ns = (budget - fixed) / stage;
+  if (ns > 8) ns = 8;
+  const size_t nwg = g_tma_nwg == 1 ? 1 : 2;
+  ns -= ns % nwg;  // equal rings per warpgroup
+  if (ns < 2 * nwg) return false;
+  p->R = R;
+  p->NS = (int)ns;
+  p->smem = fixed + ns * stage;
+  return true;
+}
+
+template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG>
+cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, FUSED, NWG>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(g_tma_mu);
+    auto key = std::make_tuple((const void*)kernel, dev);
+    if (!g_tma_attr[key]) {
+      int optin = 0;
+      cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+      if (e != cudaSuccess) return e;
+      // Full shared-memory carveout: room for the next matvec's CTA beside this one.
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, g_tma_carveout);
+      if (e != cudaSuccess) return e;
+      g_tma_attr[key] = true;
+    }
+  }
+  const void* w = a.w;
+  const void* s = a.scales;
+  const void* act = a.image ? a.image : (const void*)a.x;
+  float* y = a.y;
+  int M = (int)a.M, nb = (int)(a.K / QK);
+  int32_t* isums = a.isums;
+  int R = p.R, NS = p.NS, pre = a.weights_static ? 1 : 0;
+  void* args[] = {(void*)&w, (void*)&s, (void*)&act, (void*)&y, (void*)&M, (void*)&nb,
+                  (void*)&isums, (void*)&R, (void*)&NS, (void*)&pre};
+  long long grid = (long long)sms * (g_tma_ctas > 0 ? g_tma_ctas : 1);
+  const long long groups = (M + R - 1) / R;
+  if (grid > groups) grid = groups;
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3((NWG * 8 + 1) * 32);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, (const void*)kernel, args);
+}
+
+template <int FMT, int NWG>
+cudaError_t launch_tma_fmt(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+  const bool fused = a.image == nullptr;
+  if (a.isums) {
+    return fused ? launch_tma_t<FMT, false, true, true, NWG>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, false, true, false, NWG>(a, p, sms, stream, pdl);
+  }
+  if (a.scales_f16) {
+    return fused ? launch_tma_t<FMT, true, false, true, NWG>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, true, false, false, NWG>(a, p, sms, stream, pdl);
+  }
+  return fused ? launch_tma_t<FMT, false, false, true, NWG>(a, p, sms, stream, pdl)
+               : launch_tma_t<FMT, false, false, false, NWG>(a, p, sms, stream, pdl);
+}
+
+}  // namespace
+
+bool tma_matvec_supported(const MatvecArgs& a, int smem_optin) {
+  if (a.fp32_act || a.M <= 0 || a.K <= 0) return false;
+  TmaPlan p;
+  return tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, &p);
+}
+
+cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl) {
+  TmaPlan p;
+  if (!tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, &p)) return cudaErrorInvalidValue;
+  if (a.fmt == kFmtQ4_0)
+    return g_tma_nwg == 1 ? launch_tma_fmt<kFmtQ4_0, 1>(a, p, sms, stream, pdl)
+                          : launch_tma_fmt<kFmtQ4_0, 2>(a, p, sms, stream, pdl);
+  return g_tma_nwg == 1 ? launch_tma_fmt<kFmtQ8_0, 1>(a, p, sms, stream, pdl)
+                        : launch_tma_fmt<kFmtQ8_0, 2>(a, p, sms, stream, pdl);
+}
+
+cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream) {
+  return cudaMemcpyFromSymbolAsync(host_pinned, g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost,
+                                   stream);
+}
+
+cudaError_t read_device_error(unsigned* out, bool clear) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_device_error, sizeof(unsigned));
+  if (e == cudaSuccess && clear && *out) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(unsigned));
+  }
+  return e;
+}
+
+}  // namespace asmllm

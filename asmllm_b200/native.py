@@ -52,6 +52,14 @@ SIGNATURES = {
     "asm_quantize_q8_0_async": ([vp, vp, vp, i64, i64, vp], c_int),
     "asm_block_sums_async": ([c_int, vp, vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_gguf_split_async": ([c_int, vp, vp, vp, c_int, i64, vp], c_int),
+    "asm_act_image_bytes": ([i64], i64),
+    "asm_act_image_q8_0_async": ([vp, vp, i64, i64, vp], c_int),
+    "asm_matmul_image_async": ([c_int, vp, vp, c_int, vp, vp, i64, i64, vp], c_int),
+    "asm_act_image_q8_0_prefetch_async": ([vp, vp, i64, i64, vp, i64, vp, i64, vp], c_int),
+    "asm_weights_mark_static": ([vp, i64], c_int),
+    "asm_weights_unmark_static": ([vp], c_int),
+    "asm_device_error": ([ctypes.POINTER(ctypes.c_uint)], c_int),
+    "asm_set_option": ([ctypes.c_char_p, c_int], c_int),
     "asm_max_k": ([c_int, c_int], i64),
     "asm_version": ([], ctypes.c_char_p),
 }

@@ -191,6 +191,84 @@ def matvec(fmt: int, qweights, scales, x, out=None, *, fp32_activations=False, s
     return out
 
 
+def mark_static(*tensors) -> None:
+    """Declares device tensors (model weights) static: see asm_weights_mark_static."""
+    L = native.lib()
+    for t in tensors:
+        native.check(L.asm_weights_mark_static(_ptr(t), t.numel() * t.element_size()))
+
+
+def unmark_static(*tensors) -> None:
+    L = native.lib()
+    for t in tensors:
+        native.check(L.asm_weights_unmark_static(_ptr(t)))
+
+
+def set_option(name: str, value: int) -> int:
+    """asm_set_option: "tma" / "pdl" kernel-path switches; returns the previous value."""
+    prev = int(native.lib().asm_set_option(name.encode(), int(value)))
+    if prev < 0:
+        native.check()
+    return prev
+
+
+def device_error() -> int:
+    """Reads and clears the device error word (0 = no kernel gave up a bounded wait)."""
+    v = ctypes.c_uint(0)
+    native.check(native.lib().asm_device_error(ctypes.byref(v)))
+    return int(v.value)
+
+
+def act_image_bytes(K: int) -> int:
+    """Bytes of one row of the Q8_0 activation image (asm_act_image_bytes)."""
+    n = int(native.lib().asm_act_image_bytes(int(K)))
+    if n < 0:
+        raise ValueError(f"K={K} is not a multiple of 32")
+    return n
+
+
+def act_image_dev(x, out=None, stream=None, prefetch=None):
+    """Quantizes x fp32 [K] or [N, K] once into the activation image (uint8 [N, bytes]).
+
+    prefetch: optional (qweights, scales) of the matvec that will read the
+    image; their first bytes are streamed into L2 while the quantize waits for
+    the previous kernel (a performance hint; results are unchanged)."""
+    torch = _torch()
+    _check_dev(x, (torch.float32,), "x")
+    K = x.shape[-1]
+    N = x.numel() // K if K else 0
+    nbytes = act_image_bytes(K)
+    if out is None:
+        out = torch.empty((max(N, 1), nbytes), dtype=torch.uint8, device=x.device)
+    L = native.lib()
+    if prefetch is None:
+        rc = L.asm_act_image_q8_0_async(_ptr(x), _ptr(out), N, K, _stream_handle(stream))
+    else:
+        w, s = prefetch
+        rc = L.asm_act_image_q8_0_prefetch_async(_ptr(x), _ptr(out), N, K, _ptr(w), w.numel() * w.element_size(),
+                                                 _ptr(s), s.numel() * s.element_size(), _stream_handle(stream))
+    native.check(rc)
+    return out
+
+
+def matvec_image(fmt: int, qweights, scales, image, K: int, out=None, stream=None):
+    """y = W x with x given as a prepared activation image (see act_image_dev)."""
+    torch = _torch()
+    wdt = torch.uint8 if fmt == FMT_Q4_0 else torch.int8
+    _check_dev(qweights, (wdt,), "qweights")
+    _check_dev(scales, (torch.float32, torch.float16), "scales")
+    _check_dev(image, (torch.uint8,), "image")
+    M = scales.shape[0]
+    if image.numel() < act_image_bytes(K):
+        raise ValueError("image too small for K")
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=image.device)
+    rc = native.lib().asm_matmul_image_async(fmt, _ptr(qweights), _ptr(scales), 1 if scales.dtype == torch.float16 else 0,
+                                             _ptr(image), _ptr(out), M, K, _stream_handle(stream))
+    native.check(rc)
+    return out
+
+
 def quantize_q8_0_dev(x, xq=None, xd=None, stream=None):
     """Device quantize of x fp32 [N, K] or [K] -> (int8 same shape, fp32 [..., K/32])."""
     torch = _torch()
@@ -243,5 +321,6 @@ __all__ = [
     "matmul_q4", "matmul_q4_mt", "matmul_q4_avx512", "matmul_q4_f32", "matmul_q8", "matmul_q8_mt",
     "matmul_q8q8", "quantize_q8_0", "register_weights", "unregister_weights", "threadpool_init",
     "threadpool_shutdown", "threadpool_get_num_threads", "max_k", "matvec", "quantize_q8_0_dev",
-    "block_sums_dev", "gguf_split_dev",
+    "block_sums_dev", "gguf_split_dev", "act_image_bytes", "act_image_dev", "matvec_image",
+    "mark_static", "unmark_static", "device_error", "set_option",
 ]

@@ -234,6 +234,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true", help="skip per-shape / Q8 breakdown")
+    ap.add_argument("--mode", choices=["image", "fused"], default="image",
+                    help="image: activation-quantize pre-pass kernel + matvec (2 launches per matvec); "
+                         "fused: quantize inside the matvec (1 launch)")
     args = ap.parse_args()
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
 
@@ -271,16 +274,29 @@ def main():
 
     base = 1000 * rank
     W4 = [[make_q4(M, K, base + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+    torch.cuda.synchronize()
+    for row in W4:  # model weights: uploaded once, never rewritten (see asm_weights_mark_static)
+        for qs, d in row:
+            ops.mark_static(qs, d)
     xs = {}
     for K in sorted({K for _, K in SHAPES}):
         gen.manual_seed(base + 500 + K)
         xs[K] = torch.randn(K, device=dev, generator=gen)
     ys = {M: torch.empty(M, device=dev) for M in sorted({M for M, _ in SHAPES})}
+    imgs = {K: torch.empty(ops.act_image_bytes(K), dtype=torch.uint8, device=dev) for K in xs}
     step_bytes = sum(q4_bytes(M, K) for M, K in SHAPES)
+
+    def one_matvec(fmt, qs, d, M, K, mode=args.mode):
+        # Each matvec quantizes its own x (the activation quantize is part of the path).
+        if mode == "fused":
+            ops.matvec(fmt, qs, d, xs[K], out=ys[M])
+        else:
+            ops.act_image_dev(xs[K], out=imgs[K], prefetch=(qs, d))
+            ops.matvec_image(fmt, qs, d, imgs[K], K, out=ys[M])
 
     def step(c, W=W4, fmt=FMT_Q4_0, shapes=SHAPES):
         for (qs, d), (M, K) in zip(W[c], shapes):
-            ops.matvec(fmt, qs, d, xs[K], out=ys[M])
+            one_matvec(fmt, qs, d, M, K)
 
     # warm-up: eager steps (also primes the library's launch caches)
     for i in range(max(3, args.warmup)):
@@ -337,8 +353,10 @@ def main():
         ms = float(t.item())
     total_bytes = step_bytes * K_steps * world
     value = total_bytes / (ms / 1e3) / 1e9
-    launches = len(SHAPES) * K_steps
-    per_launch_ms = ms / launches
+    launches = len(SHAPES) * K_steps * (2 if args.mode == "image" else 1)
+    # The matvec is the dominant kernel; per-launch figures are per matvec
+    # (its quantize pre-pass, when separate, is counted inside the time).
+    per_launch_ms = ms / (len(SHAPES) * K_steps)
     per_launch_bytes = step_bytes / len(SHAPES)
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     del gA, gB
@@ -358,17 +376,30 @@ def main():
             b.synchronize()
             return a.elapsed_time(b) / (5 * n)
 
-        per_shape = {}
-        for i, (M, K) in enumerate(SHAPES):
-            def one(c, i=i, M=M, K=K):
-                qs, d = W4[c][i]
-                ops.matvec(FMT_Q4_0, qs, d, xs[K], out=ys[M])
-            t = time_graph(one, 300)
-            per_shape[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q4_bytes(M, K) / (t / 1e3) / 1e9, 1)}
-        extras["q4q8_per_shape"] = per_shape
+        for mode in ("fused", "image"):
+            per_shape = {}
+            for i, (M, K) in enumerate(SHAPES):
+                def one(c, i=i, M=M, K=K, mode=mode):
+                    qs, d = W4[c][i]
+                    one_matvec(FMT_Q4_0, qs, d, M, K, mode=mode)
+                t = time_graph(one, 300)
+                per_shape[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q4_bytes(M, K) / (t / 1e3) / 1e9, 1)}
+            extras[f"q4q8_per_shape_{mode}"] = per_shape
+        t_sw = time_graph(lambda c: step(c), 60)
+        extras["q4q8_sweep_other_mode"] = {"mode": "fused" if args.mode == "image" else "image"}
+        def step_other(c):
+            for (qs, d), (M, K) in zip(W4[c], SHAPES):
+                one_matvec(FMT_Q4_0, qs, d, M, K, mode="fused" if args.mode == "image" else "image")
+        t_o = time_graph(step_other, 60)
+        extras["q4q8_sweep_other_mode"]["GB/s"] = round(step_bytes / (t_o / 1e3) / 1e9, 1)
+        extras["q4q8_sweep_this_mode_recheck_GB/s"] = round(step_bytes / (t_sw / 1e3) / 1e9, 1)
         # Q8_0 x Q8_0 sweep on the same shapes
         del W4
         W8 = [[make_q8(M, K, base + 70 + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+        torch.cuda.synchronize()
+        for row in W8:
+            for qs, d in row:
+                ops.mark_static(qs, d)
         for i in range(COPIES):
             step(i, W=W8, fmt=FMT_Q8_0)
         t8 = time_graph(lambda c: step(c, W=W8, fmt=FMT_Q8_0), 60)
@@ -378,7 +409,7 @@ def main():
         for i, (M, K) in enumerate(SHAPES):
             def one8(c, i=i, M=M, K=K):
                 qs, d = W8[c][i]
-                ops.matvec(FMT_Q8_0, qs, d, xs[K], out=ys[M])
+                one_matvec(FMT_Q8_0, qs, d, M, K)
             t = time_graph(one8, 300)
             per8[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q8_bytes(M, K) / (t / 1e3) / 1e9, 1)}
         extras["q8q8_per_shape"] = per8
@@ -462,7 +493,9 @@ def main():
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
             "weights_layout": "resident qs[M][K/32][16] + fp16 scales (18 B/block)",
             "l2": f"rotating {COPIES} weight copies, {COPIES * step_bytes / 1e6:.0f} MB working set > 126 MB L2",
-            "launch": "CUDA graph replay of %d steps (%d kernels)" % (G, G * len(SHAPES)),
+            "launch": "CUDA graph replay of %d steps (%d matvecs), PDL between kernels" % (G, G * len(SHAPES)),
+            "quantize": "separate activation-image kernel per matvec" if args.mode == "image"
+                        else "inside each matvec kernel (fused)",
         },
         "roofline": {
             "bound": "hbm",

@@ -174,12 +174,61 @@ ASMLLM_API int asm_block_sums_async(int fmt, const void* qweights, const float* 
                                     const float* x, float* y, int32_t* isums,
                                     int64_t M, int64_t K, void* stream);
 
+/* ---- Q8_0 activation image: quantize once, share across matvecs ------- */
+
+/* Bytes of one row of the activation image for K (a multiple of 32): K/32
+ * slots of 48 bytes (32 int8 + 16 pad) followed by K/32 (d fp32, qsum int32)
+ * pairs, rounded up to 16.  -1 if K is invalid. */
+ASMLLM_API int64_t asm_act_image_bytes(int64_t K);
+/* x fp32 [N][K] -> image [N][asm_act_image_bytes(K)]: the activation quantize of
+ * matmul_q4_neon.S:57-143 (same int8 and d as asm_quantize_q8_0), laid out for
+ * the matvec kernels.  x and image 16-byte aligned device buffers. */
+ASMLLM_API int asm_act_image_q8_0_async(const float* x, void* image, int64_t N, int64_t K,
+                                        void* stream);
+/* The same, and in addition, before it waits for the previous kernel in the
+ * stream, prefetches into L2 the first bytes (up to 32 MB) of next_w / next_s --
+ * meant to be the weight and scale planes of the matvec that will read this
+ * image -- so HBM streaming overlaps the quantize step.  A hint only: results
+ * do not depend on it.  next_w / next_s may be NULL. */
+ASMLLM_API int asm_act_image_q8_0_prefetch_async(const float* x, void* image, int64_t N, int64_t K,
+                                                 const void* next_w, int64_t next_w_bytes,
+                                                 const void* next_s, int64_t next_s_bytes,
+                                                 void* stream);
+/* Matvec on a prepared activation image (fmt 2: Q4_0 x Q8_0, fmt 8: Q8_0 x Q8_0);
+ * scales fp32 or fp16 (scales_are_f16).  Same result as the x entries. */
+ASMLLM_API int asm_matmul_image_async(int fmt, const void* qweights, const void* scales,
+                                      int scales_are_f16, const void* image, float* y, int64_t M,
+                                      int64_t K, void* stream);
+
 /* GGUF block split (reference generate.py:91-119): raw GGUF Q4_0 blocks
  * (18 bytes: fp16 d + 16 nibble bytes) or Q8_0 blocks (34 bytes: fp16 d +
  * 32 int8) for `nblocks` blocks -> qs plane (16 or 32 bytes per block) and a
  * scale plane, fp32 (scales_are_f16 = 0) or fp16 (= 1). */
 ASMLLM_API int asm_gguf_split_async(int fmt, const uint8_t* raw, uint8_t* qs, void* scales,
                                     int scales_are_f16, int64_t nblocks, void* stream);
+
+/* Declares the device range [ptr, ptr+bytes) static: the caller guarantees
+ * that no kernel immediately preceding a matvec in its stream writes it (model
+ * weights uploaded once).  Matvecs whose weights and scales lie in static
+ * ranges start streaming them before the previous kernel in the stream has
+ * finished (programmatic dependent launch); others wait first.  Unmark before
+ * rewriting the buffer from a kernel.  Host-registered weights
+ * (asm_weights_register) are static automatically. */
+ASMLLM_API int asm_weights_mark_static(const void* ptr, int64_t bytes);
+ASMLLM_API int asm_weights_unmark_static(const void* ptr);
+
+/* Reads and clears the device error word: bit 0 = a kernel's bounded wait on
+ * its shared-memory pipeline timed out (the call's output is not valid).
+ * Synchronous entries check it themselves; callers of *_async entries can
+ * call this after synchronizing. */
+ASMLLM_API int asm_device_error(unsigned* flags);
+
+/* Kernel-path switches for testing and tuning; returns the previous value
+ * (-1 for an unknown name).  "tma": 1 = Q8_0-activation matvecs use the
+ * bulk-copy pipeline kernel where the shape allows (default), 0 = the
+ * register-streaming kernels.  "pdl": programmatic dependent launch on/off.
+ * Results are identical either way up to fp32 summation order. */
+ASMLLM_API int asm_set_option(const char* name, int value);
 
 /* Largest K each matvec family supports (shared-memory staging of x). */
 ASMLLM_API int64_t asm_max_k(int fmt, int fp32_activations);

@@ -19,6 +19,15 @@ from conftest import YTOL, rel_err
 
 pytestmark = pytest.mark.gpu
 
+
+@pytest.fixture(params=["tma", "ldg"])
+def kernel_path(request, cuda):
+    """Runs a test on the bulk-copy pipeline kernel and on the register-streaming one."""
+    prev = ops.set_option("tma", 1 if request.param == "tma" else 0)
+    yield request.param
+    ops.set_option("tma", prev)
+    assert ops.device_error() == 0
+
 SHAPES_SMALL = [(1, 32), (5, 64), (7, 96), (33, 4096), (129, 4096), (257, 1024), (1000, 11008)]
 SHAPES_7B = list(synth.SHAPES_7B.values())
 
@@ -107,13 +116,55 @@ def test_quantize_random_bulk(cuda, oracle):
     assert_quant_equal(xq.cpu().numpy(), xd.cpu().numpy(), rq, rd)
 
 
+def split_image(img, K):
+    """(xq int8 [K], d fp32 [K/32], qsum int32 [K/32]) from one activation image row."""
+    nb = K // 32
+    raw = np.asarray(img, dtype=np.uint8).reshape(-1)
+    xq = raw[: nb * 48].reshape(nb, 48)[:, :32].reshape(-1).view(np.int8)
+    pairs = raw[nb * 48: nb * 56].view(np.uint32).reshape(nb, 2)
+    return xq, pairs[:, 0].copy().view(np.float32), pairs[:, 1].copy().view(np.int32)
+
+
+@pytest.mark.parametrize("K", [32, 64, 96, 4096, 11008, 28672])
+def test_activation_image_bit_exact(cuda, oracle, K):
+    x = special_x(K)
+    rq, rd = oracle.quantize_q8_0(x)
+    img = ops.act_image_dev(dev(cuda, x)).cpu().numpy()[0]
+    assert img.size == ops.act_image_bytes(K) and img.size % 16 == 0
+    xq, d, qsum = split_image(img, K)
+    assert_quant_equal(xq, d, rq, rd)
+    assert np.array_equal(qsum, oracle.block_qsum(rq))
+
+
+def test_activation_image_batched(cuda, oracle):
+    X = synth.activation(11008, seed=8, n=5)
+    imgs = ops.act_image_dev(dev(cuda, X)).cpu().numpy()
+    for n in range(5):
+        xq, d, _ = split_image(imgs[n], 11008)
+        rq, rd = oracle.quantize_q8_0(X[n])
+        assert_quant_equal(xq, d, rq, rd)
+
+
+@pytest.mark.parametrize("M,K", [(5, 64), (129, 4096), (4096, 11008), (32000, 4096)])
+@pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
+def test_image_path_equals_fused_path(cuda, kernel_path, fmt, M, K):
+    # Same int8 image either way, same kernel arithmetic: identical y.
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=13)
+    x = synth.activation(K, seed=14)
+    dw, ds, dx = dev(cuda, w), dev(cuda, s).half(), dev(cuda, x)
+    y_fused = ops.matvec(fmt, dw, ds, dx)
+    img = ops.act_image_dev(dx)
+    y_img = ops.matvec_image(fmt, dw, ds, img, K)
+    assert cuda.equal(y_fused, y_img)
+
+
 # --------------------------------------------------------------------------
 # Block sums: bit-exact (the matvec kernel's own debug instantiation)
 # --------------------------------------------------------------------------
 
 @pytest.mark.parametrize("M,K", SHAPES_SMALL + [(4096, 4096)])
 @pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
-def test_block_sums_bit_exact(cuda, oracle, fmt, M, K):
+def test_block_sums_bit_exact(cuda, oracle, kernel_path, fmt, M, K):
     w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=M + K)
     x = special_x(K) if K >= 256 else synth.activation(K, seed=2)
     xq, _ = oracle.quantize_q8_0(x)
@@ -134,7 +185,7 @@ def _oracle_y(oracle, fmt, fp32_act, w, s, x):
 
 @pytest.mark.parametrize("M,K", SHAPES_SMALL + SHAPES_7B)
 @pytest.mark.parametrize("fmt,fp32_act", [(FMT_Q4_0, False), (FMT_Q8_0, False), (FMT_Q4_0, True), (FMT_Q8_0, True)])
-def test_matvec_parity(cuda, oracle, fmt, fp32_act, M, K):
+def test_matvec_parity(cuda, oracle, kernel_path, fmt, fp32_act, M, K):
     w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=M * 7 + K)
     x = synth.activation(K, seed=K)
     ref = _oracle_y(oracle, fmt, fp32_act, w, s, x)
@@ -146,8 +197,30 @@ def test_matvec_parity(cuda, oracle, fmt, fp32_act, M, K):
         assert np.array_equal(y16, y)
 
 
+@pytest.mark.parametrize("M,K", [(129, 4096), (4096, 11008), (11008, 4096)])
 @pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
-def test_matvec_edge_activations(cuda, oracle, fmt):
+def test_static_weights_same_result(cuda, kernel_path, fmt, M, K):
+    # Weights declared static are streamed before the previous kernel finishes;
+    # the result must not change.  The preceding kernel here writes x.
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=17)
+    x = synth.activation(K, seed=18)
+    dw, ds, dx = dev(cuda, w), dev(cuda, s).half(), dev(cuda, x)
+    cuda.cuda.synchronize()
+    ref = ops.matvec(fmt, dw, ds, dx).clone()
+    ops.mark_static(dw, ds)
+    try:
+        for _ in range(3):
+            x2 = dx * 1.0  # a kernel right before the matvec (writes the activation)
+            y = ops.matvec(fmt, dw, ds, x2)
+            img = ops.act_image_dev(x2 * 1.0)
+            y2 = ops.matvec_image(fmt, dw, ds, img, K)
+            assert cuda.equal(y, ref) and cuda.equal(y2, ref)
+    finally:
+        ops.unmark_static(dw, ds)
+
+
+@pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
+def test_matvec_edge_activations(cuda, oracle, kernel_path, fmt):
     M, K = 300, 4096
     w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=9)
     x = special_x(K)
@@ -233,7 +306,7 @@ def test_mt_entries_and_threadpool(cuda, golden):
     assert np.array_equal(ops.matmul_q4(q, s, x), ops.matmul_q4_mt(q, s, x, 2))
 
 
-def test_deterministic(cuda):
+def test_deterministic(cuda, kernel_path):
     M, K = 11008, 4096
     w, s = synth.q4_0_weights(M, K)
     x = synth.activation(K)
@@ -254,6 +327,22 @@ def test_async_rejects_host_pointers(cuda):
     rc = native.lib().asm_matmul_q4_async(w.ctypes.data, s.ctypes.data, x.ctypes.data, y.ctypes.data, 8, 64, None)
     assert rc == native.ASM_E_NOT_DEVICE
     native.last_error()
+
+
+def test_misaligned_device_pointers_are_rejected(cuda):
+    M, K = 16, 128
+    dw = cuda.zeros(M * K // 2 + 16, dtype=cuda.uint8, device="cuda")
+    ds = cuda.zeros(M * K // 32, dtype=cuda.float32, device="cuda")
+    dx = cuda.zeros(K + 4, dtype=cuda.float32, device="cuda")
+    dy = cuda.zeros(M, dtype=cuda.float32, device="cuda")
+    L = native.lib()
+    rc = L.asm_matmul_q4_async(dw.data_ptr() + 8, ds.data_ptr(), dx.data_ptr(), dy.data_ptr(), M, K, None)
+    assert rc == native.ASM_E_INVALID and "aligned" in native.last_error()[1]
+    rc = L.asm_matmul_q4_async(dw.data_ptr(), ds.data_ptr(), dx.data_ptr() + 4, dy.data_ptr(), M, K, None)
+    assert rc == native.ASM_E_INVALID and "aligned" in native.last_error()[1]
+    L.asm_matmul_q4(dw.data_ptr(), ds.data_ptr(), dx.data_ptr() + 4, dy.data_ptr(), M, K)
+    assert native.last_error()[0] == native.ASM_E_INVALID
+    cuda.cuda.synchronize()
 
 
 def test_k_beyond_maximum_is_rejected(cuda):

@@ -7,8 +7,8 @@
 // exact, and y[r] = sum_b fma(float(isum), wd*xd) differs from the reference
 // only in fp32 summation order.
 //
-// Structure of one CTA (persistent, one per SM by default, ~110 KB of shared
-// memory so the NEXT matvec's CTA fits beside it):
+// Structure of one CTA (persistent: two per SM by default, ~100 KB of shared
+// memory each):
 //   * The CTA owns a contiguous range of rows, cut into stages of R whole rows
 //     (R in {8,4,2,1}, ~16 KB of weights).  Rows are contiguous in memory, so
 //     a stage is exactly two cp.async.bulk copies: the R rows' weights and
@@ -136,7 +136,7 @@ template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG>
 __global__ void __launch_bounds__((NWG * 8 + 1) * 32, 2)
 tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales,
                   const void* __restrict__ act, float* __restrict__ y, int M, int nb,
-                  int32_t* __restrict__ isums, int R, int NS, int pre) {
+                  int32_t* __restrict__ isums, int R, int NS, int pre, int pf_stages) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;  // weight bytes per block
   constexpr int SS = F16S ? 2 : 4;               // scale bytes per block
@@ -179,8 +179,24 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   if (warp == NCW) {
     if (lane == 0) {
       if (!pre) pdl_wait();  // weights may be written by the previous kernel
+      // Stages beyond the ring go to L2 ahead of time (bulk prefetch: no shared
+      // memory, nothing waits on it), keeping HBM busy while the consumers wait
+      // for the previous kernel and quantize x.
+      int pf_next = NS;
+      const int pf_end = min(S, NS + pf_stages);
+      auto prefetch_stage = [&](int t) {
+        const int row0 = r0 + t * R;
+        const int nrows = min(R, r1 - row0);
+        prefetch_l2_bulk(w + (size_t)row0 * row_w, (unsigned)((size_t)nrows * row_w));
+        prefetch_l2_bulk(static_cast<const unsigned char*>(scales) + (size_t)row0 * row_s,
+                         (unsigned)((size_t)nrows * row_s));
+      };
       int s = 0;
       for (; s < S && !*s_abort; ++s) {
+        if (s == 1)
+          for (; pf_next < pf_end; ++pf_next) prefetch_stage(pf_next);
+        else if (s > 1 && pf_next < S && pf_next < s + NS + pf_stages)
+          prefetch_stage(pf_next++);  // keep the window pf_stages ahead of the ring
         const int g = s % NWG, k = s / NWG;  // k-th stage of warpgroup g
         const int slot = g * NSW + k % NSW, round = k / NSW;
         if (round > 0 && !mbar_wait_bounded(smem_u32(&bars[NS + slot]), (round - 1) & 1)) {
@@ -215,6 +231,9 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     const float* x = static_cast<const float*>(act);
     const int lane8 = threadIdx.x & 7;
     constexpr int BPP = NCT / 8;  // blocks per pass
+    // One L2 round trip for all of x: prefetch every pass's 16 bytes into L1 first.
+    for (int b = threadIdx.x >> 3; b < nb; b += BPP)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(x + (size_t)b * QK + lane8 * 4));
     for (int base = 0; base < nb; base += 4 * BPP) {
       float4 v[4];
 #pragma unroll
@@ -344,10 +363,13 @@ int env_int2(const char* name, int dflt) {
   const char* e = getenv(name);
   return e ? atoi(e) : dflt;
 }
-const int g_tma_ctas = env_int2("ASMLLM_TMA_CTAS_PER_SM", 1);
-const int g_tma_smem_kb = env_int2("ASMLLM_TMA_SMEM_KB", 110);
+// Defaults from measurement on B200 (2 CTAs per SM with ~100 KB each streamed
+// best; deeper single-CTA rings and L2 prefetch windows did not help).
+const int g_tma_ctas = env_int2("ASMLLM_TMA_CTAS_PER_SM", 2);
+const int g_tma_smem_kb = env_int2("ASMLLM_TMA_SMEM_KB", 100);
 const int g_tma_nwg = env_int2("ASMLLM_TMA_NWG", 2);
 const int g_tma_carveout = env_int2("ASMLLM_TMA_CARVEOUT", 100);  // percent of the unified L1/shared
+const int g_tma_pf_kb = env_int2("ASMLLM_TMA_PF_KB", 0);          // L2 prefetch window per CTA (off)
 
 struct TmaPlan {
   int R = 0, NS = 0;
@@ -408,8 +430,10 @@ cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStr
   int M = (int)a.M, nb = (int)(a.K / QK);
   int32_t* isums = a.isums;
   int R = p.R, NS = p.NS, pre = a.weights_static ? 1 : 0;
+  const size_t stage_b = (size_t)R * (size_t)nb * ((FMT == kFmtQ4_0 ? 16 : 32) + (F16S ? 2 : 4));
+  int pf = (int)(((size_t)g_tma_pf_kb * 1024) / stage_b);
   void* args[] = {(void*)&w, (void*)&s, (void*)&act, (void*)&y, (void*)&M, (void*)&nb,
-                  (void*)&isums, (void*)&R, (void*)&NS, (void*)&pre};
+                  (void*)&isums, (void*)&R, (void*)&NS, (void*)&pre, (void*)&pf};
   long long grid = (long long)sms * (g_tma_ctas > 0 ? g_tma_ctas : 1);
   const long long groups = (M + R - 1) / R;
   if (grid > groups) grid = groups;

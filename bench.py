@@ -234,7 +234,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true", help="skip per-shape / Q8 breakdown")
-    ap.add_argument("--mode", choices=["image", "fused"], default="image",
+    ap.add_argument("--mode", choices=["image", "fused"], default="fused",
                     help="image: activation-quantize pre-pass kernel + matvec (2 launches per matvec); "
                          "fused: quantize inside the matvec (1 launch)")
     args = ap.parse_args()

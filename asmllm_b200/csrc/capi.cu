@@ -431,6 +431,21 @@ int async_matvec(const char* name, int fmt, bool fp32_act, bool f16s, const void
   return ASM_OK;
 }
 
+// --------------------------------------------------------------------------
+// Scratch of the allocation-free entry point (asm_matmul_q4_noalloc_async).
+// One activation image of at most kNoAllocMaxK columns: K/32 blocks of 56
+// bytes.  Every device that loads this library holds one copy of it until
+// the process exits.  In host code `g_noalloc_image` is only a stand-in for
+// the symbol: its device address comes from cudaGetSymbolAddress, looked up
+// once per device (with that device current) and kept in g_noalloc_addr.
+// --------------------------------------------------------------------------
+constexpr int64_t kNoAllocMaxK = 32768;
+constexpr size_t kNoAllocImageBytes = (size_t)(kNoAllocMaxK / 32) * 56;  // 57344
+static __device__ __align__(256) unsigned char g_noalloc_image[kNoAllocImageBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDev];
+
 }  // namespace
 
 // ==========================================================================
@@ -845,6 +860,73 @@ ASMLLM_API int asm_device_error(unsigned* flags) {
   cudaError_t e = read_device_error(&v, true);
   if (e != cudaSuccess) return cuda_error(e, "asm_device_error");
   if (flags) *flags = v;
+  return ASM_OK;
+}
+
+// Q4_0 x Q8_0 matvec for callers that must not allocate device memory during
+// the call (a capture under a fixed memory plan, a serving loop with a fixed
+// budget, a plugin whose host owns all allocations).  It runs the same two
+// kernels as the synchronous path -- the activation-quantize pre-pass into an
+// image, then the matvec reading the image -- with the image in the
+// library's fixed device array instead of an allocated buffer.  It calls no
+// cudaMalloc / cudaFree / allocating routine.  The first call on a device
+// looks the array's address up (cudaGetSymbolAddress) and sets up the kernel
+// attributes; make that first call before any stream capture.  All calls
+// share the one array, so calls that overlap on the GPU (different streams or
+// parallel graph branches) race; calls on one stream are ordered.  The array
+// keeps the previous call's contents; nothing in it needs clearing, since
+// each call rewrites every byte of it that the matvec uses.
+ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* scales,
+                                           int scales_are_f16, const float* x, float* y, int64_t M,
+                                           int64_t K, void* stream) {
+  const char* name = "asm_matmul_q4_noalloc_async";
+  int rc = validate(name, qweights, scales, x, y, M, K);
+  if (rc) return rc;
+  if (K > kNoAllocMaxK)
+    return set_error(ASM_E_UNSUPPORTED, "%s: K=%lld exceeds %lld, the size of this entry's fixed scratch", name,
+                     (long long)K, (long long)kNoAllocMaxK);
+  if (M == 0) return ASM_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDev) return set_error(ASM_E_UNSUPPORTED, "%s: device %d out of range", name, dev);
+  if ((rc = require_device(name, y, "y"))) return rc;
+  if (K > 0) {
+    if ((rc = require_device(name, qweights, "qweights")) || (rc = require_device(name, scales, "scales")) ||
+        (rc = require_device(name, x, "x")))
+      return rc;
+    if ((rc = check_align(name, qweights, scales, scales_are_f16 ? 2 : 4, x))) return rc;
+  }
+  void* img = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      e = cudaGetSymbolAddress(&g_noalloc_addr[dev], g_noalloc_image);
+      if (e != cudaSuccess) {
+        g_noalloc_addr[dev] = nullptr;
+        return cuda_error(e, "cudaGetSymbolAddress (no-alloc scratch)");
+      }
+    }
+    img = g_noalloc_addr[dev];
+  }
+  MatvecArgs a;
+  a.fmt = kFmtQ4_0;
+  a.scales_f16 = scales_are_f16 != 0;
+  a.w = qweights;
+  a.scales = scales;
+  a.image = img;
+  a.y = y;
+  a.M = M;
+  a.K = K;
+  a.weights_static = K > 0 && is_static(qweights, weight_bytes(kFmtQ4_0, M, K)) &&
+                     is_static(scales, (size_t)M * (K / 32) * (scales_are_f16 ? 2 : 4));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K > 0) {
+    e = launch_act_image(x, img, 1, K, st);
+    if (e != cudaSuccess) return cuda_error(e, name);
+  }
+  e = launch_matvec(a, st);
+  if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
 }
 

@@ -60,6 +60,7 @@ SIGNATURES = {
     "asm_weights_unmark_static": ([vp], c_int),
     "asm_device_error": ([ctypes.POINTER(ctypes.c_uint)], c_int),
     "asm_set_option": ([ctypes.c_char_p, c_int], c_int),
+    "asm_matmul_q4_noalloc_async": ([vp, vp, c_int, vp, vp, i64, i64, vp], c_int),
     "asm_max_k": ([c_int, c_int], i64),
     "asm_version": ([], ctypes.c_char_p),
 }

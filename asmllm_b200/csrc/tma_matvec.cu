@@ -232,8 +232,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     const int lane8 = threadIdx.x & 7;
     constexpr int BPP = NCT / 8;  // blocks per pass
     // One L2 round trip for all of x: prefetch every pass's 16 bytes into L1 first.
-    for (int b = threadIdx.x >> 3; b < nb; b += BPP)
-      asm volatile("prefetch.global.L1 [%0];" ::"l"(x + (size_t)b * QK + lane8 * 4));
+
     for (int base = 0; base < nb; base += 4 * BPP) {
       float4 v[4];
 #pragma unroll

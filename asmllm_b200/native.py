@@ -10,7 +10,9 @@ every op in this package runs through this library.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
+from pathlib import Path
 
 from . import build as _build
 
@@ -75,15 +77,25 @@ class AsmError(RuntimeError):
 
 
 def library_path():
-    return _build.LIB_PATH
+    alt = os.environ.get("ASMLLM_LIBRARY")
+    return Path(alt) if alt else _build.LIB_PATH
 
 
 def try_load_native_library() -> ctypes.CDLL:
-    """Returns the loaded library, building it first if needed; raises on failure."""
+    """Returns the loaded library, building it first if needed; raises on failure.
+
+    ASMLLM_LIBRARY=<path> loads another build of the same library instead
+    (for side-by-side measurements); it must exist, nothing is built then."""
     global _lib
     with _lock:
         if _lib is None:
-            path = _build.build()
+            alt = os.environ.get("ASMLLM_LIBRARY")
+            if alt:
+                path = Path(alt)
+                if not path.exists():
+                    raise RuntimeError(f"ASMLLM_LIBRARY={alt} does not exist")
+            else:
+                path = _build.build()
             L = ctypes.CDLL(str(path))
             for name, (argt, rest) in SIGNATURES.items():
                 f = getattr(L, name)

@@ -1,0 +1,61 @@
+"""Small, bounded workload for profiling the matvec kernels under ncu.
+
+    python -m asmllm_b200.profdrive [--fmt q4|q8] [--mode fused|image] [--launches N]
+                                    [--path tma|ldg] MxK [MxK ...]
+
+For each shape it builds one weight matrix on cuda:0 (random seeded quants,
+fp16 scales, declared static like model weights), then runs N matvecs
+(default 2) on torch's current stream.  Device memory stays at the size of
+the largest matrix, so an ncu capture of it ends quickly.
+"""
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+from . import ops
+from .native import FMT_Q4_0, FMT_Q8_0
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("shapes", nargs="+")
+    ap.add_argument("--fmt", choices=["q4", "q8"], default="q4")
+    ap.add_argument("--mode", choices=["fused", "image"], default="fused")
+    ap.add_argument("--launches", type=int, default=2)
+    ap.add_argument("--path", choices=["tma", "ldg"], default="tma")
+    args = ap.parse_args()
+    fmt = FMT_Q4_0 if args.fmt == "q4" else FMT_Q8_0
+    ops.set_option("tma", 1 if args.path == "tma" else 0)
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+    for shape in args.shapes:
+        M, K = (int(v) for v in shape.lower().split("x"))
+        if fmt == FMT_Q4_0:
+            qs = torch.randint(0, 256, (M, K // 32, 16), dtype=torch.uint8, device=dev, generator=gen)
+        else:
+            qs = torch.randint(-127, 128, (M, K // 32, 32), dtype=torch.int8, device=dev, generator=gen)
+        d = torch.randn((M, K // 32), device=dev, generator=gen).abs_().mul_(0.02).half()
+        x = torch.randn(K, device=dev, generator=gen)
+        y = torch.empty(M, device=dev)
+        torch.cuda.synchronize()
+        ops.mark_static(qs, d)
+        for _ in range(args.launches):
+            if args.mode == "fused":
+                ops.matvec(fmt, qs, d, x, out=y)
+            else:
+                img = ops.act_image_dev(x)
+                ops.matvec_image(fmt, qs, d, img, K, out=y)
+        torch.cuda.synchronize()
+        ops.unmark_static(qs, d)
+        del qs, d
+    err = ops.device_error()
+    print(f"profdrive: {len(args.shapes)} shape(s) x {args.launches} launch(es), device error word {err}")
+    if err:
+        raise SystemExit(1)
+
+
+if __name__ == "__main__":
+    main()

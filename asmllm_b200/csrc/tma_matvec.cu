@@ -47,7 +47,7 @@ namespace {
 
 constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200 SM clock
 constexpr int kBarBytes = 256;                   // room for 2 x 8 mbarriers + abort flag
-constexpr int kPartBytes = 2 * 2 * 8 * 4;        // row partials [2 stage parities][2 warpgroups][8]
+constexpr int kPartBytes = 2 * 2 * 8 * 2 * 4;    // row partials [2 parities][2 warpgroups][8 warps][2 rows]
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -132,11 +132,11 @@ __device__ __forceinline__ bool wg_bar_or(int wg, bool v) {
 
 }  // namespace
 
-template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG>
+template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG, int R, int RW>
 __global__ void __launch_bounds__((NWG * 8 + 1) * 32, 2)
 tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales,
                   const void* __restrict__ act, float* __restrict__ y, int M, int nb,
-                  int32_t* __restrict__ isums, int R, int NS, int pre, int pf_stages) {
+                  int32_t* __restrict__ isums, int NS, int pre, int pf_stages) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;  // weight bytes per block
   constexpr int SS = F16S ? 2 : 4;               // scale bytes per block
@@ -147,13 +147,14 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   // Shared layout: [barriers + abort flag | row partials | activation image | ring]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);  // full[0..NS), empty[NS..2NS)
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + kBarBytes - 4);
-  float* part = reinterpret_cast<float*>(smem + kBarBytes);  // [2][NWG][8] partial row sums
+  float* part = reinterpret_cast<float*>(smem + kBarBytes);  // [2][NWG][8][2] partial row sums
   unsigned char* img = smem + kBarBytes + kPartBytes;
   const size_t img_bytes = (act_image_bytes(nb) + 127) & ~(size_t)127;
   unsigned char* stages = img + img_bytes;
   const size_t row_w = (size_t)nb * UB, row_s = (size_t)nb * SS;
   const size_t stage_bytes = (size_t)R * (row_w + row_s);  // R whole rows, then their scales
-  const int WPR = 8 / R;                                   // warps per row
+  constexpr int NRG = R / RW;                              // row groups per stage (RW rows each)
+  constexpr int WPG = 8 / NRG;                             // warps sharing a row group (unit slices)
   const int NU = nb * UPB;                                 // units per row
   const int NSW = NS / NWG;                                // ring slots per warpgroup
 
@@ -225,7 +226,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
 
   // ------------------------------------------------------------ consumers
   const int wg = warp >> 3, wi = warp & 7;
-  const int rr = wi / WPR, sg = wi - rr * WPR;  // this warp's row in a stage and its segment
+  const int rg = wi / WPG, sg = wi - rg * WPG;  // this warp's row group in a stage and its unit slice
   pdl_wait();  // x / the image may come from the previous kernel; y may still be in use
   if (FUSED) {
     const float* x = static_cast<const float*>(act);
@@ -269,71 +270,104 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     const int row0 = r0 + s * R;
     const int nrows = min(R, r1 - row0);
     const unsigned char* st = stages + (size_t)slot * stage_bytes;
-    float acc = 0.0f;
-    if (ok && rr < nrows) {
-      const unsigned char* wrow = st + (size_t)rr * row_w;
-      const unsigned char* srow = st + (size_t)R * row_w + (size_t)rr * row_s;
-      const int row = row0 + rr;
+    // Rows rbase .. rbase+RW-1 of the stage; this warp takes units
+    // sg*32 + lane + 32*WPG*j and reads each activation block once for its RW rows.
+    const int rbase = rg * RW;
+    const int nr = nrows - rbase;  // rows of this group present (<= 0: none)
+    float acc[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) acc[r] = 0.0f;
+    if (ok && nr > 0) {
+      const unsigned char* w0 = st + (size_t)rbase * row_w;
+      const unsigned char* s0 = st + (size_t)R * row_w + (size_t)rbase * row_s;
       if (FMT == kFmtQ4_0) {
 #pragma unroll 4
-        for (int b = sg * 32 + lane; b < nb; b += 32 * WPR) {
-          const uint4 q = *reinterpret_cast<const uint4*>(wrow + b * 16);
-          const float sc = F16S ? __half2float(*reinterpret_cast<const __half*>(srow + b * 2))
-                                : *reinterpret_cast<const float*>(srow + b * 4);
+        for (int b = sg * 32 + lane; b < nb; b += 32 * WPG) {
           const uint4* xp = reinterpret_cast<const uint4*>(img + b * 48);
           const uint4 xa = xp[0], xb = xp[1];
           const float2 dq = sdq[b];
-          int lo = 0, hi = 0;
-          lo = dp4a_us(q.x & 0x0F0F0F0Fu, (int)xa.x, lo);
-          hi = dp4a_us(q.x & 0xF0F0F0F0u, (int)xb.x, hi);
-          lo = dp4a_us(q.y & 0x0F0F0F0Fu, (int)xa.y, lo);
-          hi = dp4a_us(q.y & 0xF0F0F0F0u, (int)xb.y, hi);
-          lo = dp4a_us(q.z & 0x0F0F0F0Fu, (int)xa.z, lo);
-          hi = dp4a_us(q.z & 0xF0F0F0F0u, (int)xb.z, hi);
-          lo = dp4a_us(q.w & 0x0F0F0F0Fu, (int)xa.w, lo);
-          hi = dp4a_us(q.w & 0xF0F0F0F0u, (int)xb.w, hi);
-          const int isum = lo + (hi >> 4) - __float_as_int(dq.y) * 8;
-          if (DBG) isums[(size_t)row * nb + b] = isum;
-          acc = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, dq.x), acc);
+          const int qsum8 = __float_as_int(dq.y) * 8;
+#pragma unroll
+          for (int r = 0; r < RW; ++r) {
+            if (r < nr) {  // uniform across the warp
+              const uint4 q = *reinterpret_cast<const uint4*>(w0 + r * row_w + b * 16);
+              const float sc = F16S ? __half2float(*reinterpret_cast<const __half*>(s0 + r * row_s + b * 2))
+                                    : *reinterpret_cast<const float*>(s0 + r * row_s + b * 4);
+              int lo = 0, hi = 0;
+              lo = dp4a_us(q.x & 0x0F0F0F0Fu, (int)xa.x, lo);
+              hi = dp4a_us(q.x & 0xF0F0F0F0u, (int)xb.x, hi);
+              lo = dp4a_us(q.y & 0x0F0F0F0Fu, (int)xa.y, lo);
+              hi = dp4a_us(q.y & 0xF0F0F0F0u, (int)xb.y, hi);
+              lo = dp4a_us(q.z & 0x0F0F0F0Fu, (int)xa.z, lo);
+              hi = dp4a_us(q.z & 0xF0F0F0F0u, (int)xb.z, hi);
+              lo = dp4a_us(q.w & 0x0F0F0F0Fu, (int)xa.w, lo);
+              hi = dp4a_us(q.w & 0xF0F0F0F0u, (int)xb.w, hi);
+              const int isum = lo + (hi >> 4) - qsum8;
+              if (DBG) isums[(size_t)(row0 + rbase + r) * nb + b] = isum;
+              acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, dq.x), acc[r]);
+            }
+          }
         }
       } else {
 #pragma unroll 4
-        for (int u0 = sg * 32; u0 < NU; u0 += 32 * WPR) {
+        for (int u0 = sg * 32; u0 < NU; u0 += 32 * WPG) {
           const int u = u0 + lane;
           const bool valid = u < NU;  // same for both lanes of a pair
           const int b = u >> 1;
-          uint4 q = make_uint4(0u, 0u, 0u, 0u), xa = make_uint4(0u, 0u, 0u, 0u);
-          float sc = 0.0f, xd = 0.0f;
+          uint4 xa = make_uint4(0u, 0u, 0u, 0u);
+          float xd = 0.0f;
           if (valid) {
-            q = *reinterpret_cast<const uint4*>(wrow + u * 16);
             xa = *reinterpret_cast<const uint4*>(img + b * 48 + (u & 1) * 16);
-            sc = F16S ? __half2float(*reinterpret_cast<const __half*>(srow + b * 2))
-                      : *reinterpret_cast<const float*>(srow + b * 4);
             xd = sdq[b].x;
           }
-          int p = 0;
-          p = dp4a_ss((int)q.x, (int)xa.x, p);
-          p = dp4a_ss((int)q.y, (int)xa.y, p);
-          p = dp4a_ss((int)q.z, (int)xa.z, p);
-          p = dp4a_ss((int)q.w, (int)xa.w, p);
-          const int isum = p + __shfl_xor_sync(kFull, p, 1);
-          if (valid && !(lane & 1)) {
-            if (DBG) isums[(size_t)row * nb + b] = isum;
-            acc = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, xd), acc);
+#pragma unroll
+          for (int r = 0; r < RW; ++r) {
+            if (r < nr) {  // uniform across the warp
+              uint4 q = make_uint4(0u, 0u, 0u, 0u);
+              float sc = 0.0f;
+              if (valid) {
+                q = *reinterpret_cast<const uint4*>(w0 + r * row_w + u * 16);
+                sc = F16S ? __half2float(*reinterpret_cast<const __half*>(s0 + r * row_s + b * 2))
+                          : *reinterpret_cast<const float*>(s0 + r * row_s + b * 4);
+              }
+              int p = 0;
+              p = dp4a_ss((int)q.x, (int)xa.x, p);
+              p = dp4a_ss((int)q.y, (int)xa.y, p);
+              p = dp4a_ss((int)q.z, (int)xa.z, p);
+              p = dp4a_ss((int)q.w, (int)xa.w, p);
+              const int isum = p + __shfl_xor_sync(kFull, p, 1);
+              if (valid && !(lane & 1)) {
+                if (DBG) isums[(size_t)(row0 + rbase + r) * nb + b] = isum;
+                acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, xd), acc[r]);
+              }
+            }
           }
         }
       }
-      acc = warp_sum(acc);
+    }
+    // Lane sums: RW == 1 -> lane 0 holds the row; RW == 2 -> a butterfly that
+    // first trades rows between half-warps (lane 0 ends with row 0, lane 16 row 1).
+    float v;
+    if (RW == 1) {
+      v = warp_sum(acc[0]);
+    } else {
+      const bool upper = lane & 16;
+      v = upper ? acc[RW - 1] : acc[0];
+      v += __shfl_xor_sync(kFull, upper ? acc[0] : acc[RW - 1], 16);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&bars[NS + slot]));  // this warp is done with the slot
-    // Rows split over WPR warps: partials through shared memory, summed in
-    // segment order (deterministic); double-buffered by stage parity.
-    float* pb = part + ((k & 1) * NWG + wg) * 8;
-    if (WPR == 1) {
-      if (ok && rr < nrows && lane == 0) y[row0 + rr] = acc;
-    } else if (lane == 0) {
-      pb[wi] = acc;
+    const int my_row = RW == 1 ? 0 : (lane >> 4);            // row (within the group) this lane's v covers
+    const bool holder = (lane & 15) == 0 && (RW == 2 || lane == 0);
+    // Row groups split over WPG warps: partials through shared memory, summed
+    // in slice order (deterministic); double-buffered by stage parity.
+    float* pb = part + ((k & 1) * NWG + wg) * 16;  // [8 warps][2 rows]
+    if (WPG == 1) {
+      if (ok && holder && my_row < nr) y[row0 + rbase + my_row] = v;
+    } else if (holder) {
+      pb[wi * 2 + my_row] = v;
     }
     // One decision per warpgroup: stop together if any warp timed out or the
     // producer gave up (no warp can be left waiting at this barrier).
@@ -342,10 +376,10 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       *s_abort = 1;
       break;
     }
-    if (WPR > 1 && sg == 0 && rr < nrows && lane == 0) {
-      float v = pb[rr * WPR];
-      for (int t = 1; t < WPR; ++t) v += pb[rr * WPR + t];
-      y[row0 + rr] = v;
+    if (WPG > 1 && sg == 0 && lane < RW && lane < nr) {  // lane r finishes row rbase + r
+      float t = pb[(rg * WPG) * 2 + lane];
+      for (int j = 1; j < WPG; ++j) t += pb[(rg * WPG + j) * 2 + lane];
+      y[row0 + rbase + lane] = t;
     }
   }
 }
@@ -366,7 +400,11 @@ int env_int2(const char* name, int dflt) {
 // best; deeper single-CTA rings and L2 prefetch windows did not help).
 const int g_tma_ctas = env_int2("ASMLLM_TMA_CTAS_PER_SM", 2);
 const int g_tma_smem_kb = env_int2("ASMLLM_TMA_SMEM_KB", 100);
-const int g_tma_nwg = env_int2("ASMLLM_TMA_NWG", 2);
+constexpr int g_tma_nwg = 2;  // consumer warpgroups
+#ifndef ASMLLM_TMA_RW
+#define ASMLLM_TMA_RW 2
+#endif
+constexpr int kTmaRowsPerWarp = ASMLLM_TMA_RW;  // rows each consumer warp takes in a stage
 const int g_tma_carveout = env_int2("ASMLLM_TMA_CARVEOUT", 100);  // percent of the unified L1/shared
 const int g_tma_pf_kb = env_int2("ASMLLM_TMA_PF_KB", 0);          // L2 prefetch window per CTA (off)
 
@@ -403,9 +441,10 @@ bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
   return true;
 }
 
-template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG>
+template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG, int R>
 cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
-  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, FUSED, NWG>;
+  constexpr int RW = R >= 2 ? kTmaRowsPerWarp : 1;
+  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, FUSED, NWG, R, RW>;
   int dev = 0;
   cudaGetDevice(&dev);
   {
@@ -428,11 +467,11 @@ cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStr
   float* y = a.y;
   int M = (int)a.M, nb = (int)(a.K / QK);
   int32_t* isums = a.isums;
-  int R = p.R, NS = p.NS, pre = a.weights_static ? 1 : 0;
+  int NS = p.NS, pre = a.weights_static ? 1 : 0;
   const size_t stage_b = (size_t)R * (size_t)nb * ((FMT == kFmtQ4_0 ? 16 : 32) + (F16S ? 2 : 4));
   int pf = (int)(((size_t)g_tma_pf_kb * 1024) / stage_b);
   void* args[] = {(void*)&w, (void*)&s, (void*)&act, (void*)&y, (void*)&M, (void*)&nb,
-                  (void*)&isums, (void*)&R, (void*)&NS, (void*)&pre, (void*)&pf};
+                  (void*)&isums, (void*)&NS, (void*)&pre, (void*)&pf};
   long long grid = (long long)sms * (g_tma_ctas > 0 ? g_tma_ctas : 1);
   const long long groups = (M + R - 1) / R;
   if (grid > groups) grid = groups;
@@ -450,19 +489,29 @@ cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStr
   return cudaLaunchKernelExC(&cfg, (const void*)kernel, args);
 }
 
-template <int FMT, int NWG>
-cudaError_t launch_tma_fmt(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+template <int FMT, int NWG, int R>
+cudaError_t launch_tma_r(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
   const bool fused = a.image == nullptr;
   if (a.isums) {
-    return fused ? launch_tma_t<FMT, false, true, true, NWG>(a, p, sms, stream, pdl)
-                 : launch_tma_t<FMT, false, true, false, NWG>(a, p, sms, stream, pdl);
+    return fused ? launch_tma_t<FMT, false, true, true, NWG, R>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, false, true, false, NWG, R>(a, p, sms, stream, pdl);
   }
   if (a.scales_f16) {
-    return fused ? launch_tma_t<FMT, true, false, true, NWG>(a, p, sms, stream, pdl)
-                 : launch_tma_t<FMT, true, false, false, NWG>(a, p, sms, stream, pdl);
+    return fused ? launch_tma_t<FMT, true, false, true, NWG, R>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, true, false, false, NWG, R>(a, p, sms, stream, pdl);
   }
-  return fused ? launch_tma_t<FMT, false, false, true, NWG>(a, p, sms, stream, pdl)
-               : launch_tma_t<FMT, false, false, false, NWG>(a, p, sms, stream, pdl);
+  return fused ? launch_tma_t<FMT, false, false, true, NWG, R>(a, p, sms, stream, pdl)
+               : launch_tma_t<FMT, false, false, false, NWG, R>(a, p, sms, stream, pdl);
+}
+
+template <int FMT, int NWG>
+cudaError_t launch_tma_fmt(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+  switch (p.R) {
+    case 8: return launch_tma_r<FMT, NWG, 8>(a, p, sms, stream, pdl);
+    case 4: return launch_tma_r<FMT, NWG, 4>(a, p, sms, stream, pdl);
+    case 2: return launch_tma_r<FMT, NWG, 2>(a, p, sms, stream, pdl);
+    default: return launch_tma_r<FMT, NWG, 1>(a, p, sms, stream, pdl);
+  }
 }
 
 }  // namespace
@@ -476,11 +525,8 @@ bool tma_matvec_supported(const MatvecArgs& a, int smem_optin) {
 cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl) {
   TmaPlan p;
   if (!tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, &p)) return cudaErrorInvalidValue;
-  if (a.fmt == kFmtQ4_0)
-    return g_tma_nwg == 1 ? launch_tma_fmt<kFmtQ4_0, 1>(a, p, sms, stream, pdl)
-                          : launch_tma_fmt<kFmtQ4_0, 2>(a, p, sms, stream, pdl);
-  return g_tma_nwg == 1 ? launch_tma_fmt<kFmtQ8_0, 1>(a, p, sms, stream, pdl)
-                        : launch_tma_fmt<kFmtQ8_0, 2>(a, p, sms, stream, pdl);
+  if (a.fmt == kFmtQ4_0) return launch_tma_fmt<kFmtQ4_0, 2>(a, p, sms, stream, pdl);
+  return launch_tma_fmt<kFmtQ8_0, 2>(a, p, sms, stream, pdl);
 }
 
 cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream) {

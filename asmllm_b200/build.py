@@ -21,7 +21,7 @@ INCLUDE = ROOT / "include"
 LIB_DIR = ROOT / "build"
 LIB_PATH = LIB_DIR / "libasmllm.so"
 
-SOURCES = ["matvec.cu", "tma_matvec.cu", "capi.cu"]
+SOURCES = ["matvec.cu", "tma_matvec.cu", "decode.cu", "capi.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -51,17 +51,33 @@ def build(verbose: bool = False, force: bool = False) -> Path:
         return LIB_PATH
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = LIB_DIR / f".libasmllm.{os.getpid()}.so"
-    cmd = [nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-shared",
-           "-Xcompiler", "-fPIC,-fvisibility=hidden", "-cudart", "static",
-           f"-I{INCLUDE}", "-o", str(tmp)]
+    common = [nvcc(), *ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17",
+              "-Xcompiler", "-fPIC,-fvisibility=hidden", f"-I{INCLUDE}"]
     if verbose:
-        cmd += ["-Xptxas", "-v"]
-    cmd += [str(CSRC / s) for s in SOURCES]
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if verbose:
-        sys.stderr.write(res.stderr)
+        common += ["-Xptxas", "-v"]
+    # One nvcc per translation unit, in parallel, then one link.
+    objs = [LIB_DIR / f".{Path(s).stem}.{os.getpid()}.o" for s in SOURCES]
+    procs = [subprocess.Popen(common + ["-c", str(CSRC / s), "-o", str(o)],
+                              stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+             for s, o in zip(SOURCES, objs)]
+    errs = []
+    for s, pr in zip(SOURCES, procs):
+        out, err = pr.communicate()
+        if pr.returncode != 0:
+            errs.append(f"nvcc {s} failed ({pr.returncode}):\n{out}\n{err}")
+        elif verbose:
+            sys.stderr.write(err)
+    try:
+        if errs:
+            raise RuntimeError("\n".join(errs))
+        cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-cudart", "static", "-o", str(tmp)] + [str(o) for o in objs]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"nvcc link failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    finally:
+        for o in objs:
+            if o.exists():
+                o.unlink()
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

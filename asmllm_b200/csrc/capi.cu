@@ -14,6 +14,7 @@
 #include <cuda_fp16.h>
 
 #include <cstdarg>
+#include <cstddef>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -926,6 +927,121 @@ ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* 
     if (e != cudaSuccess) return cuda_error(e, name);
   }
   e = launch_matvec(a, st);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+// ctypes mirrors of the descriptor (asmllm_b200/native.py FusedMatvec) rely on this layout.
+static_assert(sizeof(asm_fused_matvec_t) == 160 && offsetof(asm_fused_matvec_t, eps) == 128 &&
+                  offsetof(asm_fused_matvec_t, M) == 144,
+              "asm_fused_matvec_t layout");
+
+ASMLLM_API int asm_fused_matvec_async(const asm_fused_matvec_t* p, void* stream) {
+  const char* name = "asm_fused_matvec_async";
+  if (!p) return set_error(ASM_E_INVALID, "%s: null descriptor", name);
+  if (p->fmt != kFmtQ4_0 && p->fmt != kFmtQ8_0)
+    return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, p->fmt);
+  if (p->epilogue < ASM_EPI_STORE || p->epilogue > ASM_EPI_ARGMAX)
+    return set_error(ASM_E_INVALID, "%s: unknown epilogue %d", name, p->epilogue);
+  if (p->M <= 0 || p->K <= 0 || p->K % 32 != 0 || p->M > INT32_MAX)
+    return set_error(ASM_E_INVALID, "%s: need M > 0 and K > 0 a multiple of 32 (M=%lld K=%lld)", name,
+                     (long long)p->M, (long long)p->K);
+  int rc;
+  if ((rc = require_device(name, p->qweights, "qweights")) || (rc = require_device(name, p->scales, "scales")) ||
+      (rc = require_device(name, p->y, "y")))
+    return rc;
+  if ((uintptr_t)p->qweights % 16 || (uintptr_t)p->scales % 16 || (uintptr_t)p->y % 4)
+    return set_error(ASM_E_INVALID, "%s: qweights and scales must be 16-byte aligned", name);
+  auto dev16 = [&](const void* q, const char* what) -> int {
+    if ((rc = require_device(name, q, what))) return rc;
+    if ((uintptr_t)q % 16) return set_error(ASM_E_INVALID, "%s: %s must be 16-byte aligned", name, what);
+    return ASM_OK;
+  };
+  if (p->image) {
+    if ((rc = dev16(p->image, "image"))) return rc;
+    if (p->norm_w || p->embed)
+      return set_error(ASM_E_INVALID, "%s: an image prologue takes no norm_w or embed", name);
+  } else if (p->embed) {
+    if ((rc = dev16(p->embed, "embed")) || (rc = require_device(name, p->tokens, "tokens")) ||
+        (rc = require_device(name, p->pos, "pos")))
+      return rc;
+    if (p->vocab <= 0 || p->max_tokens <= 0)
+      return set_error(ASM_E_INVALID, "%s: embed needs vocab > 0 and max_tokens > 0", name);
+  } else if ((rc = dev16(p->x, "x"))) {
+    return rc;
+  }
+  if (p->norm_w && (rc = dev16(p->norm_w, "norm_w"))) return rc;
+  if (p->x_copy && (rc = dev16(p->x_copy, "x_copy"))) return rc;
+  if (p->epilogue == ASM_EPI_SWIGLU) {
+    if (p->M % 64 != 0) return set_error(ASM_E_INVALID, "%s: SWIGLU needs M %% 64 == 0 (M=%lld)", name, (long long)p->M);
+    if ((rc = dev16(p->h, "h")) || (rc = dev16(p->image_out, "image_out")) ||
+        (rc = require_device(name, p->counters, "counters")))
+      return rc;
+  }
+  if (p->epilogue == ASM_EPI_ARGMAX) {
+    if ((rc = require_device(name, p->best, "best")) || (rc = require_device(name, p->done, "done")) ||
+        (rc = require_device(name, p->tokens, "tokens")) || (rc = require_device(name, p->pos, "pos")))
+      return rc;
+    if ((uintptr_t)p->best % 8) return set_error(ASM_E_INVALID, "%s: best must be 8-byte aligned", name);
+    if (p->max_tokens <= 0) return set_error(ASM_E_INVALID, "%s: ARGMAX needs max_tokens > 0", name);
+  }
+  MvFuse f;
+  f.norm_w = p->norm_w;
+  f.eps = p->eps;
+  f.embed = p->image ? nullptr : p->embed;
+  f.vocab = p->vocab;
+  f.tokens = p->tokens;
+  f.pos = p->pos;
+  f.max_tokens = p->max_tokens;
+  f.n_prompt = p->n_prompt;
+  f.x_copy = p->x_copy;
+  f.h = p->h;
+  f.image_out = static_cast<unsigned char*>(p->image_out);
+  f.counters = p->counters;
+  f.best = reinterpret_cast<unsigned long long*>(p->best);
+  f.done = p->done;
+  MatvecArgs a;
+  a.fmt = p->fmt;
+  a.scales_f16 = true;
+  a.w = p->qweights;
+  a.scales = p->scales;
+  a.x = p->x;
+  a.image = p->image;
+  a.y = p->y;
+  a.M = p->M;
+  a.K = p->K;
+  a.epi = p->epilogue;
+  a.fuse = &f;
+  a.weights_static = is_static(p->qweights, weight_bytes(p->fmt, p->M, p->K)) &&
+                     is_static(p->scales, (size_t)p->M * (p->K / 32) * 2);
+  const cudaError_t e = launch_matvec(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported)
+    return set_error(ASM_E_UNSUPPORTED, "%s: no bulk-copy plan for this shape and fusion (M=%lld K=%lld epilogue %d)",
+                     name, (long long)p->M, (long long)p->K, p->epilogue);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_attention_decode_async(const float* qkv, void* k_cache, void* v_cache,
+                                          const float* rope_cs, const int32_t* pos, void* image_out,
+                                          int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                          int32_t ctx, float sqrt_head_dim, void* stream) {
+  const char* name = "asm_attention_decode_async";
+  if (head_dim != 128) return set_error(ASM_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, head_dim);
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || ctx <= 0)
+    return set_error(ASM_E_INVALID, "%s: need n_heads a multiple of n_kv_heads and ctx > 0", name);
+  int rc;
+  if ((rc = require_device(name, qkv, "qkv")) || (rc = require_device(name, k_cache, "k_cache")) ||
+      (rc = require_device(name, v_cache, "v_cache")) || (rc = require_device(name, rope_cs, "rope_cs")) ||
+      (rc = require_device(name, pos, "pos")) || (rc = require_device(name, image_out, "image_out")))
+    return rc;
+  if ((uintptr_t)qkv % 16 || (uintptr_t)k_cache % 16 || (uintptr_t)v_cache % 16 || (uintptr_t)rope_cs % 8 ||
+      (uintptr_t)image_out % 16)
+    return set_error(ASM_E_INVALID, "%s: misaligned buffer", name);
+  const cudaError_t e = launch_attention_decode(qkv, k_cache, v_cache, rope_cs, pos, image_out, n_heads, n_kv_heads,
+                                                head_dim, ctx, sqrt_head_dim, static_cast<cudaStream_t>(stream),
+                                                g_opt_pdl.load() != 0);
+  if (e == cudaErrorNotSupported) return set_error(ASM_E_UNSUPPORTED, "%s: ctx %d too long for shared memory", name, ctx);
   if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
 }

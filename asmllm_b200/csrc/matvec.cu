@@ -673,6 +673,10 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
 
   int pf = 0;
   int pre = a.weights_static ? 1 : 0;
+  if (matvec_is_fused(a)) {  // the decode fusions live in the bulk-copy kernel only
+    if (a.fp32_act || !tma_matvec_supported(a, di.smem_optin)) return cudaErrorNotSupported;
+    return launch_tma_matvec(a, di.sms, di.smem_optin, stream, g_opt_pdl.load() != 0);
+  }
   if (!a.fp32_act && g_opt_tma.load() && !a.isums_force_ldg && tma_matvec_supported(a, di.smem_optin))
     return launch_tma_matvec(a, di.sms, di.smem_optin, stream, g_opt_pdl.load() != 0);
   if (!a.fp32_act) {

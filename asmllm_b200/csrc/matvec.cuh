@@ -12,6 +12,41 @@ namespace asmllm {
 constexpr int kFmtQ4_0 = 2;
 constexpr int kFmtQ8_0 = 8;
 
+// Decode-step fusions of the bulk-copy matvec (tma_matvec.cu).
+//
+// Prologue (how the CTA builds its Q8_0 activation image):
+constexpr int kProImage = 0;  // copy a prepared image (MatvecArgs::image)
+constexpr int kProQuant = 1;  // quantize fp32 x
+constexpr int kProNorm = 2;   // RMSNorm x with norm_w, then quantize
+// Epilogue (what happens to a finished row value v):
+constexpr int kEpiStore = 0;     // y[r] = v
+constexpr int kEpiResidual = 1;  // y[r] += v (y is the residual stream)
+constexpr int kEpiSwiglu = 2;    // rows (2i, 2i+1) = (gate_i, up_i): h_i = silu(gate_i) * up_i,
+                                 // quantized to Q8_0 into image_out block by block
+constexpr int kEpiArgmax = 3;    // y[r] = v, then the next token = argmax over all rows
+
+struct MvFuse {
+  const float* norm_w = nullptr;  // kProNorm: weight [K]
+  float eps = 0.0f;
+  // Source row of the prologue: embed + tokens[*pos] * K when embed is set
+  // (the first layer of a decode step), else MatvecArgs::x.  CTA 0 copies the
+  // source row to x_copy (the residual stream) when x_copy is set.
+  const float* embed = nullptr;
+  int32_t vocab = 0;
+  int32_t* tokens = nullptr;  // [max_tokens]: prompt ids, then generated ids
+  int32_t* pos = nullptr;     // current position (device); advanced by kEpiArgmax
+  int32_t max_tokens = 0;
+  int32_t n_prompt = 0;
+  float* x_copy = nullptr;
+  // kEpiSwiglu
+  float* h = nullptr;                 // [M/2] fp32
+  unsigned char* image_out = nullptr; // Q8_0 image of h (nb = M/64 blocks)
+  unsigned* counters = nullptr;       // [M/64] zero on entry; left zero
+  // kEpiArgmax
+  unsigned long long* best = nullptr;  // packed (value, row); zero on entry, left zero
+  unsigned* done = nullptr;            // CTAs finished; zero on entry, left zero
+};
+
 struct MatvecArgs {
   int fmt = kFmtQ4_0;       // kFmtQ4_0 or kFmtQ8_0
   bool fp32_act = false;    // false: Q8_0 activations (NEON semantics); true: fp32 x (x86)
@@ -28,7 +63,16 @@ struct MatvecArgs {
   // Use the register-streaming (LDG) kernel even where the bulk-copy one applies.
   bool isums_force_ldg = false;
   int64_t M = 0, K = 0;
+  // Decode fusions (bulk-copy kernel, fp16 scales only): the prologue is
+  // kProImage when image is set, else kProNorm when fuse->norm_w is set, else
+  // kProQuant.
+  int epi = kEpiStore;
+  const MvFuse* fuse = nullptr;
 };
+
+// Device error word bits (read_device_error).
+constexpr unsigned kErrRingTimeout = 1u;  // a shared-memory ring barrier wait gave up
+constexpr unsigned kErrDecodeRange = 2u;  // decode position or token id out of range: step skipped
 
 // Bytes of one row of the Q8_0 activation image for nb = K/32 blocks:
 // nb 48-byte slots (32 int8 + 16 pad) then nb (d, qsum) float pairs, rounded to 16.
@@ -52,11 +96,22 @@ int64_t max_k(int fmt, bool fp32_act, int dev);
 // Bulk-copy (TMA) pipeline kernel for the Q8_0-activation families
 // (tma_matvec.cu); launch_matvec uses it when the shape allows.
 bool tma_matvec_supported(const MatvecArgs& a, int smem_optin);
+// True when a asks for a decode fusion (which only the bulk-copy kernel has).
+bool matvec_is_fused(const MatvecArgs& a);
 cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl);
 // Reads (and optionally clears) the device error word the kernels set when a
 // bounded wait gives up (bit 0: a shared-memory ring barrier timed out).
 cudaError_t read_device_error(unsigned* out, bool clear);
 cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream);
+// Device address of the error word on the current device (for kernels in
+// other translation units); nullptr if it cannot be looked up.
+unsigned* device_error_word();
+
+// Attention for one decode position (decode.cu): RoPE, fp16 KV append,
+// softmax(q.K^T / sqrt_hd).V per query head, Q8_0 image of the output.
+cudaError_t launch_attention_decode(const float* qkv, void* k_cache, void* v_cache, const float* rope_cs,
+                                    const int32_t* pos, void* image, int n_heads, int n_kv, int head_dim, int ctx,
+                                    float sqrt_hd, cudaStream_t stream, bool pdl);
 
 extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
 extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch

@@ -132,11 +132,52 @@ __device__ __forceinline__ bool wg_bar_or(int wg, bool v) {
 
 }  // namespace
 
-template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG, int R, int RW>
+// Orderable 64-bit key of (value, row): larger value first, then lower row
+// (numpy.argmax returns the first maximum).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)row);
+}
+
+// Called once per CTA (thread 0) after its rows' keys are folded into
+// fz.best: the last CTA to arrive turns the maximum into the next token,
+// advances the position and leaves best / done zero for the next launch.
+__device__ void argmax_arrive(const MvFuse& fz, unsigned nctas) {
+  __threadfence();
+  if (atomicAdd(fz.done, 1u) != nctas - 1) return;
+  __threadfence();
+  const unsigned long long b = atomicExch(fz.best, 0ull);
+  const int idx = b ? (int)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull)) : 0;
+  volatile int32_t* pos = fz.pos;
+  const int p = *pos;
+  if (p >= 0 && p + 1 < fz.max_tokens) {
+    if (p + 1 >= fz.n_prompt) fz.tokens[p + 1] = idx;  // prompt positions keep their ids
+  } else {
+    atomicOr(&g_device_error, kErrDecodeRange);
+  }
+  *pos = p + 1;
+  atomicExch(fz.done, 0u);
+}
+
+// Source row of a quantizing prologue: x, or the embedding row of the token
+// at the current position (out-of-range ids read row 0 and set an error bit).
+__device__ __forceinline__ const float* prologue_source(const MvFuse& fz, const void* act, int K) {
+  if (fz.embed == nullptr) return static_cast<const float*>(act);
+  const int p = *fz.pos;
+  int tok = (p >= 0 && p < fz.max_tokens) ? fz.tokens[p] : -1;
+  if (tok < 0 || tok >= fz.vocab) {
+    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrDecodeRange);
+    tok = 0;
+  }
+  return fz.embed + (size_t)tok * K;
+}
+
+template <int FMT, bool F16S, bool DBG, int PRO, int EPI, int NWG, int R, int RW>
 __global__ void __launch_bounds__((NWG * 8 + 1) * 32, 2)
 tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales,
                   const void* __restrict__ act, float* __restrict__ y, int M, int nb,
-                  int32_t* __restrict__ isums, int NS, int pre, int pf_stages) {
+                  int32_t* __restrict__ isums, int NS, int pre, int pf_stages, const MvFuse fz) {
   extern __shared__ __align__(128) unsigned char smem[];
   constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;  // weight bytes per block
   constexpr int SS = F16S ? 2 : 4;               // scale bytes per block
@@ -158,13 +199,23 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   const int NU = nb * UPB;                                 // units per row
   const int NSW = NS / NWG;                                // ring slots per warpgroup
 
+  // SwiGLU pairs (gate, up) must not straddle CTAs or row groups.
+  static_assert(EPI != kEpiSwiglu || (RW == 2 && WPG > 1), "SwiGLU epilogue needs two-row groups");
+  constexpr int G = EPI == kEpiSwiglu ? 2 : 1;  // row granularity of the CTA split
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r0 = (int)((long long)M * blockIdx.x / gridDim.x);
-  const int r1 = (int)((long long)M * (blockIdx.x + 1) / gridDim.x);
+  const int r0 = G * (int)((long long)(M / G) * blockIdx.x / gridDim.x);
+  const int r1 = G * (int)((long long)(M / G) * (blockIdx.x + 1) / gridDim.x);
   const int S = (r1 - r0 + R - 1) / R;  // stages; stage s owned by warpgroup s % NWG
 
   pdl_trigger();
-  if (S == 0) return;
+  if (S == 0) {
+    if (EPI == kEpiArgmax && threadIdx.x == 0) {
+      pdl_wait();
+      argmax_arrive(fz, gridDim.x);
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSW * NWG; ++i) {
@@ -228,11 +279,32 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   const int wg = warp >> 3, wi = warp & 7;
   const int rg = wi / WPG, sg = wi - rg * WPG;  // this warp's row group in a stage and its unit slice
   pdl_wait();  // x / the image may come from the previous kernel; y may still be in use
-  if (FUSED) {
-    const float* x = static_cast<const float*>(act);
+  if (PRO != kProImage) {
+    const float* x = prologue_source(fz, act, nb * QK);
+    const bool copy = fz.x_copy != nullptr && blockIdx.x == 0;
     const int lane8 = threadIdx.x & 7;
     constexpr int BPP = NCT / 8;  // blocks per pass
-    // One L2 round trip for all of x: prefetch every pass's 16 bytes into L1 first.
+    float rms = 1.0f;
+    if (PRO == kProNorm) {
+      // rms = sqrt(mean(x^2) + eps), one fixed-order sum shared by every thread.
+      float ss = 0.0f;
+      for (int i = threadIdx.x; i < nb * 8; i += NCT) {
+        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                                     __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
+        if (copy) reinterpret_cast<float4*>(fz.x_copy)[i] = v;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) part[warp] = ss;
+      consumer_bar_sync(NCT);
+      float tot = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NCW; ++i) tot = __fadd_rn(tot, part[i]);
+      rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * QK)), fz.eps));
+    } else if (copy) {
+      for (int i = threadIdx.x; i < nb * 8; i += NCT)
+        reinterpret_cast<float4*>(fz.x_copy)[i] = reinterpret_cast<const float4*>(x)[i];
+    }
 
     for (int base = 0; base < nb; base += 4 * BPP) {
       float4 v[4];
@@ -240,6 +312,11 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       for (int p = 0; p < 4; ++p) {  // issue the loads of 4 passes before any use
         const int b = base + p * BPP + (threadIdx.x >> 3);
         v[p] = b < nb ? reinterpret_cast<const float4*>(x + (size_t)b * QK)[lane8] : make_float4(0.f, 0.f, 0.f, 0.f);
+        if (PRO == kProNorm && b < nb) {  // (x / rms) * w, as the reference RMSNorm
+          const float4 nw = reinterpret_cast<const float4*>(fz.norm_w + (size_t)b * QK)[lane8];
+          v[p] = make_float4(__fmul_rn(__fdiv_rn(v[p].x, rms), nw.x), __fmul_rn(__fdiv_rn(v[p].y, rms), nw.y),
+                             __fmul_rn(__fdiv_rn(v[p].z, rms), nw.z), __fmul_rn(__fdiv_rn(v[p].w, rms), nw.w));
+        }
       }
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
@@ -263,6 +340,50 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   consumer_bar_sync(NCT);
 
   const float2* sdq = reinterpret_cast<const float2*>(img + (size_t)nb * 48);
+  unsigned long long best_local = 0;  // kEpiArgmax: this lane's best (value, row)
+  auto emit = [&](int row, float t) {
+    if (EPI == kEpiResidual) {
+      y[row] = __fadd_rn(y[row], t);
+    } else {
+      y[row] = t;
+      if (EPI == kEpiArgmax && t == t) {
+        const unsigned long long key = argmax_key(t, row);
+        best_local = key > best_local ? key : best_local;
+      }
+    }
+  };
+  // Rows (row, row + 1) = (gate_i, up_i): h_i = silu(gate) * up, as the
+  // reference's (gate / (1 + exp(-gate))) * up.  The warp that completes the
+  // 32nd h of a block (arrival counter) quantizes that block into image_out.
+  auto swiglu_emit = [&](int row, const float* pr) {
+    const int i = row >> 1;
+    int last = 0;
+    if (lane == 0) {
+      float g = pr[0], u = pr[1];
+      for (int j = 1; j < WPG; ++j) {
+        g += pr[j * 2];
+        u += pr[j * 2 + 1];
+      }
+      const float hv = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+      __stcg(fz.h + i, hv);
+      __threadfence();
+      last = atomicAdd(fz.counters + (i >> 5), 1u) == 31u;
+    }
+    last = __shfl_sync(kFull, last, 0);
+    if (last) {
+      __threadfence();
+      const int blk = i >> 5;
+      const float4 hv4 = __ldcg(reinterpret_cast<const float4*>(fz.h + (size_t)blk * QK) + (lane & 7));
+      float d;
+      int qsum;
+      const unsigned q = quantize_quad(hv4, d, qsum);
+      if (lane < 8) reinterpret_cast<unsigned*>(fz.image_out + (size_t)blk * 48)[lane] = q;
+      if (lane == 0) {
+        reinterpret_cast<float2*>(fz.image_out + (size_t)(M >> 6) * 48)[blk] = make_float2(d, __int_as_float(qsum));
+        fz.counters[blk] = 0u;
+      }
+    }
+  };
   for (int s = wg, k = 0; s < S; s += NWG, ++k) {
     const int slot = wg * NSW + k % NSW;
     const bool ok = mbar_wait_bounded(smem_u32(&bars[slot]), (k / NSW) & 1);
@@ -365,7 +486,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     // in slice order (deterministic); double-buffered by stage parity.
     float* pb = part + ((k & 1) * NWG + wg) * 16;  // [8 warps][2 rows]
     if (WPG == 1) {
-      if (ok && holder && my_row < nr) y[row0 + rbase + my_row] = v;
+      if (ok && holder && my_row < nr) emit(row0 + rbase + my_row, v);
     } else if (holder) {
       pb[wi * 2 + my_row] = v;
     }
@@ -376,11 +497,26 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       *s_abort = 1;
       break;
     }
-    if (WPG > 1 && sg == 0 && lane < RW && lane < nr) {  // lane r finishes row rbase + r
-      float t = pb[(rg * WPG) * 2 + lane];
-      for (int j = 1; j < WPG; ++j) t += pb[(rg * WPG + j) * 2 + lane];
-      y[row0 + rbase + lane] = t;
+    if (WPG > 1 && sg == 0) {
+      if (EPI == kEpiSwiglu) {
+        if (nr >= 2) swiglu_emit(row0 + rbase, pb + rg * WPG * 2);  // whole warp
+      } else if (lane < RW && lane < nr) {  // lane r finishes row rbase + r
+        float t = pb[(rg * WPG) * 2 + lane];
+        for (int j = 1; j < WPG; ++j) t += pb[(rg * WPG + j) * 2 + lane];
+        emit(row0 + rbase + lane, t);
+      }
     }
+  }
+  if (EPI == kEpiArgmax) {
+    unsigned long long b = best_local;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long t = __shfl_xor_sync(kFull, b, o);
+      b = t > b ? t : b;
+    }
+    if (lane == 0 && b) atomicMax(fz.best, b);
+    consumer_bar_sync(NCT);
+    if (threadIdx.x == 0) argmax_arrive(fz, gridDim.x);
   }
 }
 
@@ -429,11 +565,17 @@ bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
   size_t budget = (size_t)g_tma_smem_kb * 1024;
   if (budget > (size_t)smem_optin) budget = smem_optin;
   const size_t fixed = kBarBytes + kPartBytes + img;
-  if (budget < fixed) return false;
-  size_t ns = (budget - fixed) / stage;
-  if (ns > 8) ns = 8;
   const size_t nwg = g_tma_nwg == 1 ? 1 : 2;
-  ns -= ns % nwg;  // equal rings per warpgroup
+  auto slots = [&](size_t b) -> size_t {
+    if (b < fixed) return 0;
+    size_t n = (b - fixed) / stage;
+    if (n > 8) n = 8;
+    return n - n % nwg;  // equal rings per warpgroup
+  };
+  size_t ns = slots(budget);
+  // Long rows (a large activation image plus big stages): take the whole
+  // opt-in shared memory, one CTA per SM.
+  if (ns < 2 * nwg) ns = slots(budget = (size_t)smem_optin);
   if (ns < 2 * nwg) return false;
   p->R = R;
   p->NS = (int)ns;
@@ -441,10 +583,10 @@ bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
   return true;
 }
 
-template <int FMT, bool F16S, bool DBG, bool FUSED, int NWG, int R>
+template <int FMT, bool F16S, bool DBG, int PRO, int EPI, int NWG, int R>
 cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
   constexpr int RW = R >= 2 ? kTmaRowsPerWarp : 1;
-  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, FUSED, NWG, R, RW>;
+  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, PRO, EPI, NWG, R, RW>;
   int dev = 0;
   cudaGetDevice(&dev);
   {
@@ -470,9 +612,17 @@ cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStr
   int NS = p.NS, pre = a.weights_static ? 1 : 0;
   const size_t stage_b = (size_t)R * (size_t)nb * ((FMT == kFmtQ4_0 ? 16 : 32) + (F16S ? 2 : 4));
   int pf = (int)(((size_t)g_tma_pf_kb * 1024) / stage_b);
-  void* args[] = {(void*)&w, (void*)&s, (void*)&act, (void*)&y, (void*)&M, (void*)&nb,
-                  (void*)&isums, (void*)&NS, (void*)&pre, (void*)&pf};
-  long long grid = (long long)sms * (g_tma_ctas > 0 ? g_tma_ctas : 1);
+  MvFuse fz = a.fuse ? *a.fuse : MvFuse{};
+  void* args[] = {(void*)&w,     (void*)&s,  (void*)&act, (void*)&y,  (void*)&M,  (void*)&nb,
+                  (void*)&isums, (void*)&NS, (void*)&pre, (void*)&pf, (void*)&fz};
+  // Persistent grid: as many CTAs per SM as fit beside each other (the
+  // default 2 at ~100 KB; 1 for the long-row plans that take more).
+  int smem_sm = 0;
+  cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+  int per_sm = g_tma_ctas > 0 ? g_tma_ctas : 1;
+  const int fit = smem_sm > 0 ? (int)((size_t)smem_sm / (p.smem + 1024)) : per_sm;
+  if (per_sm > fit) per_sm = fit > 0 ? fit : 1;
+  long long grid = (long long)sms * per_sm;
   const long long groups = (M + R - 1) / R;
   if (grid > groups) grid = groups;
   if (grid < 1) grid = 1;
@@ -489,19 +639,56 @@ cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStr
   return cudaLaunchKernelExC(&cfg, (const void*)kernel, args);
 }
 
+int prologue_of(const MatvecArgs& a) {
+  if (a.image) return kProImage;
+  return (a.fuse && a.fuse->norm_w) ? kProNorm : kProQuant;
+}
+
+bool is_fused(const MatvecArgs& a) {
+  return a.epi != kEpiStore || prologue_of(a) == kProNorm || (a.fuse && (a.fuse->embed || a.fuse->x_copy));
+}
+
+// Decode fusions: fp16 scales, no per-block sums; the combinations a decode
+// step uses (RMSNorm -> q/k/v, gate/up or lm_head; image or x -> residual).
+template <int FMT, int NWG, int R>
+cudaError_t launch_tma_fused(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+  const int pro = prologue_of(a);
+  switch (a.epi) {
+    case kEpiStore:
+      if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiStore, NWG, R>(a, p, sms, stream, pdl);
+      break;
+    case kEpiResidual:
+      if (pro == kProImage) return launch_tma_t<FMT, true, false, kProImage, kEpiResidual, NWG, R>(a, p, sms, stream, pdl);
+      if (pro == kProQuant) return launch_tma_t<FMT, true, false, kProQuant, kEpiResidual, NWG, R>(a, p, sms, stream, pdl);
+      break;
+    case kEpiSwiglu:
+      if constexpr (R >= 2) {
+        if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiSwiglu, NWG, R>(a, p, sms, stream, pdl);
+      }
+      break;
+    case kEpiArgmax:
+      if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiArgmax, NWG, R>(a, p, sms, stream, pdl);
+      break;
+    default:
+      break;
+  }
+  return cudaErrorNotSupported;
+}
+
 template <int FMT, int NWG, int R>
 cudaError_t launch_tma_r(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+  if (is_fused(a)) return launch_tma_fused<FMT, NWG, R>(a, p, sms, stream, pdl);
   const bool fused = a.image == nullptr;
   if (a.isums) {
-    return fused ? launch_tma_t<FMT, false, true, true, NWG, R>(a, p, sms, stream, pdl)
-                 : launch_tma_t<FMT, false, true, false, NWG, R>(a, p, sms, stream, pdl);
+    return fused ? launch_tma_t<FMT, false, true, kProQuant, kEpiStore, NWG, R>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, false, true, kProImage, kEpiStore, NWG, R>(a, p, sms, stream, pdl);
   }
   if (a.scales_f16) {
-    return fused ? launch_tma_t<FMT, true, false, true, NWG, R>(a, p, sms, stream, pdl)
-                 : launch_tma_t<FMT, true, false, false, NWG, R>(a, p, sms, stream, pdl);
+    return fused ? launch_tma_t<FMT, true, false, kProQuant, kEpiStore, NWG, R>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, true, false, kProImage, kEpiStore, NWG, R>(a, p, sms, stream, pdl);
   }
-  return fused ? launch_tma_t<FMT, false, false, true, NWG, R>(a, p, sms, stream, pdl)
-               : launch_tma_t<FMT, false, false, false, NWG, R>(a, p, sms, stream, pdl);
+  return fused ? launch_tma_t<FMT, false, false, kProQuant, kEpiStore, NWG, R>(a, p, sms, stream, pdl)
+               : launch_tma_t<FMT, false, false, kProImage, kEpiStore, NWG, R>(a, p, sms, stream, pdl);
 }
 
 template <int FMT, int NWG>
@@ -519,8 +706,15 @@ cudaError_t launch_tma_fmt(const MatvecArgs& a, const TmaPlan& p, int sms, cudaS
 bool tma_matvec_supported(const MatvecArgs& a, int smem_optin) {
   if (a.fp32_act || a.M <= 0 || a.K <= 0) return false;
   TmaPlan p;
-  return tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, &p);
+  if (!tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, &p)) return false;
+  if (is_fused(a)) {
+    if (!a.scales_f16 || a.isums) return false;
+    if (a.epi == kEpiSwiglu && (p.R < 2 || a.M % 64 != 0)) return false;
+  }
+  return true;
 }
+
+bool matvec_is_fused(const MatvecArgs& a) { return is_fused(a); }
 
 cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl) {
   TmaPlan p;
@@ -532,6 +726,20 @@ cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cuda
 cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream) {
   return cudaMemcpyFromSymbolAsync(host_pinned, g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost,
                                    stream);
+}
+
+unsigned* device_error_word() {
+  static std::mutex mu;
+  static std::map<int, unsigned*> addr;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = addr.find(dev);
+  if (it != addr.end()) return it->second;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+  addr[dev] = static_cast<unsigned*>(p);
+  return static_cast<unsigned*>(p);
 }
 
 cudaError_t read_device_error(unsigned* out, bool clear) {

@@ -1,0 +1,301 @@
+"""Batch-1 Llama decode on one B200 through the fused C-ABI entries.
+
+The reference decodes one token at a time in
+``AsmEngineForward.forward_token`` (THRISHAL12345/asmllm
+src/runtime/generate.py:255-326) and picks the next token with a numpy
+argmax (generate.py:410-411).  ``LlamaDecoder`` runs the same step as five
+launches per layer plus one for the lm_head:
+
+  1. q/k/v matvec (rows [wq; wk; wv]) with RMSNorm + Q8_0 quantize in its
+     prologue (layer 0: the source row is the token's embedding, copied to
+     the residual stream x by CTA 0);
+  2. RoPE + fp16 KV append + attention, output quantized to a Q8_0 image;
+  3. o matvec from that image, residual add into x in its epilogue;
+  4. gate/up matvec (rows interleaved gate_0, up_0, gate_1, ...) with RMSNorm
+     in its prologue and silu(gate)*up + Q8_0 quantize in its epilogue;
+  5. down matvec from that image, residual add into x;
+  and the lm_head matvec with the final RMSNorm in its prologue and the
+  argmax in its epilogue, which writes the next token id and advances the
+  position.
+
+The position and the token ids live in device memory, so one captured CUDA
+graph of a step replays for every token with no host round trip.  Weights
+are random-init in GGUF Q4_0 (or Q8_0) form with fp16 scales, generated on
+the device from a seed; norm weights are 1 + N(0, 0.01) fp32.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import native, ops
+from .native import FMT_Q4_0, FMT_Q8_0, FusedMatvec
+
+
+@dataclass(frozen=True)
+class LlamaShape:
+    n_layers: int
+    dim: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    eps: float = 1e-5
+    theta: float = 10000.0
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.n_heads + 2 * self.n_kv_heads) * self.head_dim
+
+    def weight_bytes(self, fmt: int = FMT_Q4_0) -> int:
+        """GGUF-size bytes of every linear weight read per token (18 B or 34 B per block)."""
+        bb = 18 if fmt == FMT_Q4_0 else 34
+        per_layer = (self.qkv_rows * self.dim + self.dim * self.n_heads * self.head_dim
+                     + 2 * self.ffn * self.dim + self.dim * self.ffn) // 32 * bb
+        return self.n_layers * per_layer + self.vocab * self.dim // 32 * bb
+
+    def kv_bytes(self, pos: int) -> int:
+        """fp16 KV bytes the attention of one token at position pos reads (all layers)."""
+        return self.n_layers * 2 * (pos + 1) * self.n_kv_heads * self.head_dim * 2
+
+
+LLAMA_7B = LlamaShape(n_layers=32, dim=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000)
+LLAMA2_70B = LlamaShape(n_layers=80, dim=8192, n_heads=64, n_kv_heads=8, head_dim=128, ffn=28672, vocab=32000)
+
+
+def rope_table(ctx: int, head_dim: int, theta: float) -> np.ndarray:
+    """fp32 [ctx][head_dim/2][2] = (cos, sin) of pos * freq_i, computed with the
+    reference's numpy expressions (tests/reference/ops.py:125-128) in float32."""
+    freqs = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
+    angles = np.arange(ctx, dtype=np.float32)[:, None] * freqs[None, :]
+    assert freqs.dtype == np.float32 and angles.dtype == np.float32
+    return np.ascontiguousarray(np.stack([np.cos(angles), np.sin(angles)], axis=-1))
+
+
+def _random_weights(torch, fmt, M, K, gen, dev):
+    """GGUF-style random block weights: Q4_0 nibbles U[0,15] with d = |N(0,0.02)|,
+    or Q8_0 int8 U[-127,127] with d = |N(0,0.002)|; fp16 scales."""
+    nb = K // 32
+    if fmt == FMT_Q4_0:
+        qs = torch.randint(0, 256, (M, nb, 16), dtype=torch.uint8, device=dev, generator=gen)
+        d = torch.randn((M, nb), device=dev, generator=gen).abs_().mul_(0.02).half()
+    else:
+        qs = torch.randint(-127, 128, (M, nb, 32), dtype=torch.int8, device=dev, generator=gen)
+        d = torch.randn((M, nb), device=dev, generator=gen).abs_().mul_(0.002).half()
+    return qs, d
+
+
+class LlamaDecoder:
+    """Random-init Llama-style model resident on one GPU, decoded at batch 1."""
+
+    def __init__(self, shape: LlamaShape, ctx: int = 512, max_tokens: int | None = None, seed: int = 0,
+                 fmt: int = FMT_Q4_0, device=None):
+        import torch
+
+        self.torch = torch
+        self.shape = s = shape
+        self.fmt = fmt
+        self.ctx = ctx
+        self.max_tokens = max_tokens or ctx
+        if s.head_dim != 128:
+            raise ValueError("head_dim must be 128")
+        if s.dim % 256 or s.ffn % 256 or (s.n_heads * s.head_dim) % 256:
+            raise ValueError("dim, ffn and n_heads*head_dim must be multiples of 256 (whole fp16 scale rows)")
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        qdim = s.n_heads * s.head_dim
+        self.layers = []
+        for _ in range(s.n_layers):
+            L = {}
+            L["wqkv"] = _random_weights(torch, fmt, s.qkv_rows, s.dim, gen, dev)
+            L["wo"] = _random_weights(torch, fmt, s.dim, qdim, gen, dev)
+            g = _random_weights(torch, fmt, s.ffn, s.dim, gen, dev)
+            u = _random_weights(torch, fmt, s.ffn, s.dim, gen, dev)
+            # rows gate_0, up_0, gate_1, up_1, ...: a pair is finished by one warp
+            L["wgu"] = (torch.stack([g[0], u[0]], 1).reshape(2 * s.ffn, *g[0].shape[1:]).contiguous(),
+                        torch.stack([g[1], u[1]], 1).reshape(2 * s.ffn, g[1].shape[1]).contiguous())
+            del g, u
+            L["wdown"] = _random_weights(torch, fmt, s.dim, s.ffn, gen, dev)
+            L["attn_norm"] = 1.0 + 0.01 * torch.randn(s.dim, device=dev, generator=gen)
+            L["ffn_norm"] = 1.0 + 0.01 * torch.randn(s.dim, device=dev, generator=gen)
+            self.layers.append(L)
+        self.final_norm = 1.0 + 0.01 * torch.randn(s.dim, device=dev, generator=gen)
+        self.lm_head = _random_weights(torch, fmt, s.vocab, s.dim, gen, dev)
+        self.embed = torch.randn((s.vocab, s.dim), device=dev, generator=gen)
+        for L in self.layers:
+            for k in ("wqkv", "wo", "wgu", "wdown"):
+                ops.mark_static(*L[k])
+        ops.mark_static(*self.lm_head)
+
+        self.rope = torch.from_numpy(rope_table(ctx, s.head_dim, s.theta)).to(dev)
+        self.k_cache = torch.zeros((s.n_layers, ctx, s.n_kv_heads, s.head_dim), dtype=torch.float16, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.x = torch.zeros(s.dim, device=dev)
+        self.qkv = torch.zeros(s.qkv_rows, device=dev)
+        self.img_attn = torch.zeros(ops.act_image_bytes(qdim), dtype=torch.uint8, device=dev)
+        self.h = torch.zeros(s.ffn, device=dev)
+        self.img_h = torch.zeros(ops.act_image_bytes(s.ffn), dtype=torch.uint8, device=dev)
+        self.counters = torch.zeros(s.ffn // 32, dtype=torch.int32, device=dev)
+        self.logits = torch.zeros(s.vocab, device=dev)
+        self.best = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.tokens = torch.zeros(self.max_tokens, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        # the reference divides the scores by np.sqrt(head_dim, dtype=np.float32)
+        self.sqrt_hd = float(np.sqrt(np.float32(s.head_dim), dtype=np.float32))
+        self.n_prompt = 0
+        self._descs = None
+        self._graphs = {}
+
+    # ------------------------------------------------------------------ launches
+    def _mv(self, w, epi, M, K, **kw) -> FusedMatvec:
+        d = FusedMatvec()
+        d.fmt, d.epilogue = self.fmt, epi
+        d.qweights, d.scales = w[0].data_ptr(), w[1].data_ptr()
+        d.M, d.K = M, K
+        d.eps = self.shape.eps
+        d.vocab, d.max_tokens, d.n_prompt = self.shape.vocab, self.max_tokens, self.n_prompt
+        d.tokens, d.pos = self.tokens.data_ptr(), self.pos.data_ptr()
+        for k, v in kw.items():
+            setattr(d, k, v.data_ptr() if hasattr(v, "data_ptr") else v)
+        return d
+
+    def _build(self):
+        s = self.shape
+        qdim = s.n_heads * s.head_dim
+        kv_layer = s.n_kv_heads * s.head_dim * self.ctx
+        descs = []
+        for li, L in enumerate(self.layers):
+            src = dict(embed=self.embed, x_copy=self.x) if li == 0 else dict(x=self.x)
+            descs.append(("mv", self._mv(L["wqkv"], native.EPI_STORE, s.qkv_rows, s.dim,
+                                         norm_w=L["attn_norm"], y=self.qkv, **src)))
+            descs.append(("attn", (self.qkv.data_ptr(), self.k_cache.data_ptr() + 2 * li * kv_layer,
+                                   self.v_cache.data_ptr() + 2 * li * kv_layer, self.rope.data_ptr(),
+                                   self.pos.data_ptr(), self.img_attn.data_ptr(), s.n_heads, s.n_kv_heads,
+                                   s.head_dim, self.ctx, self.sqrt_hd)))
+            descs.append(("mv", self._mv(L["wo"], native.EPI_RESIDUAL, s.dim, qdim, image=self.img_attn, y=self.x)))
+            descs.append(("mv", self._mv(L["wgu"], native.EPI_SWIGLU, 2 * s.ffn, s.dim, x=self.x,
+                                         norm_w=L["ffn_norm"], y=self.h, h=self.h, image_out=self.img_h,
+                                         counters=self.counters)))
+            descs.append(("mv", self._mv(L["wdown"], native.EPI_RESIDUAL, s.dim, s.ffn, image=self.img_h, y=self.x)))
+        descs.append(("mv", self._mv(self.lm_head, native.EPI_ARGMAX, s.vocab, s.dim, x=self.x,
+                                     norm_w=self.final_norm, y=self.logits, best=self.best, done=self.done)))
+        self._descs = descs
+
+    @property
+    def launches_per_step(self) -> int:
+        return 5 * self.shape.n_layers + 1
+
+    def launch_step(self, stream=None):
+        """Enqueue one decode step (token at *pos -> logits, next token, pos+1)."""
+        if self._descs is None:
+            self._build()
+        L = native.lib()
+        st = ctypes.c_void_p(stream if stream is not None else self.torch.cuda.current_stream().cuda_stream)
+        for kind, d in self._descs:
+            if kind == "mv":
+                rc = L.asm_fused_matvec_async(ctypes.byref(d), st)
+            else:
+                rc = L.asm_attention_decode_async(*d, st)
+            if rc:
+                native.check(rc)
+
+    # ------------------------------------------------------------------ state
+    def reset(self, prompt) -> None:
+        """Loads the prompt ids; the next step runs position 0."""
+        prompt = [int(t) for t in prompt]
+        if not 1 <= len(prompt) <= self.max_tokens:
+            raise ValueError("prompt length must be in [1, max_tokens]")
+        if len(prompt) != self.n_prompt:  # n_prompt is part of the captured launches
+            self.n_prompt = len(prompt)
+            self._descs = None
+            self._graphs = {}
+        t = np.zeros(self.max_tokens, dtype=np.int32)
+        t[: len(prompt)] = prompt
+        self.tokens.copy_(self.torch.from_numpy(t))
+        self.pos.zero_()
+
+    def step(self, n: int = 1) -> None:
+        """n eager steps on the current stream."""
+        for _ in range(n):
+            self.launch_step()
+
+    def _graph(self, k: int):
+        g = self._graphs.get(k)
+        if g is None:
+            torch = self.torch
+            if self._descs is None:
+                self._build()
+            saved_pos = self.pos.clone()
+            saved_tok = self.tokens.clone()
+            self.launch_step()  # one eager step: per-kernel attributes and pointer kinds are cached
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(k):
+                    self.launch_step()
+            torch.cuda.synchronize()
+            self.pos.copy_(saved_pos)
+            self.tokens.copy_(saved_tok)
+            self._graphs[k] = g
+        return g
+
+    def run(self, n: int, chunk: int = 16) -> None:
+        """n steps by CUDA graph replay (graphs of `chunk` steps and of one step)."""
+        while n >= chunk:
+            self._graph(chunk).replay()
+            n -= chunk
+        for _ in range(n):
+            self._graph(1).replay()
+
+    def generate(self, prompt, n_new: int, chunk: int = 16) -> list[int]:
+        """Greedy decode: the prompt's positions, then n_new generated tokens."""
+        if len(prompt) + n_new > self.max_tokens:
+            raise ValueError("prompt + n_new exceeds max_tokens")
+        self.reset(prompt)
+        self.run(len(prompt) - 1 + n_new, chunk)
+        self.torch.cuda.synchronize()
+        return self.tokens[len(prompt): len(prompt) + n_new].cpu().tolist()
+
+    def position(self) -> int:
+        return int(self.pos.item())
+
+    # ------------------------------------------------------------------ export
+    def host_weights(self):
+        """Host copies in the reference ABI layout (qs + fp32 scales per matrix,
+        gate/up de-interleaved) for a CPU re-computation of the step."""
+        s = self.shape
+        qdim = s.n_heads * s.head_dim
+
+        def host(w):
+            return w[0].cpu().numpy(), w[1].float().cpu().numpy()
+
+        out = {"embed": self.embed.cpu().numpy(), "final_norm": self.final_norm.cpu().numpy(),
+               "lm_head": host(self.lm_head), "rope": self.rope.cpu().numpy(), "layers": []}
+        for L in self.layers:
+            q, sc = host(L["wqkv"])
+            gq, gs = host(L["wgu"])
+            kvr = s.n_kv_heads * s.head_dim
+            out["layers"].append({
+                "wq": (q[:qdim], sc[:qdim]), "wk": (q[qdim:qdim + kvr], sc[qdim:qdim + kvr]),
+                "wv": (q[qdim + kvr:], sc[qdim + kvr:]),
+                "wo": host(L["wo"]), "w_gate": (gq[0::2], gs[0::2]), "w_up": (gq[1::2], gs[1::2]),
+                "w_down": host(L["wdown"]),
+                "attn_norm": L["attn_norm"].cpu().numpy(), "ffn_norm": L["ffn_norm"].cpu().numpy(),
+            })
+        return out
+
+    def close(self):
+        for L in self.layers:
+            for k in ("wqkv", "wo", "wgu", "wdown"):
+                ops.unmark_static(*L[k])
+        ops.unmark_static(*self.lm_head)
+        self._graphs = {}
+
+
+__all__ = ["LlamaShape", "LLAMA_7B", "LLAMA2_70B", "LlamaDecoder", "rope_table", "FMT_Q4_0", "FMT_Q8_0"]

@@ -23,6 +23,24 @@ ASM_OK, ASM_E_INVALID, ASM_E_UNSUPPORTED, ASM_E_CUDA, ASM_E_NOT_DEVICE = 0, 1, 2
 FMT_Q4_0, FMT_Q8_0 = 2, 8
 
 vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+i32, f32 = ctypes.c_int32, ctypes.c_float
+
+# Epilogues of asm_fused_matvec_async (ASM_EPI_*) and device error bits.
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_ARGMAX = 0, 1, 2, 3
+DEVERR_RING_TIMEOUT, DEVERR_DECODE_RANGE = 1, 2
+
+
+class FusedMatvec(ctypes.Structure):
+    """asm_fused_matvec_t (include/asmllm.h), field for field."""
+    _fields_ = [
+        ("fmt", i32), ("epilogue", i32),
+        ("qweights", vp), ("scales", vp), ("x", vp), ("image", vp), ("norm_w", vp),
+        ("embed", vp), ("x_copy", vp), ("y", vp), ("h", vp), ("image_out", vp),
+        ("counters", vp), ("best", vp), ("done", vp), ("tokens", vp), ("pos", vp),
+        ("eps", f32), ("vocab", i32), ("max_tokens", i32), ("n_prompt", i32),
+        ("M", i64), ("K", i64),
+    ]
+
 
 # name -> (argtypes, restype); every symbol include/asmllm.h declares.
 SIGNATURES = {
@@ -63,6 +81,8 @@ SIGNATURES = {
     "asm_device_error": ([ctypes.POINTER(ctypes.c_uint)], c_int),
     "asm_set_option": ([ctypes.c_char_p, c_int], c_int),
     "asm_matmul_q4_noalloc_async": ([vp, vp, c_int, vp, vp, i64, i64, vp], c_int),
+    "asm_fused_matvec_async": ([ctypes.POINTER(FusedMatvec), vp], c_int),
+    "asm_attention_decode_async": ([vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp], c_int),
     "asm_max_k": ([c_int, c_int], i64),
     "asm_version": ([], ctypes.c_char_p),
 }

@@ -324,3 +324,38 @@ __all__ = [
     "block_sums_dev", "gguf_split_dev", "act_image_bytes", "act_image_dev", "matvec_image",
     "mark_static", "unmark_static", "device_error", "set_option",
 ]
+
+
+def fused_matvec(fmt: int, qweights, scales, epilogue: int, *, y, x=None, image=None, norm_w=None,
+                 eps: float = 1e-5, embed=None, x_copy=None, h=None, image_out=None, counters=None,
+                 best=None, done=None, tokens=None, pos=None, vocab: int = 0, max_tokens: int = 0,
+                 n_prompt: int = 0, stream=None):
+    """One decode-step matvec with its prologue / epilogue fusion (asm_fused_matvec_async).
+
+    epilogue: native.EPI_STORE, EPI_RESIDUAL (y += W x), EPI_SWIGLU (rows
+    interleaved gate/up -> h and its Q8_0 image) or EPI_ARGMAX (y = logits,
+    tokens[*pos + 1] = argmax, *pos += 1).  Scales must be fp16."""
+    torch = _torch()
+    _check_dev(scales, (torch.float16,), "scales")
+    M, K = scales.shape[0], scales.shape[1] * 32
+    d = native.FusedMatvec()
+    d.fmt, d.epilogue, d.M, d.K, d.eps = fmt, epilogue, M, K, eps
+    d.vocab, d.max_tokens, d.n_prompt = vocab, max_tokens, n_prompt
+    for name, t in (("qweights", qweights), ("scales", scales), ("x", x), ("image", image), ("norm_w", norm_w),
+                    ("embed", embed), ("x_copy", x_copy), ("y", y), ("h", h), ("image_out", image_out),
+                    ("counters", counters), ("best", best), ("done", done), ("tokens", tokens), ("pos", pos)):
+        if t is not None:
+            setattr(d, name, t.data_ptr())
+    native.check(native.lib().asm_fused_matvec_async(ctypes.byref(d), _stream_handle(stream)))
+    return y
+
+
+def attention_decode(qkv, k_cache, v_cache, rope_cs, pos, image_out, n_heads: int, n_kv_heads: int,
+                     ctx: int, sqrt_head_dim: float, stream=None):
+    """RoPE + fp16 KV append + attention at position *pos (asm_attention_decode_async)."""
+    L = native.lib()
+    rc = L.asm_attention_decode_async(_ptr(qkv), _ptr(k_cache), _ptr(v_cache), _ptr(rope_cs), _ptr(pos),
+                                      _ptr(image_out), n_heads, n_kv_heads, 128, ctx, sqrt_head_dim,
+                                      _stream_handle(stream))
+    native.check(rc)
+    return image_out

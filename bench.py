@@ -234,6 +234,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2000)
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true", help="skip per-shape / Q8 breakdown")
+    ap.add_argument("--decode-steps", type=int, default=128,
+                    help="greedy steps of the 7B batch-1 decode timed after the matvec sweep (0: skip)")
     ap.add_argument("--mode", choices=["image", "fused"], default="fused",
                     help="image: activation-quantize pre-pass kernel + matvec (2 launches per matvec); "
                          "fused: quantize inside the matvec (1 launch)")
@@ -458,6 +460,51 @@ def main():
         for hq, _, _, _ in host_w[c]:
             ops.unregister_weights(hq)
 
+    # ---- 7B Q4_0 batch-1 decode (the metric's second half) ----
+    decode = None
+    if args.decode_steps > 0:
+        from asmllm_b200 import decode as D
+
+        torch.cuda.empty_cache()
+        dec = D.LlamaDecoder(D.LLAMA_7B, ctx=512, seed=base + 7)
+        prompt = np.random.default_rng(base + 1).integers(0, D.LLAMA_7B.vocab, 16).tolist()
+        n_new = args.decode_steps
+        dec.generate(prompt, n_new)  # warm-up: captures the step graphs, runs every kernel
+        dec.reset(prompt)
+        dec.run(len(prompt) - 1)  # the prompt's positions
+        barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record()
+        dec.run(n_new)
+        d1.record()
+        d1.synchronize()
+        barrier()
+        dms = d0.elapsed_time(d1)
+        if world > 1:
+            t = torch.tensor([dms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dms = float(t.item())
+        gen_toks = dec.tokens[len(prompt):len(prompt) + n_new].cpu().tolist()
+        derr = ops.device_error()
+        wb = D.LLAMA_7B.weight_bytes()
+        kvb = sum(D.LLAMA_7B.kv_bytes(p) for p in range(len(prompt) - 1, len(prompt) - 1 + n_new)) / n_new
+        per_tok_s = dms / 1e3 / n_new
+        decode = {
+            "tokens_per_s": round(n_new * world / (dms / 1e3), 2),
+            "ms_per_token": round(dms / n_new, 4),
+            "model": "random-init Llama-7B shape (32 L, d 4096, 32 heads x 128, FFN 11008, vocab 32000), Q4_0 linear "
+                     "weights with fp16 scales, fp32 norms 1+N(0,0.01), fp16 KV cache ctx 512",
+            "prompt_tokens": len(prompt), "greedy_steps": n_new, "batch": 1,
+            "launches_per_token": dec.launches_per_step,
+            "launch": "CUDA graphs of 16 decode steps, PDL between kernels; position and token ids on the device",
+            "weight_bytes_per_token": wb, "kv_bytes_per_token_avg": round(kvb),
+            "achieved_GB/s": round((wb + kvb) / per_tok_s / 1e9, 1),
+            "first_tokens": gen_toks[:8], "device_error": derr,
+        }
+        dec.close()
+        del dec
+        torch.cuda.empty_cache()
+
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -514,6 +561,16 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if decode is not None:
+        decode["frac_of_measured_hbm"] = round(decode["achieved_GB/s"] / peak, 4)
+        decode["roofline_tokens_per_s"] = round(peak * 1e9 / (decode["weight_bytes_per_token"]
+                                                             + decode["kv_bytes_per_token_avg"]), 1)
+        if cpu is not None:  # labelled estimate: the reference decode driver is hard-wired to a 15M model
+            decode["reference_cpu_estimate_tokens_per_s"] = round(cpu["value"] * 1e9 / decode["weight_bytes_per_token"], 3)
+            decode["reference_cpu_estimate_basis"] = ("weight bytes per token / the cpu_baseline matvec GB/s "
+                                                      "(derived, not a measured reference decode)")
+        line["decode_7b"] = decode
+        line["gpu_launches_decode"] = decode["launches_per_token"] * decode["greedy_steps"] * world
     line.update(extras)
     print(json.dumps(line), flush=True)
     if world > 1:

@@ -237,6 +237,79 @@ ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* 
                                            int scales_are_f16, const float* x, float* y, int64_t M,
                                            int64_t K, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Batch-1 decode step on the GPU.  The reference runs one token through a
+ * Llama layer in AsmEngineForward.forward_token (src/runtime/generate.py:
+ * 255-326): asm_rmsnorm, three asm_matmul_q4, asm_rope per head, a numpy KV
+ * append and attention, asm_matmul_q4 (o), a residual add, asm_rmsnorm, two
+ * asm_matmul_q4 (gate, up), asm_silu_hadamard, asm_matmul_q4 (down), a
+ * residual add; then the final asm_rmsnorm and the lm_head product with a
+ * numpy argmax (generate.py:318-326, 410-411).  Here the same step is five
+ * launches per layer: every norm, residual, SwiGLU and argmax is fused into
+ * a matvec's prologue or epilogue, and RoPE + KV append + attention +
+ * quantization of its output is one kernel.  Device pointers, stream ordered,
+ * capturable in a CUDA graph after one call per shape; the position and the
+ * token ids live in device memory, so one captured step replays for every
+ * token.  No single counterpart in the reference (it composes the calls
+ * above from Python).
+ * ------------------------------------------------------------------------ */
+#define ASM_EPI_STORE 0    /* y[r] = v */
+#define ASM_EPI_RESIDUAL 1 /* y[r] += v (y = residual stream) */
+#define ASM_EPI_SWIGLU 2   /* rows (2i, 2i+1) = (gate_i, up_i) -> h_i = silu(gate_i)*up_i -> Q8_0 image */
+#define ASM_EPI_ARGMAX 3   /* y[r] = v; then tokens[*pos+1] = argmax_r y[r] and *pos += 1 */
+
+/* Device error word bits (asm_device_error). */
+#define ASM_DEVERR_RING_TIMEOUT 1u /* a shared-memory ring wait gave up */
+#define ASM_DEVERR_DECODE_RANGE 2u /* position >= ctx / max_tokens or token id >= vocab: step skipped */
+
+typedef struct asm_fused_matvec {
+  int32_t fmt;      /* 2 = Q4_0, 8 = Q8_0 */
+  int32_t epilogue; /* ASM_EPI_* */
+  const void* qweights;
+  const void* scales;   /* fp16 [M][K/32] */
+  /* Prologue: `image` (a Q8_0 activation image, asm_act_image_q8_0_async
+   * layout) is copied when set; else the fp32 source row -- embed[tokens[*pos]]
+   * when `embed` is set, else `x` -- is quantized, after RMSNorm
+   * ((x / sqrt(mean(x^2) + eps)) * norm_w, tests/reference/ops.py:103-116)
+   * when `norm_w` is set.  `x_copy`, when set, receives the source row (the
+   * residual stream of the first layer). */
+  const float* x;
+  const void* image;
+  const float* norm_w;
+  const float* embed; /* fp32 [vocab][K] */
+  float* x_copy;
+  float* y; /* [M]: output (STORE, ARGMAX: logits) or residual stream (RESIDUAL) */
+  float* h; /* SWIGLU: fp32 [M/2] */
+  void* image_out;    /* SWIGLU: Q8_0 image of h (K' = M/2) */
+  uint32_t* counters; /* SWIGLU: [M/64], zero before the first call, left zero */
+  uint64_t* best;     /* ARGMAX: zero before the first call, left zero */
+  uint32_t* done;     /* ARGMAX: zero before the first call, left zero */
+  int32_t* tokens;    /* [max_tokens]: prompt ids then generated ids */
+  int32_t* pos;       /* current position */
+  float eps;
+  int32_t vocab;
+  int32_t max_tokens;
+  int32_t n_prompt; /* ARGMAX writes tokens[p+1] only when p+1 >= n_prompt */
+  int64_t M, K;
+} asm_fused_matvec_t;
+
+/* One fused matvec of a decode step (see above).  Q4_0 / Q8_0 weights with
+ * fp16 scales; SWIGLU needs M % 64 == 0. */
+ASMLLM_API int asm_fused_matvec_async(const asm_fused_matvec_t* p, void* stream);
+
+/* RoPE + KV append + attention for position *pos of one layer, one CTA per
+ * query head (reference generate.py:281-296 with ops.py:119-141 RoPE):
+ *   qkv     fp32 [(n_heads + 2 n_kv_heads) * head_dim] (q, k, v heads)
+ *   k_cache, v_cache  fp16 [ctx][n_kv_heads][head_dim] (this layer)
+ *   rope_cs fp32 [ctx][head_dim/2][2] = (cos, sin) of pos * theta^(-2i/head_dim)
+ *   image_out  Q8_0 activation image of the attention output (K = n_heads*head_dim)
+ * scores = q.k / sqrt_head_dim (the reference divides by float32 sqrt(hd)).
+ * head_dim must be 128; n_heads a multiple of n_kv_heads (grouped KV). */
+ASMLLM_API int asm_attention_decode_async(const float* qkv, void* k_cache, void* v_cache,
+                                          const float* rope_cs, const int32_t* pos, void* image_out,
+                                          int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                          int32_t ctx, float sqrt_head_dim, void* stream);
+
 /* Kernel-path switches for testing and tuning; returns the previous value
  * (-1 for an unknown name).  "tma": 1 = Q8_0-activation matvecs use the
  * bulk-copy pipeline kernel where the shape allows (default), 0 = the

@@ -15,8 +15,12 @@ It imports the reference's own Python (no copy of it lives in this repo):
     of the large recipes are not stored: tests regenerate them from the same
     legacy RandomState stream and check the stored SHA-256 of the bytes.
 
-Outputs: reference_seed42.npz (small fixture, all arrays) and
-bench_recipes.npz (expected y vectors + input digests).
+  * tests/reference/ops.py:103-153 ref_rmsnorm / ref_rope / ref_softmax --
+    the decode-step glue of generate.py:255-326, on seeded inputs
+    (np.random.default_rng(7)) at the 7B shapes (dim 4096, head_dim 128).
+
+Outputs: reference_seed42.npz (small fixture, all arrays),
+bench_recipes.npz (expected y vectors + input digests) and decode_glue.npz.
 """
 from __future__ import annotations
 
@@ -90,7 +94,26 @@ def main() -> None:
     out["bench_qf_q8_y"] = ref_q8_matmul(q8, s8, x).astype(np.float32)
     out["bench_qf_sha"] = np.array([_sha(x), _sha(q4), _sha(s4), _sha(q8), _sha(s8)])
     np.savez_compressed(HERE / "bench_recipes.npz", **out)
-    print("wrote", HERE / "reference_seed42.npz", "and", HERE / "bench_recipes.npz")
+
+    from tests.reference.ops import ref_rmsnorm, ref_rope, ref_softmax  # noqa: E402
+    rng = np.random.default_rng(7)
+    g = {}
+    g["norm_x"] = (3.0 * rng.standard_normal(4096)).astype(np.float32)
+    g["norm_w"] = (1.0 + 0.01 * rng.standard_normal(4096)).astype(np.float32)
+    g["norm_y"] = ref_rmsnorm(g["norm_x"], g["norm_w"], eps=1e-5)
+    g["rope_pos"] = np.array([0, 1, 17, 142, 511], dtype=np.int64)
+    g["rope_q"] = rng.standard_normal((4, 128)).astype(np.float32)
+    g["rope_k"] = rng.standard_normal((4, 128)).astype(np.float32)
+    qs, ks = [], []
+    for p in g["rope_pos"]:
+        qr, kr = ref_rope(g["rope_q"], g["rope_k"], head_dim=128, pos=int(p), theta=10000.0)
+        qs.append(qr)
+        ks.append(kr)
+    g["rope_q_out"], g["rope_k_out"] = np.stack(qs), np.stack(ks)
+    g["softmax_x"] = (8.0 * rng.standard_normal(143)).astype(np.float32)
+    g["softmax_y"] = ref_softmax(g["softmax_x"])
+    np.savez_compressed(HERE / "decode_glue.npz", **g)
+    print("wrote", HERE / "reference_seed42.npz", HERE / "bench_recipes.npz", "and", HERE / "decode_glue.npz")
 
 
 if __name__ == "__main__":

@@ -38,6 +38,7 @@
 
 #include "common.cuh"
 #include "matvec.cuh"
+#include "pipeline.cuh"
 
 namespace asmllm {
 
@@ -45,100 +46,11 @@ __device__ unsigned int g_device_error;
 
 namespace {
 
-constexpr long long kWaitCycles = 2000000000LL;  // ~1 s at the B200 SM clock
 constexpr int kBarBytes = 256;                   // room for 2 x 8 mbarriers + abort flag
 constexpr int kPartBytes = 2 * 2 * 8 * 2 * 4;    // row partials [2 parities][2 warpgroups][8 warps][2 rows]
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile(
-      "{\n\t.reg .b64 st;\n\t"
-      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(bar),
-      "r"(bytes)
-      : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile(
-      "{\n\t.reg .b64 st;\n\t"
-      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
-      : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Waits for the phase with the given parity; false after kWaitCycles.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) return false;
-  }
-  return true;
-}
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
-      : "memory");
-}
-
-__device__ __forceinline__ void consumer_bar_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
-
-// Barrier over the 256 threads of warpgroup wg (named barrier 2 + wg) that
-// also ORs a flag across them: every warp gets the same answer.
-__device__ __forceinline__ bool wg_bar_or(int wg, bool v) {
-  unsigned r;
-  if (wg == 0)
-    asm volatile(
-        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.or.pred po, 2, 256, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
-        : "=r"(r)
-        : "r"((unsigned)v)
-        : "memory");
-  else
-    asm volatile(
-        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
-        "bar.red.or.pred po, 3, 256, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
-        : "=r"(r)
-        : "r"((unsigned)v)
-        : "memory");
-  return r != 0;
-}
-
 }  // namespace
 
-// Orderable 64-bit key of (value, row): larger value first, then lower row
-// (numpy.argmax returns the first maximum).
-__device__ __forceinline__ unsigned long long argmax_key(float v, int row) {
-  unsigned u = __float_as_uint(v);
-  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return ((unsigned long long)u << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)row);
-}
 
 // Called once per CTA (thread 0) after its rows' keys are folded into
 // fz.best: the last CTA to arrive turns the maximum into the next token,
@@ -148,7 +60,7 @@ __device__ void argmax_arrive(const MvFuse& fz, unsigned nctas) {
   if (atomicAdd(fz.done, 1u) != nctas - 1) return;
   __threadfence();
   const unsigned long long b = atomicExch(fz.best, 0ull);
-  const int idx = b ? (int)(0xFFFFFFFFu - (unsigned)(b & 0xFFFFFFFFull)) : 0;
+  const int idx = argmax_row(b);
   volatile int32_t* pos = fz.pos;
   const int p = *pos;
   if (p >= 0 && p + 1 < fz.max_tokens) {
@@ -164,8 +76,8 @@ __device__ void argmax_arrive(const MvFuse& fz, unsigned nctas) {
 // at the current position (out-of-range ids read row 0 and set an error bit).
 __device__ __forceinline__ const float* prologue_source(const MvFuse& fz, const void* act, int K) {
   if (fz.embed == nullptr) return static_cast<const float*>(act);
-  const int p = *fz.pos;
-  int tok = (p >= 0 && p < fz.max_tokens) ? fz.tokens[p] : -1;
+  const int p = __ldcg(fz.pos);
+  int tok = (p >= 0 && p < fz.max_tokens) ? __ldcg(fz.tokens + p) : -1;
   if (tok < 0 || tok >= fz.vocab) {
     if (threadIdx.x == 0) atomicOr(&g_device_error, kErrDecodeRange);
     tok = 0;
@@ -289,7 +201,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       // rms = sqrt(mean(x^2) + eps), one fixed-order sum shared by every thread.
       float ss = 0.0f;
       for (int i = threadIdx.x; i < nb * 8; i += NCT) {
-        const float4 v = reinterpret_cast<const float4*>(x)[i];
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(x) + i);
         ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
                                      __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
         if (copy) reinterpret_cast<float4*>(fz.x_copy)[i] = v;
@@ -303,7 +215,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * QK)), fz.eps));
     } else if (copy) {
       for (int i = threadIdx.x; i < nb * 8; i += NCT)
-        reinterpret_cast<float4*>(fz.x_copy)[i] = reinterpret_cast<const float4*>(x)[i];
+        reinterpret_cast<float4*>(fz.x_copy)[i] = __ldcg(reinterpret_cast<const float4*>(x) + i);
     }
 
     for (int base = 0; base < nb; base += 4 * BPP) {
@@ -311,7 +223,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
 #pragma unroll
       for (int p = 0; p < 4; ++p) {  // issue the loads of 4 passes before any use
         const int b = base + p * BPP + (threadIdx.x >> 3);
-        v[p] = b < nb ? reinterpret_cast<const float4*>(x + (size_t)b * QK)[lane8] : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[p] = b < nb ? __ldcg(reinterpret_cast<const float4*>(x + (size_t)b * QK) + lane8) : make_float4(0.f, 0.f, 0.f, 0.f);
         if (PRO == kProNorm && b < nb) {  // (x / rms) * w, as the reference RMSNorm
           const float4 nw = reinterpret_cast<const float4*>(fz.norm_w + (size_t)b * QK)[lane8];
           v[p] = make_float4(__fmul_rn(__fdiv_rn(v[p].x, rms), nw.x), __fmul_rn(__fdiv_rn(v[p].y, rms), nw.y),
@@ -343,7 +255,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   unsigned long long best_local = 0;  // kEpiArgmax: this lane's best (value, row)
   auto emit = [&](int row, float t) {
     if (EPI == kEpiResidual) {
-      y[row] = __fadd_rn(y[row], t);
+      y[row] = __fadd_rn(__ldcg(y + row), t);
     } else {
       y[row] = t;
       if (EPI == kEpiArgmax && t == t) {
@@ -353,35 +265,16 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     }
   };
   // Rows (row, row + 1) = (gate_i, up_i): h_i = silu(gate) * up, as the
-  // reference's (gate / (1 + exp(-gate))) * up.  The warp that completes the
-  // 32nd h of a block (arrival counter) quantizes that block into image_out.
+  // reference's (gate / (1 + exp(-gate))) * up; stored to fz.h as the rows
+  // finish.  The Q8_0 blocks of h are made after the stage loop.
   auto swiglu_emit = [&](int row, const float* pr) {
-    const int i = row >> 1;
-    int last = 0;
     if (lane == 0) {
       float g = pr[0], u = pr[1];
       for (int j = 1; j < WPG; ++j) {
         g += pr[j * 2];
         u += pr[j * 2 + 1];
       }
-      const float hv = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-      __stcg(fz.h + i, hv);
-      __threadfence();
-      last = atomicAdd(fz.counters + (i >> 5), 1u) == 31u;
-    }
-    last = __shfl_sync(kFull, last, 0);
-    if (last) {
-      __threadfence();
-      const int blk = i >> 5;
-      const float4 hv4 = __ldcg(reinterpret_cast<const float4*>(fz.h + (size_t)blk * QK) + (lane & 7));
-      float d;
-      int qsum;
-      const unsigned q = quantize_quad(hv4, d, qsum);
-      if (lane < 8) reinterpret_cast<unsigned*>(fz.image_out + (size_t)blk * 48)[lane] = q;
-      if (lane == 0) {
-        reinterpret_cast<float2*>(fz.image_out + (size_t)(M >> 6) * 48)[blk] = make_float2(d, __int_as_float(qsum));
-        fz.counters[blk] = 0u;
-      }
+      __stcg(fz.h + (row >> 1), __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u));
     }
   };
   for (int s = wg, k = 0; s < S; s += NWG, ++k) {
@@ -508,15 +401,61 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     }
   }
   if (EPI == kEpiArgmax) {
+    // CTA maximum (warp shuffles, then the warps' values in shared memory),
+    // one atomicMax per CTA, then the last CTA to arrive picks the token.
     unsigned long long b = best_local;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const unsigned long long t = __shfl_xor_sync(kFull, b, o);
       b = t > b ? t : b;
     }
-    if (lane == 0 && b) atomicMax(fz.best, b);
+    consumer_bar_sync(NCT);  // every warp is done with the row partials
+    unsigned long long* wbest = reinterpret_cast<unsigned long long*>(part);
+    if (lane == 0) wbest[warp] = b;
     consumer_bar_sync(NCT);
-    if (threadIdx.x == 0) argmax_arrive(fz, gridDim.x);
+    if (threadIdx.x == 0) {
+      unsigned long long m = 0;
+      for (int i = 0; i < NCW; ++i) m = wbest[i] > m ? wbest[i] : m;
+      if (m) atomicMax(fz.best, m);
+      argmax_arrive(fz, gridDim.x);
+    }
+  }
+  if (EPI == kEpiSwiglu) {
+    // This CTA's pairs [p0, p1) are in fz.h.  One release per CTA, then one
+    // arrival per Q8_0 block it touched (adding its pair count); the CTA whose
+    // arrival completes a block's 32 values quantizes that block.
+    const int p0 = r0 >> 1, p1 = r1 >> 1;
+    constexpr int kChunk = 64;
+    __shared__ int s_last[kChunk];
+    const int b0 = p0 >> 5, nblk = ((p1 + 31) >> 5) - b0;  // blocks touched
+    consumer_bar_sync(NCT);
+    for (int c0 = 0; c0 < nblk; c0 += kChunk) {
+      const int nc = min(kChunk, nblk - c0);
+      if (threadIdx.x == 0) {
+        __threadfence();
+        for (int i = 0; i < nc; ++i) {
+          const int blk = b0 + c0 + i;
+          const int n = min(p1, (blk + 1) * 32) - max(p0, blk * 32);
+          s_last[i] = atomicAdd(fz.counters + blk, (unsigned)n) + (unsigned)n == 32u;
+        }
+        __threadfence();
+      }
+      consumer_bar_sync(NCT);
+      for (int i = warp; i < nc; i += NCW) {  // a warp quantizes each block this CTA completed
+        if (!s_last[i]) continue;
+        const int blk = b0 + c0 + i;
+        const float4 hv4 = __ldcg(reinterpret_cast<const float4*>(fz.h + (size_t)blk * QK) + (lane & 7));
+        float d;
+        int qsum;
+        const unsigned q = quantize_quad(hv4, d, qsum);
+        if (lane < 8) reinterpret_cast<unsigned*>(fz.image_out + (size_t)blk * 48)[lane] = q;
+        if (lane == 0) {
+          reinterpret_cast<float2*>(fz.image_out + (size_t)(M >> 6) * 48)[blk] = make_float2(d, __int_as_float(qsum));
+          fz.counters[blk] = 0u;
+        }
+      }
+      consumer_bar_sync(NCT);  // s_last is reused by the next chunk
+    }
   }
 }
 
@@ -575,7 +514,7 @@ bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
   size_t ns = slots(budget);
   // Long rows (a large activation image plus big stages): take the whole
   // opt-in shared memory, one CTA per SM.
-  if (ns < 2 * nwg) ns = slots(budget = (size_t)smem_optin);
+  if (ns < 2 * nwg) ns = slots(budget = (size_t)smem_optin - 1024);  // room for static shared memory
   if (ns < 2 * nwg) return false;
   p->R = R;
   p->NS = (int)ns;
@@ -595,7 +534,11 @@ cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStr
     if (!g_tma_attr[key]) {
       int optin = 0;
       cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin);
+      cudaFuncAttributes fa;
+      cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+      if (e != cudaSuccess) return e;
+      // dynamic + static shared memory must fit the opt-in limit
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
       if (e != cudaSuccess) return e;
       // Full shared-memory carveout: room for the next matvec's CTA beside this one.
       e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, g_tma_carveout);

@@ -2,11 +2,16 @@
 
     python -m asmllm_b200.profdrive [--fmt q4|q8] [--mode fused|image] [--launches N]
                                     [--path tma|ldg] MxK [MxK ...]
+    python -m asmllm_b200.profdrive --decode N [--layers L] [--warm W]
 
 For each shape it builds one weight matrix on cuda:0 (random seeded quants,
 fp16 scales, declared static like model weights), then runs N matvecs
 (default 2) on torch's current stream.  Device memory stays at the size of
 the largest matrix, so an ncu capture of it ends quickly.
+
+--decode N builds the random-init Llama-7B-shaped decoder (L layers, default
+32: 4.2 GB on the device), runs W greedy steps through CUDA graphs (default
+24, to fill the KV cache), then N eager steps: 5 * L + 1 launches each.
 """
 from __future__ import annotations
 
@@ -20,12 +25,29 @@ from .native import FMT_Q4_0, FMT_Q8_0
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("shapes", nargs="+")
+    ap.add_argument("shapes", nargs="*")
+    ap.add_argument("--decode", type=int, default=0)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--warm", type=int, default=24)
     ap.add_argument("--fmt", choices=["q4", "q8"], default="q4")
     ap.add_argument("--mode", choices=["fused", "image"], default="fused")
     ap.add_argument("--launches", type=int, default=2)
     ap.add_argument("--path", choices=["tma", "ldg"], default="tma")
     args = ap.parse_args()
+    if args.decode:
+        from dataclasses import replace
+
+        from . import decode as D
+
+        dec = D.LlamaDecoder(replace(D.LLAMA_7B, n_layers=args.layers), ctx=512, seed=0)
+        dec.generate(list(range(1, 17)), args.warm)
+        dec.step(args.decode)
+        torch.cuda.synchronize()
+        err = ops.device_error()
+        print(f"profdrive: decode {args.layers} layers, {args.warm} graph steps + {args.decode} eager steps "
+              f"({dec.launches_per_step} launches each), position {dec.position()}, device error word {err}")
+        dec.close()
+        raise SystemExit(1 if err else 0)
     fmt = FMT_Q4_0 if args.fmt == "q4" else FMT_Q8_0
     ops.set_option("tma", 1 if args.path == "tma" else 0)
     dev = torch.device("cuda", 0)

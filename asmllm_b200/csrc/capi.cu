@@ -26,6 +26,7 @@
 #include <vector>
 
 #include "../../include/asmllm.h"
+#include "decode_persistent.cuh"
 #include "matvec.cuh"
 
 using namespace asmllm;
@@ -1043,6 +1044,201 @@ ASMLLM_API int asm_attention_decode_async(const float* qkv, void* k_cache, void*
                                                 g_opt_pdl.load() != 0);
   if (e == cudaErrorNotSupported) return set_error(ASM_E_UNSUPPORTED, "%s: ctx %d too long for shared memory", name, ctx);
   if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Persistent decode (decode_persistent.cu)
+// ---------------------------------------------------------------------------
+struct DecodeHandle {
+  int dev = 0;
+  int fmt = 0;
+  int sms = 0, per_sm = 0;
+  size_t smem = 0;
+  int n_ops = 0;
+  PersistOp* d_ops = nullptr;
+  unsigned* d_sync = nullptr;  // [0] barrier counter, [1] abort word
+  PersistArgs args;
+  int ctx = 0, max_tokens = 0;
+};
+
+int stage_rows(int fmt, int64_t K) {
+  const size_t row_w = (size_t)(K / 32) * (fmt == kFmtQ4_0 ? 16 : 32);
+  int R = 8;
+  while (R > 2 && (size_t)R * row_w > 16 * 1024) R /= 2;
+  return R;
+}
+
+// ctypes mirrors (asmllm_b200/native.py DecodeLayer, DecodeModel) rely on these layouts.
+static_assert(sizeof(asm_decode_layer_t) == 96, "asm_decode_layer_t layout");
+static_assert(sizeof(asm_decode_model_t) == 176 && offsetof(asm_decode_model_t, layers) == 48 &&
+                  offsetof(asm_decode_model_t, pos) == 168,
+              "asm_decode_model_t layout");
+
+ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
+  const char* name = "asm_decode_create";
+  if (!m || !handle) return set_error(ASM_E_INVALID, "%s: null argument", name);
+  *handle = nullptr;
+  if (m->fmt != kFmtQ4_0 && m->fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, m->fmt);
+  if (m->head_dim != 128) return set_error(ASM_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, m->head_dim);
+  if (m->n_layers <= 0 || m->n_heads <= 0 || m->n_kv_heads <= 0 || m->n_heads % m->n_kv_heads || m->vocab <= 0 ||
+      m->ctx <= 0 || m->max_tokens <= 1 || !m->layers)
+    return set_error(ASM_E_INVALID, "%s: bad model dimensions", name);
+  const int64_t qdim = (int64_t)m->n_heads * m->head_dim;
+  if (m->dim % 256 || m->ffn % 256 || qdim % 256)
+    return set_error(ASM_E_UNSUPPORTED, "%s: dim, ffn and n_heads*head_dim must be multiples of 256", name);
+  int rc;
+  auto dev16 = [&](const void* q, const char* what) -> int {
+    if ((rc = require_device(name, q, what))) return rc;
+    if ((uintptr_t)q % 16) return set_error(ASM_E_INVALID, "%s: %s must be 16-byte aligned", name, what);
+    return ASM_OK;
+  };
+  for (int l = 0; l < m->n_layers; ++l) {
+    const asm_decode_layer_t& L = m->layers[l];
+    const void* ptrs[] = {L.wqkv, L.sqkv, L.wo, L.so, L.wgu, L.sgu, L.wdown, L.sdown, L.attn_norm, L.ffn_norm, L.k_cache, L.v_cache};
+    for (const void* q : ptrs)
+      if ((rc = dev16(q, "a layer buffer"))) return rc;
+  }
+  const void* globals[] = {m->lm_head, m->lm_scales, m->final_norm, m->embed, m->rope_cs, m->x, m->qkv, m->img_attn,
+                           m->h, m->img_h, m->counters, m->logits, m->best, m->tokens, m->pos};
+  for (const void* q : globals)
+    if ((rc = dev16(q, "a model buffer"))) return rc;
+
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  int sms = 0, optin = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+
+  std::vector<PersistOp> ops;
+  auto mv = [&](const void* w, const void* sc, int M, int64_t K, int pro, int epi) {
+    PersistOp o;
+    o.kind = kOpMatvec;
+    o.pro = pro;
+    o.epi = epi;
+    o.M = M;
+    o.nb = (int)(K / 32);
+    o.R = stage_rows(m->fmt, K);
+    o.w = static_cast<const uint8_t*>(w);
+    o.s = static_cast<const __half*>(sc);
+    return o;
+  };
+  const int qkv_rows = (m->n_heads + 2 * m->n_kv_heads) * m->head_dim;
+  for (int l = 0; l < m->n_layers; ++l) {
+    const asm_decode_layer_t& L = m->layers[l];
+    PersistOp o = mv(L.wqkv, L.sqkv, qkv_rows, m->dim, kProNorm, kEpiStore);
+    o.from_embed = l == 0;
+    o.x = m->x;
+    o.norm_w = L.attn_norm;
+    o.y = m->qkv;
+    ops.push_back(o);
+    PersistOp at;
+    at.kind = kOpAttention;
+    at.first_of_step = l == 0;
+    at.kc = static_cast<__half*>(L.k_cache);
+    at.vc = static_cast<__half*>(L.v_cache);
+    ops.push_back(at);
+    o = mv(L.wo, L.so, m->dim, qdim, kProImage, kEpiResidual);
+    o.image = static_cast<const unsigned char*>(m->img_attn);
+    o.y = m->x;
+    ops.push_back(o);
+    o = mv(L.wgu, L.sgu, 2 * m->ffn, m->dim, kProNorm, kEpiSwiglu);
+    o.x = m->x;
+    o.norm_w = L.ffn_norm;
+    ops.push_back(o);
+    o = mv(L.wdown, L.sdown, m->dim, m->ffn, kProImage, kEpiResidual);
+    o.image = static_cast<const unsigned char*>(m->img_h);
+    o.y = m->x;
+    ops.push_back(o);
+  }
+  PersistOp lm = mv(m->lm_head, m->lm_scales, m->vocab, m->dim, kProNorm, kEpiArgmax);
+  lm.x = m->x;
+  lm.norm_w = m->final_norm;
+  lm.y = m->logits;
+  ops.push_back(lm);
+
+  DecodeHandle* hd = new DecodeHandle();
+  hd->dev = dev;
+  hd->fmt = m->fmt;
+  hd->sms = sms;
+  hd->n_ops = (int)ops.size();
+  hd->ctx = m->ctx;
+  hd->max_tokens = m->max_tokens;
+  PersistArgs& a = hd->args;
+  a.n_ops = hd->n_ops;
+  a.eps = m->eps;
+  a.sqrt_hd = m->sqrt_head_dim;
+  a.embed = m->embed;
+  a.vocab = m->vocab;
+  a.rope = reinterpret_cast<const float2*>(m->rope_cs);
+  a.ctx = m->ctx;
+  a.n_heads = m->n_heads;
+  a.n_kv = m->n_kv_heads;
+  a.x = m->x;
+  a.qkv = m->qkv;
+  a.img_attn = static_cast<unsigned char*>(m->img_attn);
+  a.h = m->h;
+  a.img_h = static_cast<unsigned char*>(m->img_h);
+  a.counters = m->counters;
+  a.best = reinterpret_cast<unsigned long long*>(m->best);
+  a.tokens = m->tokens;
+  a.pos = m->pos;
+  a.max_tokens = m->max_tokens;
+  a.err = device_error_word();
+  if (!persist_plan(a, ops, m->fmt, optin, &hd->per_sm, &hd->smem)) {
+    delete hd;
+    return set_error(ASM_E_UNSUPPORTED, "%s: no shared-memory plan for these widths", name);
+  }
+  if (!a.err) {
+    delete hd;
+    return set_error(ASM_E_CUDA, "%s: device error word unavailable", name);
+  }
+  e = cudaMalloc(&hd->d_ops, ops.size() * sizeof(PersistOp));
+  if (e == cudaSuccess) e = cudaMalloc(&hd->d_sync, 2 * sizeof(unsigned));
+  if (e == cudaSuccess) e = cudaMemcpy(hd->d_ops, ops.data(), ops.size() * sizeof(PersistOp), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(hd->d_ops);
+    cudaFree(hd->d_sync);
+    delete hd;
+    return cuda_error(e, name);
+  }
+  a.ops = hd->d_ops;
+  a.sync = hd->d_sync;
+  a.abort = hd->d_sync + 1;
+  *handle = hd;
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_decode_run_async(void* handle, int32_t n_steps, int32_t n_prompt, void* stream) {
+  const char* name = "asm_decode_run_async";
+  DecodeHandle* hd = static_cast<DecodeHandle*>(handle);
+  if (!hd) return set_error(ASM_E_INVALID, "%s: null handle", name);
+  if (n_steps <= 0 || n_steps > hd->ctx || n_prompt < 0)
+    return set_error(ASM_E_INVALID, "%s: need 0 < n_steps <= ctx and n_prompt >= 0", name);
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != hd->dev) return set_error(ASM_E_INVALID, "%s: handle belongs to device %d, current is %d", name, hd->dev, cur);
+  PersistArgs a = hd->args;
+  a.n_steps = n_steps;
+  a.n_prompt = n_prompt;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(hd->d_sync, 0, 2 * sizeof(unsigned), st);
+  if (e == cudaSuccess) e = launch_decode_persistent(a, hd->fmt, hd->smem, hd->sms, hd->per_sm, st);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_decode_destroy(void* handle) {
+  DecodeHandle* hd = static_cast<DecodeHandle*>(handle);
+  if (!hd) return ASM_OK;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  cudaSetDevice(hd->dev);
+  cudaFree(hd->d_ops);
+  cudaFree(hd->d_sync);
+  cudaSetDevice(cur);
+  delete hd;
   return ASM_OK;
 }
 

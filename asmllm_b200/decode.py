@@ -19,7 +19,11 @@ launches per layer plus one for the lm_head:
   position.
 
 The position and the token ids live in device memory, so one captured CUDA
-graph of a step replays for every token with no host round trip.  Weights
+graph of a step replays for every token with no host round trip.  The
+default engine goes further: the same program runs as ONE persistent
+cooperative kernel for all the steps of a run (asm_decode_run_async), each CTA
+streaming its share of every weight matrix through a shared-memory ring
+without stopping between operations; the two engines agree bit for bit.  Weights
 are random-init in GGUF Q4_0 (or Q8_0) form with fp16 scales, generated on
 the device from a seed; norm weights are 1 + N(0, 0.01) fp32.
 """
@@ -142,7 +146,7 @@ class LlamaDecoder:
         self.img_h = torch.zeros(ops.act_image_bytes(s.ffn), dtype=torch.uint8, device=dev)
         self.counters = torch.zeros(s.ffn // 32, dtype=torch.int32, device=dev)
         self.logits = torch.zeros(s.vocab, device=dev)
-        self.best = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.best = torch.zeros(2, dtype=torch.int64, device=dev)
         self.done = torch.zeros(1, dtype=torch.int32, device=dev)
         self.tokens = torch.zeros(self.max_tokens, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -151,6 +155,7 @@ class LlamaDecoder:
         self.n_prompt = 0
         self._descs = None
         self._graphs = {}
+        self._handle = None
 
     # ------------------------------------------------------------------ launches
     def _mv(self, w, epi, M, K, **kw) -> FusedMatvec:
@@ -245,20 +250,61 @@ class LlamaDecoder:
             self._graphs[k] = g
         return g
 
-    def run(self, n: int, chunk: int = 16) -> None:
-        """n steps by CUDA graph replay (graphs of `chunk` steps and of one step)."""
+    def _persistent(self):
+        if self._handle is None:
+            s = self.shape
+            L = native.lib()
+            layers = (native.DecodeLayer * s.n_layers)()
+            kv_layer = s.n_kv_heads * s.head_dim * self.ctx * 2  # bytes of one layer's cache
+            for i, W in enumerate(self.layers):
+                layers[i] = native.DecodeLayer(
+                    W["wqkv"][0].data_ptr(), W["wqkv"][1].data_ptr(), W["wo"][0].data_ptr(), W["wo"][1].data_ptr(),
+                    W["wgu"][0].data_ptr(), W["wgu"][1].data_ptr(), W["wdown"][0].data_ptr(), W["wdown"][1].data_ptr(),
+                    W["attn_norm"].data_ptr(), W["ffn_norm"].data_ptr(),
+                    self.k_cache.data_ptr() + i * kv_layer, self.v_cache.data_ptr() + i * kv_layer)
+            m = native.DecodeModel()
+            m.fmt, m.n_layers, m.dim, m.n_heads, m.n_kv_heads = self.fmt, s.n_layers, s.dim, s.n_heads, s.n_kv_heads
+            m.head_dim, m.ffn, m.vocab, m.ctx, m.max_tokens = s.head_dim, s.ffn, s.vocab, self.ctx, self.max_tokens
+            m.eps, m.sqrt_head_dim = s.eps, self.sqrt_hd
+            m.layers = layers
+            m.lm_head, m.lm_scales = self.lm_head[0].data_ptr(), self.lm_head[1].data_ptr()
+            for name in ("final_norm", "embed"):
+                setattr(m, name, getattr(self, name).data_ptr())
+            m.rope_cs = self.rope.data_ptr()
+            for name, t in (("x", self.x), ("qkv", self.qkv), ("img_attn", self.img_attn), ("h", self.h),
+                            ("img_h", self.img_h), ("counters", self.counters), ("logits", self.logits),
+                            ("best", self.best), ("tokens", self.tokens), ("pos", self.pos)):
+                setattr(m, name, t.data_ptr())
+            h = ctypes.c_void_p()
+            native.check(L.asm_decode_create(ctypes.byref(m), ctypes.byref(h)))
+            self._handle = h
+        return self._handle
+
+    def run(self, n: int, chunk: int = 16, engine: str = "persistent") -> None:
+        """n decode steps.  engine "persistent": one cooperative launch for all
+        n steps; "graph": CUDA graphs of `chunk` steps (and of one step) of the
+        per-operation launches."""
+        if n <= 0:
+            return
+        if engine == "persistent":
+            h = self._persistent()
+            st = ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
+            native.check(native.lib().asm_decode_run_async(h, n, self.n_prompt, st))
+            return
+        if engine != "graph":
+            raise ValueError(f"unknown engine {engine!r}")
         while n >= chunk:
             self._graph(chunk).replay()
             n -= chunk
         for _ in range(n):
             self._graph(1).replay()
 
-    def generate(self, prompt, n_new: int, chunk: int = 16) -> list[int]:
+    def generate(self, prompt, n_new: int, chunk: int = 16, engine: str = "persistent") -> list[int]:
         """Greedy decode: the prompt's positions, then n_new generated tokens."""
         if len(prompt) + n_new > self.max_tokens:
             raise ValueError("prompt + n_new exceeds max_tokens")
         self.reset(prompt)
-        self.run(len(prompt) - 1 + n_new, chunk)
+        self.run(len(prompt) - 1 + n_new, chunk, engine)
         self.torch.cuda.synchronize()
         return self.tokens[len(prompt): len(prompt) + n_new].cpu().tolist()
 
@@ -291,6 +337,9 @@ class LlamaDecoder:
         return out
 
     def close(self):
+        if self._handle is not None:
+            native.lib().asm_decode_destroy(self._handle)
+            self._handle = None
         for L in self.layers:
             for k in ("wqkv", "wo", "wgu", "wdown"):
                 ops.unmark_static(*L[k])

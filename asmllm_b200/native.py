@@ -42,6 +42,21 @@ class FusedMatvec(ctypes.Structure):
     ]
 
 
+class DecodeLayer(ctypes.Structure):
+    """asm_decode_layer_t (include/asmllm.h)."""
+    _fields_ = [(n, vp) for n in ("wqkv", "sqkv", "wo", "so", "wgu", "sgu", "wdown", "sdown",
+                                  "attn_norm", "ffn_norm", "k_cache", "v_cache")]
+
+
+class DecodeModel(ctypes.Structure):
+    """asm_decode_model_t (include/asmllm.h)."""
+    _fields_ = ([(n, i32) for n in ("fmt", "n_layers", "dim", "n_heads", "n_kv_heads", "head_dim", "ffn", "vocab",
+                                     "ctx", "max_tokens")]
+                + [("eps", f32), ("sqrt_head_dim", f32), ("layers", ctypes.POINTER(DecodeLayer))]
+                + [(n, vp) for n in ("lm_head", "lm_scales", "final_norm", "embed", "rope_cs", "x", "qkv", "img_attn",
+                                     "h", "img_h", "counters", "logits", "best", "tokens", "pos")])
+
+
 # name -> (argtypes, restype); every symbol include/asmllm.h declares.
 SIGNATURES = {
     # reference ABI
@@ -83,6 +98,9 @@ SIGNATURES = {
     "asm_matmul_q4_noalloc_async": ([vp, vp, c_int, vp, vp, i64, i64, vp], c_int),
     "asm_fused_matvec_async": ([ctypes.POINTER(FusedMatvec), vp], c_int),
     "asm_attention_decode_async": ([vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp], c_int),
+    "asm_decode_create": ([ctypes.POINTER(DecodeModel), ctypes.POINTER(vp)], c_int),
+    "asm_decode_run_async": ([vp, i32, i32, vp], c_int),
+    "asm_decode_destroy": ([vp], c_int),
     "asm_max_k": ([c_int, c_int], i64),
     "asm_version": ([], ctypes.c_char_p),
 }

@@ -310,6 +310,62 @@ ASMLLM_API int asm_attention_decode_async(const float* qkv, void* k_cache, void*
                                           int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                           int32_t ctx, float sqrt_head_dim, void* stream);
 
+/* The whole decode loop as one persistent kernel.  asm_decode_create builds
+ * the per-step program of a resident model (the operations above, in
+ * order); asm_decode_run_async then runs n_steps decode steps in ONE
+ * cooperative launch: CTAs stay resident for all steps, each streams its
+ * share of every weight matrix through a shared-memory ring without stopping
+ * between operations, and operations are separated by a grid barrier (a
+ * bounded device-side counter wait).  Same arithmetic, bit for bit, as the
+ * per-operation entries.  Step s runs position *pos + s; its token is
+ * tokens[pos] while pos < n_prompt (and for the first step), else the argmax
+ * of the step before; generated ids are stored in tokens[] and *pos is
+ * advanced by n_steps.  The run is refused on the device (error bit
+ * ASM_DEVERR_DECODE_RANGE, nothing done) if it would pass ctx or max_tokens.
+ * Weights: fp16 scales; gate/up rows interleaved (gate_0, up_0, gate_1, ...);
+ * q/k/v rows stacked [wq; wk; wv].  No counterpart in the reference. */
+typedef struct asm_decode_layer {
+  const void* wqkv;
+  const void* sqkv; /* [(n_heads + 2 n_kv_heads) * head_dim][dim/32] */
+  const void* wo;
+  const void* so; /* [dim][n_heads * head_dim / 32] */
+  const void* wgu;
+  const void* sgu; /* [2 ffn][dim/32] */
+  const void* wdown;
+  const void* sdown; /* [dim][ffn/32] */
+  const float* attn_norm;
+  const float* ffn_norm; /* [dim] */
+  void* k_cache;
+  void* v_cache; /* fp16 [ctx][n_kv_heads][head_dim] */
+} asm_decode_layer_t;
+
+typedef struct asm_decode_model {
+  int32_t fmt; /* 2 = Q4_0, 8 = Q8_0 */
+  int32_t n_layers, dim, n_heads, n_kv_heads, head_dim, ffn, vocab, ctx, max_tokens;
+  float eps, sqrt_head_dim;
+  const asm_decode_layer_t* layers; /* host array [n_layers], copied by create */
+  const void* lm_head;
+  const void* lm_scales; /* [vocab][dim/32] */
+  const float* final_norm;
+  const float* embed;   /* fp32 [vocab][dim] */
+  const float* rope_cs; /* fp32 [ctx][head_dim/2][2] */
+  /* work buffers (device): */
+  float* x;          /* [dim] residual stream */
+  float* qkv;        /* [(n_heads + 2 n_kv_heads) * head_dim] */
+  void* img_attn;    /* asm_act_image_bytes(n_heads * head_dim) */
+  float* h;          /* [ffn] */
+  void* img_h;       /* asm_act_image_bytes(ffn) */
+  uint32_t* counters; /* [ffn/32], zero */
+  float* logits;     /* [vocab] */
+  uint64_t* best;    /* [2], zero */
+  int32_t* tokens;   /* [max_tokens] */
+  int32_t* pos;      /* [1] */
+} asm_decode_model_t;
+
+ASMLLM_API int asm_decode_create(const asm_decode_model_t* model, void** handle);
+ASMLLM_API int asm_decode_run_async(void* handle, int32_t n_steps, int32_t n_prompt, void* stream);
+ASMLLM_API int asm_decode_destroy(void* handle);
+
 /* Kernel-path switches for testing and tuning; returns the previous value
  * (-1 for an unknown name).  "tma": 1 = Q8_0-activation matvecs use the
  * bulk-copy pipeline kernel where the shape allows (default), 0 = the

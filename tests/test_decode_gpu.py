@@ -327,3 +327,64 @@ def test_position_out_of_range_sets_error_and_skips(cuda):
         assert len(toks) == 3 and ops.device_error() == 0
     finally:
         dec.close()
+
+
+# ---------------------------------------------------------------- persistent engine
+@pytest.mark.parametrize("shape", [SMALL, SMALL_GQA], ids=["mha", "gqa"])
+def test_persistent_engine_equals_per_launch_engine(cuda, shape):
+    torch = cuda
+    dec = D.LlamaDecoder(shape, ctx=64, seed=15)
+    try:
+        prompt = [5, 600, 7, 8]
+        g = dec.generate(prompt, 14, engine="graph")
+        lg = dec.logits.clone()
+        kc = dec.k_cache.clone()
+        p = dec.generate(prompt, 14, engine="persistent")
+        assert p == g
+        assert torch.equal(dec.logits, lg)
+        assert torch.equal(dec.k_cache[:, :17], kc[:, :17])
+        assert dec.position() == 17 and ops.device_error() == 0
+        # the same steps split over several launches
+        dec.reset(prompt)
+        for n in (1, 4, 12):
+            dec.run(n)
+        torch.cuda.synchronize()
+        assert dec.tokens[4:18].cpu().tolist() == p and torch.equal(dec.logits, lg)
+        assert not dec.best.any() and not dec.counters.any()
+    finally:
+        dec.close()
+
+
+def test_persistent_engine_7b_shapes_matches_oracle(cuda, DO):
+    torch = cuda
+    shape = D.LlamaShape(n_layers=2, dim=4096, n_heads=32, n_kv_heads=32, head_dim=128, ffn=11008, vocab=32000)
+    dec = D.LlamaDecoder(shape, ctx=16, seed=13)
+    try:
+        prompt = [31999, 0, 12345]
+        toks = dec.generate(prompt, 3, engine="persistent")
+        lg = dec.logits.cpu().numpy().copy()
+        assert dec.generate(prompt, 3, engine="graph") == toks
+        np.testing.assert_array_equal(dec.logits.cpu().numpy(), lg)
+        orc = DO.DecodeOracle(shape, dec.host_weights(), ctx=16)
+        _, ol = orc.generate(prompt, 3, forced=toks)
+        assert rel_err(lg, ol[-1]) <= WIDE_DECODE_TOL
+        assert ops.device_error() == 0
+    finally:
+        dec.close()
+
+
+def test_persistent_engine_refuses_runs_past_the_cache(cuda):
+    torch = cuda
+    dec = D.LlamaDecoder(SMALL, ctx=8, seed=16)
+    try:
+        dec.generate([1, 2], 3)  # position 4 afterwards
+        assert ops.device_error() == 0
+        dec.run(5)  # would need positions 4..8: refused on the device, nothing done
+        torch.cuda.synchronize()
+        assert ops.device_error() & native.DEVERR_DECODE_RANGE
+        assert dec.position() == 4
+        dec.run(3)  # positions 4..6 fit (the last id lands in tokens[7])
+        torch.cuda.synchronize()
+        assert dec.position() == 7 and ops.device_error() == 0
+    finally:
+        dec.close()

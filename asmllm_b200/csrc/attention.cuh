@@ -96,7 +96,7 @@ __device__ __forceinline__ float attn_block_reduce(float v, float* red, bool is_
 template <int NT, class Sync>
 __device__ void attention_head(const float* qkv, __half* kc, __half* vc, const float2* rope_cs, int pos, int h,
                                int n_heads, int n_kv, float sqrt_hd, unsigned char* image, const AttnSmem& sm,
-                               int tid, Sync sync) {
+                               int tid, Sync sync, int n_rep = 1, size_t rep_stride = 0) {
   static_assert(NT == 256, "attention is laid out for 256 working threads");
   constexpr int kSlices = NT / 16;  // position slices of P.V (16 groups of 8 dims each)
   const int warp = tid >> 5, lane = tid & 31;
@@ -216,8 +216,11 @@ __device__ void attention_head(const float* qkv, __half* kc, __half* vc, const f
     const unsigned q = quantize_quad(o, d, qsum);
     const int nb = n_heads * (kAttnHd / QK);
     const int blk = h * (kAttnHd / QK) + b;
-    reinterpret_cast<unsigned*>(image + (size_t)blk * 48)[l8] = q;
-    if (l8 == 0) reinterpret_cast<float2*>(image + (size_t)nb * 48)[blk] = make_float2(d, __int_as_float(qsum));
+    for (int r = 0; r < n_rep; ++r) {  // identical replicas (see the persistent decode kernel)
+      unsigned char* im = image + (size_t)r * rep_stride;
+      reinterpret_cast<unsigned*>(im + (size_t)blk * 48)[l8] = q;
+      if (l8 == 0) reinterpret_cast<float2*>(im + (size_t)nb * 48)[blk] = make_float2(d, __int_as_float(qsum));
+    }
   }
 }
 

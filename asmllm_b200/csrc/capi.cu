@@ -1058,6 +1058,7 @@ struct DecodeHandle {
   int n_ops = 0;
   PersistOp* d_ops = nullptr;
   unsigned* d_sync = nullptr;  // [0] barrier counter, [1] abort word
+  unsigned char* d_rep = nullptr;  // replicated x and activation images
   PersistArgs args;
   int ctx = 0, max_tokens = 0;
 };
@@ -1111,6 +1112,19 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
 
+  // Replicated activations of the persistent kernel: x [xr][dim], then the
+  // two images [xr][bytes] (each replica 16-byte aligned).
+  int xr = 1;  // measured: 8 replicas were no faster than 1 on B200
+  if (const char* ev = getenv("ASMLLM_DECODE_XR")) xr = std::max(1, std::min(64, atoi(ev)));
+  const size_t x_bytes = (size_t)m->dim * sizeof(float);
+  const size_t ia_bytes = act_image_bytes(qdim / 32), ih_bytes = act_image_bytes(m->ffn / 32);
+  unsigned char* d_rep = nullptr;
+  e = cudaMalloc(&d_rep, (size_t)xr * (x_bytes + ia_bytes + ih_bytes));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  float* x_rep = reinterpret_cast<float*>(d_rep);
+  unsigned char* ia_rep = d_rep + (size_t)xr * x_bytes;
+  unsigned char* ih_rep = ia_rep + (size_t)xr * ia_bytes;
+
   std::vector<PersistOp> ops;
   auto mv = [&](const void* w, const void* sc, int M, int64_t K, int pro, int epi) {
     PersistOp o;
@@ -1129,7 +1143,7 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
     const asm_decode_layer_t& L = m->layers[l];
     PersistOp o = mv(L.wqkv, L.sqkv, qkv_rows, m->dim, kProNorm, kEpiStore);
     o.from_embed = l == 0;
-    o.x = m->x;
+    o.x = x_rep;
     o.norm_w = L.attn_norm;
     o.y = m->qkv;
     ops.push_back(o);
@@ -1140,20 +1154,22 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
     at.vc = static_cast<__half*>(L.v_cache);
     ops.push_back(at);
     o = mv(L.wo, L.so, m->dim, qdim, kProImage, kEpiResidual);
-    o.image = static_cast<const unsigned char*>(m->img_attn);
-    o.y = m->x;
+    o.image = ia_rep;
+    o.image_stride = ia_bytes;
+    o.y = x_rep;
     ops.push_back(o);
     o = mv(L.wgu, L.sgu, 2 * m->ffn, m->dim, kProNorm, kEpiSwiglu);
-    o.x = m->x;
+    o.x = x_rep;
     o.norm_w = L.ffn_norm;
     ops.push_back(o);
     o = mv(L.wdown, L.sdown, m->dim, m->ffn, kProImage, kEpiResidual);
-    o.image = static_cast<const unsigned char*>(m->img_h);
-    o.y = m->x;
+    o.image = ih_rep;
+    o.image_stride = ih_bytes;
+    o.y = x_rep;
     ops.push_back(o);
   }
   PersistOp lm = mv(m->lm_head, m->lm_scales, m->vocab, m->dim, kProNorm, kEpiArgmax);
-  lm.x = m->x;
+  lm.x = x_rep;
   lm.norm_w = m->final_norm;
   lm.y = m->logits;
   ops.push_back(lm);
@@ -1175,11 +1191,16 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
   a.ctx = m->ctx;
   a.n_heads = m->n_heads;
   a.n_kv = m->n_kv_heads;
-  a.x = m->x;
+  a.xr = xr;
+  a.x_stride = (size_t)m->dim;
+  a.img_attn_stride = ia_bytes;
+  a.img_h_stride = ih_bytes;
+  a.x = x_rep;
   a.qkv = m->qkv;
-  a.img_attn = static_cast<unsigned char*>(m->img_attn);
+  a.img_attn = ia_rep;
   a.h = m->h;
-  a.img_h = static_cast<unsigned char*>(m->img_h);
+  a.img_h = ih_rep;
+  hd->d_rep = d_rep;
   a.counters = m->counters;
   a.best = reinterpret_cast<unsigned long long*>(m->best);
   a.tokens = m->tokens;
@@ -1187,10 +1208,12 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
   a.max_tokens = m->max_tokens;
   a.err = device_error_word();
   if (!persist_plan(a, ops, m->fmt, optin, &hd->per_sm, &hd->smem)) {
+    cudaFree(d_rep);
     delete hd;
     return set_error(ASM_E_UNSUPPORTED, "%s: no shared-memory plan for these widths", name);
   }
   if (!a.err) {
+    cudaFree(d_rep);
     delete hd;
     return set_error(ASM_E_CUDA, "%s: device error word unavailable", name);
   }
@@ -1200,6 +1223,7 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
   if (e != cudaSuccess) {
     cudaFree(hd->d_ops);
     cudaFree(hd->d_sync);
+    cudaFree(d_rep);
     delete hd;
     return cuda_error(e, name);
   }
@@ -1237,6 +1261,7 @@ ASMLLM_API int asm_decode_destroy(void* handle) {
   cudaSetDevice(hd->dev);
   cudaFree(hd->d_ops);
   cudaFree(hd->d_sync);
+  cudaFree(hd->d_rep);
   cudaSetDevice(cur);
   delete hd;
   return ASM_OK;

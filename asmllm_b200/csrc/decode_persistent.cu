@@ -53,6 +53,7 @@ constexpr int kNCT = kNCW * 32;          // consumer threads
 constexpr int kThreads = kNCT + 32;      // + 1 producer warp
 constexpr int kBarBytesP = 256;          // 2 x 8 ring mbarriers (full, empty) + flags
 constexpr int kPartBytesP = 2 * 2 * 8 * 2 * 4;
+constexpr int kNormRegs = 2;  // float4s of x per consumer thread held in registers (K <= 4096)
 
 struct ConsumerSync {
   __device__ __forceinline__ void operator()() const { consumer_bar_sync(kNCT); }
@@ -75,6 +76,12 @@ __device__ __forceinline__ bool consumers_or(bool v) {
       : "r"((unsigned)v), "r"(kNCT)
       : "memory");
   return r != 0;
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
@@ -207,14 +214,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
     consumer_bar_sync(kNCT);
     return s_flag[fi] != 0;
   };
-  // Every consumer's writes of this operation are done; one decision for the
-  // whole CTA on whether to go on (a warpgroup may have stopped alone).
+  // Every consumer's writes of this operation are done (the CTA barrier
+  // orders them before thread 0's release, and a release is cumulative), one
+  // decision for the whole CTA on whether to go on (a warpgroup may have
+  // stopped alone), then the arrival.
   auto grid_arrive = [&]() {
     dead = consumers_or(dead || *s_abort);
-    if (tid == 0) {
-      __threadfence();
-      red_release_gpu_add(a.sync, 1u);
-    }
+    if (tid == 0) red_release_gpu_add(a.sync, 1u);
   };
 
   for (int st = 0; st < a.n_steps && !dead; ++st) {
@@ -224,6 +230,17 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
       if (op.kind == kOpAttention && (int)blockIdx.x < a.n_heads) {
         // cache rows [0, pos) of this head were written in earlier steps
         attn_prefetch_rows<kNCT>(op.kc, op.vc, pos, (int)blockIdx.x / (a.n_heads / a.n_kv), a.n_kv, tid);
+      }
+      // RMSNorm weights do not depend on the previous operation: this thread's
+      // share (float4 i = tid + kNCT * j) is loaded before the wait.
+      const bool norm_regs = op.kind == kOpMatvec && op.pro == kProNorm && op.nb * 8 <= kNormRegs * kNCT;
+      float4 nw[kNormRegs];
+      if (norm_regs) {
+#pragma unroll
+        for (int j = 0; j < kNormRegs; ++j) {
+          const int i = tid + kNCT * j;
+          nw[j] = i < op.nb * 8 ? reinterpret_cast<const float4*>(op.norm_w)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
       if (opi > 0 && !grid_wait(opi * gridDim.x)) {
         dead = true;
@@ -239,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
         if ((int)blockIdx.x < a.n_heads) {
           const AttnSmem sm = attn_smem_carve<256>(scratch);
           attention_head<256>(a.qkv, op.kc, op.vc, a.rope, pos, (int)blockIdx.x, a.n_heads, a.n_kv, a.sqrt_hd,
-                              a.img_attn, sm, tid, ConsumerSync{});
+                              a.img_attn, sm, tid, ConsumerSync{}, a.xr, a.img_attn_stride);
         }
         grid_arrive();
         ++opi;
@@ -259,10 +276,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
       // Prologue: the Q8_0 image of this operation's activation.
       if (op.pro == kProImage) {
         const int n16 = (int)(act_image_bytes(nb) / 16);
-        for (int i = tid; i < n16; i += kNCT) cp_async16(img + 16 * i, op.image + 16 * i);
+        const unsigned char* src = op.image + (size_t)(blockIdx.x % a.xr) * op.image_stride;
+        for (int i = tid; i < n16; i += kNCT) cp_async16(img + 16 * i, src + 16 * i);
         cp_async_wait_all();
       } else {
-        const float* x = op.x;
+        const float* x = op.x + (size_t)(blockIdx.x % a.xr) * a.x_stride;
         if (op.from_embed) {
           // this step's token: a prompt id, or the argmax of the previous step
           int tok;
@@ -282,13 +300,58 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
         const int lane8 = tid & 7;
         constexpr int BPP = kNCT / 8;
         float rms = 1.0f;
-        if (op.pro == kProNorm) {
+        if (norm_regs) {
+          // One load of x into registers: float4 i = tid + kNCT * j is lane
+          // (tid & 7) of block i / 8, the quantize's own layout.  The same sums
+          // in the same order as the two-pass form below.
+          float4 v[kNormRegs];
+#pragma unroll
+          for (int j = 0; j < kNormRegs; ++j) {
+            const int i = tid + kNCT * j;
+            v[j] = i < nb * 8 ? __ldcg(reinterpret_cast<const float4*>(x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          float ss = 0.0f;
+#pragma unroll
+          for (int j = 0; j < kNormRegs; ++j) {
+            const int i = tid + kNCT * j;
+            if (i < nb * 8) {
+              ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v[j].x, v[j].x), __fmul_rn(v[j].y, v[j].y)),
+                                           __fadd_rn(__fmul_rn(v[j].z, v[j].z), __fmul_rn(v[j].w, v[j].w))));
+              if (copy)
+                for (int r = 0; r < a.xr; ++r) reinterpret_cast<float4*>(a.x + (size_t)r * a.x_stride)[i] = v[j];
+            }
+          }
+          ss = warp_sum(ss);
+          if (lane == 0) part[warp] = ss;
+          consumer_bar_sync(kNCT);
+          float tot = 0.0f;
+#pragma unroll
+          for (int i = 0; i < kNCW; ++i) tot = __fadd_rn(tot, part[i]);
+          rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * QK)), a.eps));
+#pragma unroll
+          for (int j = 0; j < kNormRegs; ++j) {
+            if (kNCT * j >= nb * 8) break;  // uniform
+            const int i = tid + kNCT * j, b = i >> 3;
+            const float4 e = make_float4(__fmul_rn(__fdiv_rn(v[j].x, rms), nw[j].x),
+                                         __fmul_rn(__fdiv_rn(v[j].y, rms), nw[j].y),
+                                         __fmul_rn(__fdiv_rn(v[j].z, rms), nw[j].z),
+                                         __fmul_rn(__fdiv_rn(v[j].w, rms), nw[j].w));
+            float d;
+            int qsum;
+            const unsigned q = quantize_quad(e, d, qsum);
+            if (b < nb) {
+              reinterpret_cast<unsigned*>(img + b * 48)[lane8] = q;
+              if (lane8 == 0) reinterpret_cast<float2*>(img + (size_t)nb * 48)[b] = make_float2(d, __int_as_float(qsum));
+            }
+          }
+        } else if (op.pro == kProNorm) {
           float ss = 0.0f;
           for (int i = tid; i < nb * 8; i += kNCT) {
             const float4 v = __ldcg(reinterpret_cast<const float4*>(x) + i);
             ss = __fadd_rn(ss, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
                                          __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
-            if (copy) reinterpret_cast<float4*>(a.x)[i] = v;
+            if (copy)
+              for (int r = 0; r < a.xr; ++r) reinterpret_cast<float4*>(a.x + (size_t)r * a.x_stride)[i] = v;
           }
           ss = warp_sum(ss);
           if (lane == 0) part[warp] = ss;
@@ -299,9 +362,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
           rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * QK)), a.eps));
         } else if (copy) {
           for (int i = tid; i < nb * 8; i += kNCT)
-            reinterpret_cast<float4*>(a.x)[i] = __ldcg(reinterpret_cast<const float4*>(x) + i);
+            for (int r = 0; r < a.xr; ++r)
+              reinterpret_cast<float4*>(a.x + (size_t)r * a.x_stride)[i] = __ldcg(reinterpret_cast<const float4*>(x) + i);
         }
-        for (int base = 0; base < nb; base += 4 * BPP) {
+        for (int base = 0; !norm_regs && base < nb; base += 4 * BPP) {
           float4 v[4];
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
@@ -446,7 +510,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
             for (int j = 1; j < WPG; ++j) t += pr[j * 2 + lane];
             const int row = row0 + rbase + lane;
             if (op.epi == kEpiResidual) {
-              op.y[row] = __fadd_rn(__ldcg(op.y + row), t);
+              const float nv = __fadd_rn(__ldcg(op.y + row), t);  // y is x: every replica
+              for (int r = 0; r < a.xr; ++r) op.y[(size_t)r * a.x_stride + row] = nv;
             } else {
               op.y[row] = t;
               if (op.epi == kEpiArgmax && t == t) {
@@ -478,37 +543,39 @@ __global__ void __launch_bounds__(kThreads, 2) decode_persistent_kernel(const Pe
         }
       }
       if (op.epi == kEpiSwiglu) {
+        // This CTA's h values are stored.  One arrival per Q8_0 block it
+        // touched: lane i of warp 0 adds this CTA's pair count for block b0 + i
+        // with an acq_rel atomic (release of this CTA's h after the barrier,
+        // acquire of the other CTAs'), and warp 0 quantizes every block whose
+        // arrival completed its 32 values.
         const int p0 = r0 >> 1, p1 = r1 >> 1;
-        constexpr int kChunk = 64;
-        int* s_last = reinterpret_cast<int*>(part);  // 64 ints fit the partials area
         const int b0 = p0 >> 5, nblk = p1 > p0 ? ((p1 + 31) >> 5) - b0 : 0;
         consumer_bar_sync(kNCT);
-        for (int c0 = 0; c0 < nblk; c0 += kChunk) {
-          const int nc = min(kChunk, nblk - c0);
-          if (tid == 0) {
-            __threadfence();
-            for (int i = 0; i < nc; ++i) {
-              const int blk = b0 + c0 + i;
-              const int n = min(p1, (blk + 1) * 32) - max(p0, blk * 32);
-              s_last[i] = atomicAdd(a.counters + blk, (unsigned)n) + (unsigned)n == 32u;
+        if (warp == 0) {
+          for (int c0 = 0; c0 < nblk; c0 += 32) {
+            bool last = false;
+            if (c0 + lane < nblk) {
+              const int blk = b0 + c0 + lane;
+              const unsigned n = (unsigned)(min(p1, (blk + 1) * 32) - max(p0, blk * 32));
+              last = atom_add_acq_rel_gpu(a.counters + blk, n) + n == 32u;
             }
-            __threadfence();
-          }
-          consumer_bar_sync(kNCT);
-          for (int i = warp; i < nc; i += kNCW) {
-            if (!s_last[i]) continue;
-            const int blk = b0 + c0 + i;
-            const float4 hv4 = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)blk * QK) + (lane & 7));
-            float d;
-            int qsum;
-            const unsigned q = quantize_quad(hv4, d, qsum);
-            if (lane < 8) reinterpret_cast<unsigned*>(a.img_h + (size_t)blk * 48)[lane] = q;
-            if (lane == 0) {
-              reinterpret_cast<float2*>(a.img_h + (size_t)(M >> 6) * 48)[blk] = make_float2(d, __int_as_float(qsum));
-              a.counters[blk] = 0u;
+            unsigned ballot = __ballot_sync(kFull, last);
+            __syncwarp();  // the acquiring lane's view reaches the lanes that read h
+            while (ballot) {
+              const int qb = b0 + c0 + __ffs(ballot) - 1;
+              ballot &= ballot - 1;
+              const float4 hv4 = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)qb * QK) + (lane & 7));
+              float d;
+              int qsum;
+              const unsigned q = quantize_quad(hv4, d, qsum);
+              for (int r = 0; r < a.xr; ++r) {
+                unsigned char* im = a.img_h + (size_t)r * a.img_h_stride;
+                if (lane < 8) reinterpret_cast<unsigned*>(im + (size_t)qb * 48)[lane] = q;
+                if (lane == 0) reinterpret_cast<float2*>(im + (size_t)(M >> 6) * 48)[qb] = make_float2(d, __int_as_float(qsum));
+              }
+              if (lane == 0) a.counters[qb] = 0u;
             }
           }
-          consumer_bar_sync(kNCT);
         }
       }
       gsb += S;

@@ -22,7 +22,8 @@ struct PersistOp {
   const uint8_t* w = nullptr;
   const __half* s = nullptr;
   const float* x = nullptr;             // prologue source (kProQuant / kProNorm)
-  const unsigned char* image = nullptr; // prologue source (kProImage)
+  const unsigned char* image = nullptr; // prologue source (kProImage), replica 0
+  size_t image_stride = 0;              // bytes between its replicas
   const float* norm_w = nullptr;
   float* y = nullptr;                   // kEpiStore / kEpiResidual / kEpiArgmax output
   __half* kc = nullptr;                 // attention: this layer's caches [ctx][n_kv][128]
@@ -38,11 +39,19 @@ struct PersistArgs {
   int vocab = 0;
   const float2* rope = nullptr;
   int ctx = 0, n_heads = 0, n_kv = 0;
-  float* x = nullptr;  // residual stream
+  // Activations every CTA reads after a barrier (the residual stream x and
+  // the two activation images) are kept in xr identical replicas, CTA b
+  // reading replica b % xr: the same few cache lines read by every SM at once
+  // would otherwise queue at a handful of L2 slices.
+  int xr = 1;
+  size_t x_stride = 0;         // floats between replicas of x
+  size_t img_attn_stride = 0;  // bytes between replicas of img_attn
+  size_t img_h_stride = 0;     // bytes between replicas of img_h
+  float* x = nullptr;  // residual stream [xr][dim]
   float* qkv = nullptr;
-  unsigned char* img_attn = nullptr;
+  unsigned char* img_attn = nullptr;  // [xr][image bytes]
   float* h = nullptr;
-  unsigned char* img_h = nullptr;
+  unsigned char* img_h = nullptr;  // [xr][image bytes]
   unsigned* counters = nullptr;
   unsigned long long* best = nullptr;  // [2], zero between runs
   int32_t* tokens = nullptr;

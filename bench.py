@@ -490,8 +490,12 @@ def main():
 
         dms_graph = time_decode("graph")
         graph_toks = dec.tokens[len(prompt):len(prompt) + n_new].cpu().tolist()
-        dms = time_decode("persistent")
-        gen_toks = dec.tokens[len(prompt):len(prompt) + n_new].cpu().tolist()
+        dms_pers = time_decode("persistent")
+        pers_toks = dec.tokens[len(prompt):len(prompt) + n_new].cpu().tolist()
+        # both engines are measured in this run; the headline is the faster one
+        engine = "persistent" if dms_pers <= dms_graph else "graph"
+        dms = min(dms_pers, dms_graph)
+        gen_toks = pers_toks if engine == "persistent" else graph_toks
         derr = ops.device_error()
         wb = D.LLAMA_7B.weight_bytes()
         kvb = sum(D.LLAMA_7B.kv_bytes(p) for p in range(len(prompt) - 1, len(prompt) - 1 + n_new)) / n_new
@@ -502,14 +506,18 @@ def main():
             "model": "random-init Llama-7B shape (32 L, d 4096, 32 heads x 128, FFN 11008, vocab 32000), Q4_0 linear "
                      "weights with fp16 scales, fp32 norms 1+N(0,0.01), fp16 KV cache ctx 512",
             "prompt_tokens": len(prompt), "greedy_steps": n_new, "batch": 1,
-            "engine": "persistent: one cooperative launch for all the timed steps (operations separated by "
-                      "device-side grid barriers, weights streamed through shared-memory rings without pauses)",
-            "launches": 1,
-            "graph_engine": {"tokens_per_s": round(n_new * world / (dms_graph / 1e3), 2),
-                             "ms_per_token": round(dms_graph / n_new, 4),
-                             "launches_per_token": dec.launches_per_step,
-                             "launch": "CUDA graphs of 16 steps of per-operation kernels, PDL between kernels",
-                             "same_tokens": graph_toks == gen_toks},
+            "engine": engine,
+            "launches": 1 if engine == "persistent" else dec.launches_per_step * n_new,
+            "engines": {
+                "graph": {"tokens_per_s": round(n_new * world / (dms_graph / 1e3), 2),
+                          "ms_per_token": round(dms_graph / n_new, 4),
+                          "launches_per_token": dec.launches_per_step,
+                          "launch": "CUDA graphs of 16 steps of per-operation kernels, PDL between kernels"},
+                "persistent": {"tokens_per_s": round(n_new * world / (dms_pers / 1e3), 2),
+                               "ms_per_token": round(dms_pers / n_new, 4),
+                               "launch": "one cooperative kernel for all the timed steps; grid barriers between "
+                                         "operations, weight rings streaming across operation boundaries"},
+                "same_tokens": graph_toks == pers_toks},
             "weight_bytes_per_token": wb, "kv_bytes_per_token_avg": round(kvb),
             "achieved_GB/s": round((wb + kvb) / per_tok_s / 1e9, 1),
             "first_tokens": gen_toks[:8], "device_error": derr,

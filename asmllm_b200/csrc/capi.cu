@@ -107,7 +107,7 @@ struct Buf {
 struct DeviceState {
   bool init = false;
   cudaStream_t stream = nullptr;
-  Buf dev[4];   // device staging: weights, scales, x, y
+  Buf dev[5];   // device staging: weights, scales, x, y, Q5_0 high bits
   Buf host[2];  // pinned host staging: x, y
   Buf image;    // Q8_0 activation image of the synchronous calls
   unsigned* err_word = nullptr;  // pinned copy of the device error word
@@ -497,6 +497,93 @@ ASMLLM_API void asm_matmul_q8_mt(const int8_t* qweights, const float* scales, co
                                  float* y, int64_t M, int64_t K, int num_threads) {
   (void)num_threads;
   sync_matvec("asm_matmul_q8_mt", kFmtQ8_0, true, qweights, scales, x, y, M, K);
+}
+
+// Q5_0 x fp32 (matmul_q5_avx2.asm): host or device pointers, like the other
+// synchronous entries (no weight registry for Q5_0: staged per call).
+void sync_q5(const char* name, const uint8_t* ql, const uint8_t* qh, const float* s, const float* x, float* y,
+             int64_t M, int64_t K) {
+  if (validate(name, ql, s, x, y, M, K)) return;
+  if (K > 0 && !qh) {
+    set_error(ASM_E_INVALID, "%s: null qh", name);
+    return;
+  }
+  if (M == 0) return;
+  DeviceState* stp = nullptr;
+  int dev = 0;
+  if (get_state(&stp, &dev)) return;
+  DeviceState& st = *stp;
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (K > 0 && q5_smem_bytes(K) > (size_t)optin) {  // x is staged in shared memory
+    set_error(ASM_E_UNSUPPORTED, "%s: K=%lld exceeds the supported maximum %lld", name, (long long)K,
+              (long long)(optin / (36 * 4) * 32));
+    return;
+  }
+  std::lock_guard<std::mutex> lk(st.mu);
+  const void *dl = nullptr, *dh = nullptr, *ds = nullptr, *dx = nullptr;
+  const int64_t nb = K / 32;
+  if (K > 0) {
+    if (device_in(st, dev, ql, (size_t)M * nb * 16, 0, &dl, name) ||
+        device_in(st, dev, s, (size_t)M * nb * sizeof(float), 1, &ds, name) ||
+        device_in(st, dev, x, (size_t)K * sizeof(float), 2, &dx, name) ||
+        device_in(st, dev, qh, (size_t)M * nb * 4, 4, &dh, name))
+      return;
+    if ((uintptr_t)dl % 16 || (uintptr_t)dh % 4 || (uintptr_t)ds % 4 || (uintptr_t)dx % 16) {
+      set_error(ASM_E_INVALID, "%s: ql/x must be 16-byte, qh/scales 4-byte aligned", name);
+      return;
+    }
+  }
+  int ydev = -1;
+  const PtrKind yk = classify(y, &ydev);
+  const size_t ybytes = (size_t)M * sizeof(float);
+  float* dy = nullptr;
+  if (yk == kDevice) {
+    if (ydev != dev) {
+      set_error(ASM_E_INVALID, "%s: y lives on device %d but the current device is %d", name, ydev, dev);
+      return;
+    }
+    dy = y;
+  } else {
+    if (ensure_dev(st.dev[3], ybytes)) return;
+    dy = static_cast<float*>(st.dev[3].p);
+  }
+  cudaError_t e = launch_q5_matvec(static_cast<const uint8_t*>(dl), static_cast<const uint8_t*>(dh),
+                                   static_cast<const float*>(ds), static_cast<const float*>(dx), dy, M, K, st.stream);
+  if (e == cudaSuccess && yk != kDevice) e = cudaMemcpyAsync(y, dy, ybytes, cudaMemcpyDeviceToHost, st.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st.stream);
+  if (e != cudaSuccess) cuda_error(e, name);
+}
+
+ASMLLM_API void asm_matmul_q5(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x, float* y,
+                              int64_t M, int64_t K) {
+  sync_q5("asm_matmul_q5", ql, qh, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_matmul_q5_mt(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x,
+                                 float* y, int64_t M, int64_t K, int num_threads) {
+  (void)num_threads;
+  sync_q5("asm_matmul_q5_mt", ql, qh, scales, x, y, M, K);
+}
+
+ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x,
+                                   float* y, int64_t M, int64_t K, void* stream) {
+  const char* name = "asm_matmul_q5_async";
+  int rc = validate(name, ql, scales, x, y, M, K);
+  if (rc) return rc;
+  if (M == 0) return ASM_OK;
+  if ((rc = require_device(name, y, "y"))) return rc;
+  if (K > 0) {
+    if ((rc = require_device(name, ql, "ql")) || (rc = require_device(name, qh, "qh")) ||
+        (rc = require_device(name, scales, "scales")) || (rc = require_device(name, x, "x")))
+      return rc;
+    if ((uintptr_t)ql % 16 || (uintptr_t)qh % 4 || (uintptr_t)scales % 4 || (uintptr_t)x % 16)
+      return set_error(ASM_E_INVALID, "%s: ql/x must be 16-byte, qh/scales 4-byte aligned", name);
+  }
+  const cudaError_t e = launch_q5_matvec(ql, qh, scales, x, y, M, K, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue) return set_error(ASM_E_UNSUPPORTED, "%s: K=%lld too large", name, (long long)K);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
 }
 
 ASMLLM_API void asm_threadpool_dispatch_q8(const int8_t* qweights, const float* scales,
@@ -933,8 +1020,8 @@ ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* 
 }
 
 // ctypes mirrors of the descriptor (asmllm_b200/native.py FusedMatvec) rely on this layout.
-static_assert(sizeof(asm_fused_matvec_t) == 160 && offsetof(asm_fused_matvec_t, eps) == 128 &&
-                  offsetof(asm_fused_matvec_t, M) == 144,
+static_assert(sizeof(asm_fused_matvec_t) == 256 && offsetof(asm_fused_matvec_t, eps) == 128 &&
+                  offsetof(asm_fused_matvec_t, M) == 144 && offsetof(asm_fused_matvec_t, xchg) == 176,
               "asm_fused_matvec_t layout");
 
 ASMLLM_API int asm_fused_matvec_async(const asm_fused_matvec_t* p, void* stream) {
@@ -1001,6 +1088,27 @@ ASMLLM_API int asm_fused_matvec_async(const asm_fused_matvec_t* p, void* stream)
   f.counters = p->counters;
   f.best = reinterpret_cast<unsigned long long*>(p->best);
   f.done = p->done;
+  if (p->tp > 1) {
+    if (p->tp > kMaxTp || p->tp_rank < 0 || p->tp_rank >= p->tp)
+      return set_error(ASM_E_INVALID, "%s: tp %d / rank %d out of range", name, p->tp, p->tp_rank);
+    if (p->epilogue != ASM_EPI_RESIDUAL && p->epilogue != ASM_EPI_ARGMAX)
+      return set_error(ASM_E_UNSUPPORTED, "%s: tensor parallelism needs the RESIDUAL or ARGMAX epilogue", name);
+    if (p->xchg_rows < (p->epilogue == ASM_EPI_RESIDUAL ? p->M : 2))
+      return set_error(ASM_E_INVALID, "%s: xchg_rows %d too small", name, p->xchg_rows);
+    if ((rc = require_device(name, p->ar_seq, "ar_seq")) || (rc = require_device(name, p->ar_done, "ar_done")))
+      return rc;
+    for (int r = 0; r < p->tp; ++r) {
+      if (!p->xchg[r] || (uintptr_t)p->xchg[r] % 8)
+        return set_error(ASM_E_INVALID, "%s: exchange buffer of rank %d missing or misaligned", name, r);
+      f.xchg[r] = static_cast<unsigned long long*>(p->xchg[r]);
+    }
+    f.tp = p->tp;
+    f.tp_rank = p->tp_rank;
+    f.xchg_rows = p->xchg_rows;
+    f.vocab_offset = p->vocab_offset;
+    f.ar_seq = p->ar_seq;
+    f.ar_done = p->ar_done;
+  }
   MatvecArgs a;
   a.fmt = p->fmt;
   a.scales_f16 = true;
@@ -1021,6 +1129,46 @@ ASMLLM_API int asm_fused_matvec_async(const asm_fused_matvec_t* p, void* stream)
                      name, (long long)p->M, (long long)p->K, p->epilogue);
   if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
+}
+
+ASMLLM_API int asm_ipc_alloc(int64_t bytes, void** ptr, void* handle64) {
+  const char* name = "asm_ipc_alloc";
+  if (bytes <= 0 || !ptr || !handle64) return set_error(ASM_E_INVALID, "%s: bad arguments", name);
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, (size_t)bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return cuda_error(e, name);
+  }
+  memcpy(handle64, &h, sizeof(h));
+  *ptr = p;
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_ipc_open(const void* handle64, void** ptr) {
+  const char* name = "asm_ipc_open";
+  if (!handle64 || !ptr) return set_error(ASM_E_INVALID, "%s: bad arguments", name);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  *ptr = p;
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? ASM_OK : cuda_error(e, "asm_ipc_close");
+}
+
+ASMLLM_API int asm_ipc_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? ASM_OK : cuda_error(e, "asm_ipc_free");
 }
 
 ASMLLM_API int asm_attention_decode_async(const float* qkv, void* k_cache, void* v_cache,

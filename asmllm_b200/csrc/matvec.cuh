@@ -45,7 +45,25 @@ struct MvFuse {
   // kEpiArgmax
   unsigned long long* best = nullptr;  // packed (value, row); zero on entry, left zero
   unsigned* done = nullptr;            // CTAs finished; zero on entry, left zero
+  // Tensor parallelism (tp > 1), kEpiResidual and kEpiArgmax only.
+  //   kEpiResidual: y here is this rank's partial sum of a row-parallel
+  //   projection; every rank writes its partial rows into every rank's
+  //   exchange buffer, then each CTA sums the tp partials of its rows in rank
+  //   order and adds them to the residual stream (identical on all ranks).
+  //   kEpiArgmax: rows are this rank's vocabulary slice (global row = row +
+  //   vocab_offset); the ranks' maxima are exchanged the same way.
+  // Exchange words are 64-bit (value bits, sequence number): a reader spins
+  // (bounded) until the word carries the current sequence, so no fence is
+  // needed.  Buffers: [2 parities][tp source ranks][xchg_rows] words, parity
+  // = sequence & 1; the sequence is *ar_seq + 1, stored back by the last CTA.
+  int tp = 1, tp_rank = 0;
+  int xchg_rows = 0;
+  int vocab_offset = 0;
+  unsigned long long* xchg[8] = {};  // exchange buffer of each rank (peer pointers)
+  unsigned* ar_seq = nullptr;        // call counter of this rank (same on all ranks)
+  unsigned* ar_done = nullptr;       // CTAs finished; zero on entry, left zero
 };
+constexpr int kMaxTp = 8;
 
 struct MatvecArgs {
   int fmt = kFmtQ4_0;       // kFmtQ4_0 or kFmtQ8_0
@@ -73,6 +91,7 @@ struct MatvecArgs {
 // Device error word bits (read_device_error).
 constexpr unsigned kErrRingTimeout = 1u;  // a shared-memory ring barrier wait gave up
 constexpr unsigned kErrDecodeRange = 2u;  // decode position or token id out of range: step skipped
+constexpr unsigned kErrXchgTimeout = 4u;  // a tensor-parallel exchange wait gave up (a peer never wrote)
 
 // Bytes of one row of the Q8_0 activation image for nb = K/32 blocks:
 // nb 48-byte slots (32 int8 + 16 pad) then nb (d, qsum) float pairs, rounded to 16.
@@ -112,6 +131,11 @@ unsigned* device_error_word();
 cudaError_t launch_attention_decode(const float* qkv, void* k_cache, void* v_cache, const float* rope_cs,
                                     const int32_t* pos, void* image, int n_heads, int n_kv, int head_dim, int ctx,
                                     float sqrt_hd, cudaStream_t stream, bool pdl);
+
+// Q5_0 x fp32 matvec (q5_matvec.cu): ql [M][K/32][16], qh [M][K/32][4], fp32 scales.
+size_t q5_smem_bytes(int64_t K);
+cudaError_t launch_q5_matvec(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x, float* y,
+                             int64_t M, int64_t K, cudaStream_t stream);
 
 extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
 extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch

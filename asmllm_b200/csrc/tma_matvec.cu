@@ -52,14 +52,69 @@ constexpr int kPartBytes = 2 * 2 * 8 * 2 * 4;    // row partials [2 parities][2 
 }  // namespace
 
 
+// ---- tensor-parallel exchange words: (sequence << 32) | payload bits ------
+__device__ __forceinline__ void st_volatile_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// The payload of the exchange word at p once it carries sequence seq; bounded
+// (a peer that never writes sets the error bit and yields 0; after one
+// timeout, `ok` makes the caller's later waits return at once).
+__device__ __forceinline__ unsigned xchg_wait(const unsigned long long* p, unsigned seq, bool& ok) {
+  unsigned long long v = ld_volatile_u64(p);
+  if ((unsigned)(v >> 32) == seq) return (unsigned)v;
+  if (!ok) return 0u;
+  const long long t0 = clock64();
+  do {
+    v = ld_volatile_u64(p);
+    if (clock64() - t0 > kWaitCycles) {
+      ok = false;
+      atomicOr(&g_device_error, kErrXchgTimeout);
+      return 0u;
+    }
+  } while ((unsigned)(v >> 32) != seq);
+  return (unsigned)v;
+}
+
+// Word of (parity, source rank, row) in the exchange buffer `buf`.
+__device__ __forceinline__ unsigned long long* xchg_word(const MvFuse& fz, unsigned long long* buf, unsigned seq,
+                                                         int src, int row) {
+  return buf + ((size_t)(seq & 1u) * fz.tp + src) * fz.xchg_rows + row;
+}
+
 // Called once per CTA (thread 0) after its rows' keys are folded into
 // fz.best: the last CTA to arrive turns the maximum into the next token,
 // advances the position and leaves best / done zero for the next launch.
-__device__ void argmax_arrive(const MvFuse& fz, unsigned nctas) {
+// With tensor parallelism the ranks' maxima are exchanged first (keys carry
+// global rows, so every rank picks the same token).
+__device__ void argmax_arrive(const MvFuse& fz, unsigned nctas, unsigned seq) {
   __threadfence();
   if (atomicAdd(fz.done, 1u) != nctas - 1) return;
   __threadfence();
-  const unsigned long long b = atomicExch(fz.best, 0ull);
+  unsigned long long b = atomicExch(fz.best, 0ull);
+  if (fz.tp > 1) {
+    const unsigned long long tag = (unsigned long long)seq << 32;
+    for (int r = 0; r < fz.tp; ++r) {
+      st_volatile_u64(xchg_word(fz, fz.xchg[r], seq, fz.tp_rank, 0), tag | (b >> 32));
+      st_volatile_u64(xchg_word(fz, fz.xchg[r], seq, fz.tp_rank, 1), tag | (b & 0xFFFFFFFFull));
+    }
+    bool ok = true;
+    unsigned long long m = 0;
+    for (int r = 0; r < fz.tp; ++r) {
+      const unsigned long long hi = xchg_wait(xchg_word(fz, fz.xchg[fz.tp_rank], seq, r, 0), seq, ok);
+      const unsigned long long lo = xchg_wait(xchg_word(fz, fz.xchg[fz.tp_rank], seq, r, 1), seq, ok);
+      const unsigned long long k = (hi << 32) | lo;
+      m = k > m ? k : m;
+    }
+    b = m;
+    *fz.ar_seq = seq;
+  }
   const int idx = argmax_row(b);
   volatile int32_t* pos = fz.pos;
   const int p = *pos;
@@ -122,9 +177,15 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
 
   pdl_trigger();
   if (S == 0) {
-    if (EPI == kEpiArgmax && threadIdx.x == 0) {
+    if ((EPI == kEpiArgmax || (EPI == kEpiResidual && fz.tp > 1)) && threadIdx.x == 0) {
       pdl_wait();
-      argmax_arrive(fz, gridDim.x);
+      const unsigned seq0 = fz.tp > 1 ? __ldcg(fz.ar_seq) + 1u : 0u;
+      if (EPI == kEpiArgmax) {
+        argmax_arrive(fz, gridDim.x, seq0);
+      } else if (atomicAdd(fz.ar_done, 1u) == gridDim.x - 1) {
+        *fz.ar_seq = seq0;
+        atomicExch(fz.ar_done, 0u);
+      }
     }
     return;
   }
@@ -191,6 +252,8 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   const int wg = warp >> 3, wi = warp & 7;
   const int rg = wi / WPG, sg = wi - rg * WPG;  // this warp's row group in a stage and its unit slice
   pdl_wait();  // x / the image may come from the previous kernel; y may still be in use
+  // Tensor-parallel call number (the previous exchange's last CTA stored it).
+  const unsigned seq = (fz.tp > 1 && (EPI == kEpiResidual || EPI == kEpiArgmax)) ? __ldcg(fz.ar_seq) + 1u : 0u;
   if (PRO != kProImage) {
     const float* x = prologue_source(fz, act, nb * QK);
     const bool copy = fz.x_copy != nullptr && blockIdx.x == 0;
@@ -255,11 +318,16 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   unsigned long long best_local = 0;  // kEpiArgmax: this lane's best (value, row)
   auto emit = [&](int row, float t) {
     if (EPI == kEpiResidual) {
-      y[row] = __fadd_rn(__ldcg(y + row), t);
+      if (fz.tp > 1) {  // this rank's partial: to every rank's exchange buffer
+        const unsigned long long wv = ((unsigned long long)seq << 32) | __float_as_uint(t);
+        for (int r = 0; r < fz.tp; ++r) st_volatile_u64(xchg_word(fz, fz.xchg[r], seq, fz.tp_rank, row), wv);
+      } else {
+        y[row] = __fadd_rn(__ldcg(y + row), t);
+      }
     } else {
       y[row] = t;
       if (EPI == kEpiArgmax && t == t) {
-        const unsigned long long key = argmax_key(t, row);
+        const unsigned long long key = argmax_key(t, row + fz.vocab_offset);
         best_local = key > best_local ? key : best_local;
       }
     }
@@ -417,7 +485,26 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       unsigned long long m = 0;
       for (int i = 0; i < NCW; ++i) m = wbest[i] > m ? wbest[i] : m;
       if (m) atomicMax(fz.best, m);
-      argmax_arrive(fz, gridDim.x);
+      argmax_arrive(fz, gridDim.x, seq);
+    }
+  }
+  if (EPI == kEpiResidual && fz.tp > 1) {
+    // Sum the tp partials of this CTA's rows in rank order (the same sum on
+    // every rank) into the residual stream; the last CTA records the sequence.
+    bool ok = true;
+    for (int row = r0 + (int)threadIdx.x; row < r1; row += NCT) {
+      float sum = 0.0f;
+      for (int r = 0; r < fz.tp; ++r)
+        sum = __fadd_rn(sum, __uint_as_float(xchg_wait(xchg_word(fz, fz.xchg[fz.tp_rank], seq, r, row), seq, ok)));
+      y[row] = __fadd_rn(__ldcg(y + row), sum);
+    }
+    consumer_bar_sync(NCT);
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(fz.ar_done, 1u) == gridDim.x - 1) {
+        *fz.ar_seq = seq;
+        atomicExch(fz.ar_done, 0u);
+      }
     }
   }
   if (EPI == kEpiSwiglu) {

@@ -92,11 +92,123 @@ def _random_weights(torch, fmt, M, K, gen, dev):
     return qs, d
 
 
+LM_UNIT = 16    # lm_head rows per generation unit
+FFN_UNIT = 256  # gate/up rows (and down-proj columns) per generation unit
+
+
+def _unit_seed(seed: int, layer: int, kind: int, index: int) -> int:
+    """Seed of one generation unit (a head, an FFN chunk, an lm_head chunk):
+    the random model does not depend on how it is sharded."""
+    h = (seed * 0x9E3779B97F4A7C15 + 0x632BE59BD9B4E019) & 0xFFFFFFFFFFFFFFFF
+    for v in (layer + 1, kind + 1, index + 1):
+        h = ((h ^ v) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+    return h & 0x7FFFFFFFFFFFFFFF
+
+
+_Q, _K, _V, _O, _G, _U, _D, _NA, _NF, _LM, _FN, _EMB = range(12)
+
+
+@dataclass(frozen=True)
+class Shard:
+    """This rank's slice of a tensor-parallel model (Megatron-style split)."""
+    tp: int
+    rank: int
+    heads: range      # query heads (column-parallel q, row-parallel o)
+    kv_heads: range
+    ffn: range        # FFN rows (column-parallel gate/up, row-parallel down)
+    vocab: range      # lm_head rows
+
+
+def shard_plan(shape: LlamaShape, tp: int, rank: int) -> Shard:
+    s = shape
+    if not 1 <= tp <= 8 or not 0 <= rank < tp:
+        raise ValueError("tp must be in [1, 8] and 0 <= rank < tp")
+    if s.n_heads % tp or s.n_kv_heads % tp:
+        raise ValueError(f"{s.n_heads} query / {s.n_kv_heads} KV heads do not split over {tp} ranks")
+    if (s.ffn // tp) % FFN_UNIT or s.ffn % tp:
+        raise ValueError(f"FFN {s.ffn} / {tp} is not a multiple of {FFN_UNIT}")
+    if (s.n_heads // tp * s.head_dim) % 256:
+        raise ValueError("each rank's n_heads * head_dim must be a multiple of 256")
+    if s.vocab % (tp * LM_UNIT):
+        raise ValueError(f"vocab {s.vocab} is not a multiple of {tp} * {LM_UNIT}")
+    def part(n):
+        return range(rank * n // tp, (rank + 1) * n // tp)
+    return Shard(tp, rank, part(s.n_heads), part(s.n_kv_heads), part(s.ffn), part(s.vocab))
+
+
+def make_weights(shape: LlamaShape, sh: Shard, seed: int, fmt: int, dev) -> dict:
+    """This rank's weights (torch tensors on `dev`): per layer wqkv (rows
+    [q heads; k heads; v heads]), wo (its heads' columns), wgu (its FFN rows,
+    gate/up interleaved), wdown (its FFN columns), norms; plus the lm_head
+    rows of its vocabulary slice, the final norm and the whole embedding.
+    Every unit (head, FFN chunk, vocabulary chunk, norm) has its own seed."""
+    import torch
+
+    s = shape
+    gen = torch.Generator(device=dev)
+    hd, nb_dim = s.head_dim, s.dim // 32
+    bpb = 16 if fmt == FMT_Q4_0 else 32
+
+    def rows(layer, kind, index, n, K):  # n rows of K columns
+        gen.manual_seed(_unit_seed(seed, layer, kind, index))
+        return _random_weights(torch, fmt, n, K, gen, dev)
+
+    def cols(layer, kind, index, M, n):  # M rows of n columns (a column block)
+        return rows(layer, kind, index, M, n)
+
+    def cat_rows(parts):
+        return (torch.cat([p[0] for p in parts]).contiguous(), torch.cat([p[1] for p in parts]).contiguous())
+
+    def cat_cols(parts):
+        return (torch.cat([p[0] for p in parts], 1).contiguous(), torch.cat([p[1] for p in parts], 1).contiguous())
+
+    def vec(layer, kind, n, scale=0.01, base=1.0):
+        gen.manual_seed(_unit_seed(seed, layer, kind, 0))
+        return base + scale * torch.randn(n, device=dev, generator=gen)
+
+    nh_l, nkv_l, ffn_l = len(sh.heads), len(sh.kv_heads), len(sh.ffn)
+    layers = []
+    for li in range(s.n_layers):
+        L = {}
+        L["wqkv"] = cat_rows([rows(li, _Q, h, hd, s.dim) for h in sh.heads]
+                             + [rows(li, _K, j, hd, s.dim) for j in sh.kv_heads]
+                             + [rows(li, _V, j, hd, s.dim) for j in sh.kv_heads])
+        L["wo"] = cat_cols([cols(li, _O, h, s.dim, hd) for h in sh.heads])
+        c0, c1 = sh.ffn.start // FFN_UNIT, sh.ffn.stop // FFN_UNIT
+        g = cat_rows([rows(li, _G, c, FFN_UNIT, s.dim) for c in range(c0, c1)])
+        u = cat_rows([rows(li, _U, c, FFN_UNIT, s.dim) for c in range(c0, c1)])
+        # rows gate_0, up_0, gate_1, up_1, ...: a pair is finished by one warp
+        L["wgu"] = (torch.stack([g[0], u[0]], 1).reshape(2 * ffn_l, nb_dim, bpb).contiguous(),
+                    torch.stack([g[1], u[1]], 1).reshape(2 * ffn_l, nb_dim).contiguous())
+        del g, u
+        L["wdown"] = cat_cols([cols(li, _D, c, s.dim, FFN_UNIT) for c in range(c0, c1)])
+        L["attn_norm"] = vec(li, _NA, s.dim)
+        L["ffn_norm"] = vec(li, _NF, s.dim)
+        layers.append(L)
+    final_norm = vec(-1, _FN, s.dim)
+    lm_head = cat_rows([rows(-1, _LM, c, LM_UNIT, s.dim)
+                             for c in range(sh.vocab.start // LM_UNIT, sh.vocab.stop // LM_UNIT)])
+    gen.manual_seed(_unit_seed(seed, -1, _EMB, 0))
+    return {"layers": layers, "final_norm": final_norm, "lm_head": lm_head,
+            "embed": torch.randn((s.vocab, s.dim), device=dev, generator=gen)}
+
+
 class LlamaDecoder:
-    """Random-init Llama-style model resident on one GPU, decoded at batch 1."""
+    """Random-init Llama-style model resident on one GPU (or this rank's slice
+    of it, tp > 1), decoded at batch 1.
+
+    Tensor parallelism: q/k/v, gate/up and the lm_head are split by rows
+    (heads, FFN rows, vocabulary), o and down by columns; the row-parallel
+    projections exchange their partial rows over NVLink inside the matvec
+    kernel (peer stores into every rank's exchange buffer, each rank sums in
+    rank order), and the lm_head ranks exchange their maxima.  Every rank
+    holds the full residual stream, embedding and norms.  The weights are
+    generated per unit (head, 256-row FFN chunk, 16-row vocabulary chunk)
+    from `seed`, so the model is the same whatever tp is.
+    """
 
     def __init__(self, shape: LlamaShape, ctx: int = 512, max_tokens: int | None = None, seed: int = 0,
-                 fmt: int = FMT_Q4_0, device=None):
+                 fmt: int = FMT_Q4_0, device=None, tp: int = 1, tp_rank: int = 0, group=None):
         import torch
 
         self.torch = torch
@@ -108,54 +220,75 @@ class LlamaDecoder:
             raise ValueError("head_dim must be 128")
         if s.dim % 256 or s.ffn % 256 or (s.n_heads * s.head_dim) % 256:
             raise ValueError("dim, ffn and n_heads*head_dim must be multiples of 256 (whole fp16 scale rows)")
+        self.shard = sh = shard_plan(s, tp, tp_rank)
+        self.tp, self.tp_rank = tp, tp_rank
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
-        gen = torch.Generator(device=dev)
-        gen.manual_seed(seed)
-        qdim = s.n_heads * s.head_dim
-        self.layers = []
-        for _ in range(s.n_layers):
-            L = {}
-            L["wqkv"] = _random_weights(torch, fmt, s.qkv_rows, s.dim, gen, dev)
-            L["wo"] = _random_weights(torch, fmt, s.dim, qdim, gen, dev)
-            g = _random_weights(torch, fmt, s.ffn, s.dim, gen, dev)
-            u = _random_weights(torch, fmt, s.ffn, s.dim, gen, dev)
-            # rows gate_0, up_0, gate_1, up_1, ...: a pair is finished by one warp
-            L["wgu"] = (torch.stack([g[0], u[0]], 1).reshape(2 * s.ffn, *g[0].shape[1:]).contiguous(),
-                        torch.stack([g[1], u[1]], 1).reshape(2 * s.ffn, g[1].shape[1]).contiguous())
-            del g, u
-            L["wdown"] = _random_weights(torch, fmt, s.dim, s.ffn, gen, dev)
-            L["attn_norm"] = 1.0 + 0.01 * torch.randn(s.dim, device=dev, generator=gen)
-            L["ffn_norm"] = 1.0 + 0.01 * torch.randn(s.dim, device=dev, generator=gen)
-            self.layers.append(L)
-        self.final_norm = 1.0 + 0.01 * torch.randn(s.dim, device=dev, generator=gen)
-        self.lm_head = _random_weights(torch, fmt, s.vocab, s.dim, gen, dev)
-        self.embed = torch.randn((s.vocab, s.dim), device=dev, generator=gen)
+        W = make_weights(s, sh, seed, fmt, dev)
+        self.layers, self.final_norm, self.lm_head, self.embed = W["layers"], W["final_norm"], W["lm_head"], W["embed"]
+        hd = s.head_dim
+        nh_l, nkv_l, ffn_l = len(sh.heads), len(sh.kv_heads), len(sh.ffn)
         for L in self.layers:
             for k in ("wqkv", "wo", "wgu", "wdown"):
                 ops.mark_static(*L[k])
         ops.mark_static(*self.lm_head)
 
         self.rope = torch.from_numpy(rope_table(ctx, s.head_dim, s.theta)).to(dev)
-        self.k_cache = torch.zeros((s.n_layers, ctx, s.n_kv_heads, s.head_dim), dtype=torch.float16, device=dev)
+        self.k_cache = torch.zeros((s.n_layers, ctx, nkv_l, s.head_dim), dtype=torch.float16, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
         self.x = torch.zeros(s.dim, device=dev)
-        self.qkv = torch.zeros(s.qkv_rows, device=dev)
-        self.img_attn = torch.zeros(ops.act_image_bytes(qdim), dtype=torch.uint8, device=dev)
-        self.h = torch.zeros(s.ffn, device=dev)
-        self.img_h = torch.zeros(ops.act_image_bytes(s.ffn), dtype=torch.uint8, device=dev)
-        self.counters = torch.zeros(s.ffn // 32, dtype=torch.int32, device=dev)
-        self.logits = torch.zeros(s.vocab, device=dev)
+        self.qkv = torch.zeros((nh_l + 2 * nkv_l) * hd, device=dev)
+        self.img_attn = torch.zeros(ops.act_image_bytes(nh_l * hd), dtype=torch.uint8, device=dev)
+        self.h = torch.zeros(ffn_l, device=dev)
+        self.img_h = torch.zeros(ops.act_image_bytes(ffn_l), dtype=torch.uint8, device=dev)
+        self.counters = torch.zeros(ffn_l // 32, dtype=torch.int32, device=dev)
+        self.logits = torch.zeros(len(sh.vocab), device=dev)
         self.best = torch.zeros(2, dtype=torch.int64, device=dev)
         self.done = torch.zeros(1, dtype=torch.int32, device=dev)
         self.tokens = torch.zeros(self.max_tokens, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ar_seq = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ar_done = torch.zeros(1, dtype=torch.int32, device=dev)
         # the reference divides the scores by np.sqrt(head_dim, dtype=np.float32)
         self.sqrt_hd = float(np.sqrt(np.float32(s.head_dim), dtype=np.float32))
         self.n_prompt = 0
         self._descs = None
         self._graphs = {}
         self._handle = None
+        self._xchg_own = None
+        self._xchg_peers = []
+        self._xchg = [0] * 8
+        if tp > 1:
+            self._open_exchange(group)
+
+    def _open_exchange(self, group):
+        """Exchange buffers: one per rank (CUDA IPC), every rank maps all of them."""
+        import torch.distributed as dist
+
+        L = native.lib()
+        nbytes = 2 * self.tp * self.shape.dim * 8
+        ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        native.check(L.asm_ipc_alloc(nbytes, ctypes.byref(ptr), handle))
+        self._xchg_own = ptr
+        handles = [None] * self.tp
+        dist.all_gather_object(handles, handle.raw, group=group)
+        for r, hr in enumerate(handles):
+            if r == self.tp_rank:
+                self._xchg[r] = ptr.value
+                continue
+            peer = ctypes.c_void_p()
+            native.check(L.asm_ipc_open(hr, ctypes.byref(peer)))
+            self._xchg_peers.append(peer)
+            self._xchg[r] = peer.value
+        dist.barrier(group=group)
+
+    def _tp_fields(self, d, epi):
+        if self.tp > 1 and epi in (native.EPI_RESIDUAL, native.EPI_ARGMAX):
+            d.tp, d.tp_rank, d.xchg_rows = self.tp, self.tp_rank, self.shape.dim
+            d.vocab_offset = self.shard.vocab.start if epi == native.EPI_ARGMAX else 0
+            for r in range(self.tp):
+                d.xchg[r] = self._xchg[r]
+            d.ar_seq, d.ar_done = self.ar_seq.data_ptr(), self.ar_done.data_ptr()
 
     # ------------------------------------------------------------------ launches
     def _mv(self, w, epi, M, K, **kw) -> FusedMatvec:
@@ -168,27 +301,29 @@ class LlamaDecoder:
         d.tokens, d.pos = self.tokens.data_ptr(), self.pos.data_ptr()
         for k, v in kw.items():
             setattr(d, k, v.data_ptr() if hasattr(v, "data_ptr") else v)
+        self._tp_fields(d, epi)
         return d
 
     def _build(self):
-        s = self.shape
-        qdim = s.n_heads * s.head_dim
-        kv_layer = s.n_kv_heads * s.head_dim * self.ctx
+        s, sh = self.shape, self.shard
+        nh_l, nkv_l, ffn_l = len(sh.heads), len(sh.kv_heads), len(sh.ffn)
+        qdim = nh_l * s.head_dim
+        kv_layer = nkv_l * s.head_dim * self.ctx
         descs = []
         for li, L in enumerate(self.layers):
             src = dict(embed=self.embed, x_copy=self.x) if li == 0 else dict(x=self.x)
-            descs.append(("mv", self._mv(L["wqkv"], native.EPI_STORE, s.qkv_rows, s.dim,
+            descs.append(("mv", self._mv(L["wqkv"], native.EPI_STORE, (nh_l + 2 * nkv_l) * s.head_dim, s.dim,
                                          norm_w=L["attn_norm"], y=self.qkv, **src)))
             descs.append(("attn", (self.qkv.data_ptr(), self.k_cache.data_ptr() + 2 * li * kv_layer,
                                    self.v_cache.data_ptr() + 2 * li * kv_layer, self.rope.data_ptr(),
-                                   self.pos.data_ptr(), self.img_attn.data_ptr(), s.n_heads, s.n_kv_heads,
+                                   self.pos.data_ptr(), self.img_attn.data_ptr(), nh_l, nkv_l,
                                    s.head_dim, self.ctx, self.sqrt_hd)))
             descs.append(("mv", self._mv(L["wo"], native.EPI_RESIDUAL, s.dim, qdim, image=self.img_attn, y=self.x)))
-            descs.append(("mv", self._mv(L["wgu"], native.EPI_SWIGLU, 2 * s.ffn, s.dim, x=self.x,
+            descs.append(("mv", self._mv(L["wgu"], native.EPI_SWIGLU, 2 * ffn_l, s.dim, x=self.x,
                                          norm_w=L["ffn_norm"], y=self.h, h=self.h, image_out=self.img_h,
                                          counters=self.counters)))
-            descs.append(("mv", self._mv(L["wdown"], native.EPI_RESIDUAL, s.dim, s.ffn, image=self.img_h, y=self.x)))
-        descs.append(("mv", self._mv(self.lm_head, native.EPI_ARGMAX, s.vocab, s.dim, x=self.x,
+            descs.append(("mv", self._mv(L["wdown"], native.EPI_RESIDUAL, s.dim, ffn_l, image=self.img_h, y=self.x)))
+        descs.append(("mv", self._mv(self.lm_head, native.EPI_ARGMAX, len(sh.vocab), s.dim, x=self.x,
                                      norm_w=self.final_norm, y=self.logits, best=self.best, done=self.done)))
         self._descs = descs
 
@@ -251,6 +386,8 @@ class LlamaDecoder:
         return g
 
     def _persistent(self):
+        if self.tp > 1:
+            raise ValueError("the persistent engine runs one GPU; use engine='graph' with tensor parallelism")
         if self._handle is None:
             s = self.shape
             L = native.lib()
@@ -314,7 +451,9 @@ class LlamaDecoder:
     # ------------------------------------------------------------------ export
     def host_weights(self):
         """Host copies in the reference ABI layout (qs + fp32 scales per matrix,
-        gate/up de-interleaved) for a CPU re-computation of the step."""
+        gate/up de-interleaved) for a CPU re-computation of the step (tp = 1)."""
+        if self.tp != 1:
+            raise ValueError("host_weights needs the whole model (tp = 1)")
         s = self.shape
         qdim = s.n_heads * s.head_dim
 
@@ -340,6 +479,13 @@ class LlamaDecoder:
         if self._handle is not None:
             native.lib().asm_decode_destroy(self._handle)
             self._handle = None
+        self._graphs = {}
+        if self._xchg_own is not None:
+            self.torch.cuda.synchronize()
+            for p in self._xchg_peers:
+                native.lib().asm_ipc_close(p)
+            native.lib().asm_ipc_free(self._xchg_own)
+            self._xchg_peers, self._xchg_own = [], None
         for L in self.layers:
             for k in ("wqkv", "wo", "wgu", "wdown"):
                 ops.unmark_static(*L[k])
@@ -347,4 +493,5 @@ class LlamaDecoder:
         self._graphs = {}
 
 
-__all__ = ["LlamaShape", "LLAMA_7B", "LLAMA2_70B", "LlamaDecoder", "rope_table", "FMT_Q4_0", "FMT_Q8_0"]
+__all__ = ["LlamaShape", "LLAMA_7B", "LLAMA2_70B", "LlamaDecoder", "Shard", "shard_plan", "rope_table",
+           "FMT_Q4_0", "FMT_Q8_0"]

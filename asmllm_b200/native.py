@@ -39,6 +39,8 @@ class FusedMatvec(ctypes.Structure):
         ("counters", vp), ("best", vp), ("done", vp), ("tokens", vp), ("pos", vp),
         ("eps", f32), ("vocab", i32), ("max_tokens", i32), ("n_prompt", i32),
         ("M", i64), ("K", i64),
+        ("tp", i32), ("tp_rank", i32), ("xchg_rows", i32), ("vocab_offset", i32),
+        ("xchg", vp * 8), ("ar_seq", vp), ("ar_done", vp),
     ]
 
 
@@ -70,6 +72,9 @@ SIGNATURES = {
     "asm_threadpool_shutdown": ([], None),
     "asm_threadpool_get_num_threads": ([], c_int),
     "asm_threadpool_dispatch_q8": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_matmul_q5": ([vp, vp, vp, vp, vp, i64, i64], None),
+    "asm_matmul_q5_mt": ([vp, vp, vp, vp, vp, i64, i64, c_int], None),
+    "asm_matmul_q5_async": ([vp, vp, vp, vp, vp, i64, i64, vp], c_int),
     # additions
     "asm_matmul_q8q8": ([vp, vp, vp, vp, i64, i64], None),
     "asm_quantize_q8_0": ([vp, vp, vp, i64], None),
@@ -97,6 +102,10 @@ SIGNATURES = {
     "asm_set_option": ([ctypes.c_char_p, c_int], c_int),
     "asm_matmul_q4_noalloc_async": ([vp, vp, c_int, vp, vp, i64, i64, vp], c_int),
     "asm_fused_matvec_async": ([ctypes.POINTER(FusedMatvec), vp], c_int),
+    "asm_ipc_alloc": ([i64, ctypes.POINTER(vp), ctypes.c_char_p], c_int),
+    "asm_ipc_open": ([ctypes.c_char_p, ctypes.POINTER(vp)], c_int),
+    "asm_ipc_close": ([vp], c_int),
+    "asm_ipc_free": ([vp], c_int),
     "asm_attention_decode_async": ([vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, vp], c_int),
     "asm_decode_create": ([ctypes.POINTER(DecodeModel), ctypes.POINTER(vp)], c_int),
     "asm_decode_run_async": ([vp, i32, i32, vp], c_int),

@@ -236,6 +236,8 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="skip per-shape / Q8 breakdown")
     ap.add_argument("--decode-steps", type=int, default=128,
                     help="greedy steps of the 7B batch-1 decode timed after the matvec sweep (0: skip)")
+    ap.add_argument("--decode70-steps", type=int, default=64,
+                    help="greedy steps of the Llama-2-70B-shape decode, tensor-parallel over the N GPUs (0: skip)")
     ap.add_argument("--mode", choices=["image", "fused"], default="fused",
                     help="image: activation-quantize pre-pass kernel + matvec (2 launches per matvec); "
                          "fused: quantize inside the matvec (1 launch)")
@@ -526,6 +528,54 @@ def main():
         del dec
         torch.cuda.empty_cache()
 
+    # ---- Llama-2-70B-shape batch-1 decode, tensor-parallel over the N GPUs ----
+    decode70 = None
+    if args.decode70_steps > 0:
+        from asmllm_b200 import decode as D
+
+        torch.cuda.empty_cache()
+        shape70 = D.LLAMA2_70B
+        dec = D.LlamaDecoder(shape70, ctx=1024, seed=70, tp=world, tp_rank=rank, group=None)
+        prompt = np.random.default_rng(1).integers(0, shape70.vocab, 16).tolist()  # same on every rank
+        n70 = args.decode70_steps
+        dec.generate(prompt, n70, engine="graph")  # warm-up and graph capture
+        dec.reset(prompt)
+        dec.run(len(prompt) - 1, engine="graph")
+        barrier()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record()
+        dec.run(n70, engine="graph")
+        d1.record()
+        d1.synchronize()
+        barrier()
+        t70 = d0.elapsed_time(d1)
+        if world > 1:
+            tt = torch.tensor([t70], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            t70 = float(tt.item())
+        toks70 = dec.tokens[len(prompt):len(prompt) + n70].cpu().tolist()
+        err70 = ops.device_error()
+        wb70 = shape70.weight_bytes()
+        kv70 = sum(shape70.kv_bytes(p) for p in range(len(prompt) - 1, len(prompt) - 1 + n70)) / n70
+        per_tok = t70 / 1e3 / n70
+        decode70 = {
+            "tokens_per_s": round(n70 / (t70 / 1e3), 2),
+            "ms_per_token": round(t70 / n70, 4),
+            "model": "random-init Llama-2-70B shape (80 L, d 8192, 64 q / 8 KV heads x 128, FFN 28672, vocab 32000), "
+                     "Q4_0 linear weights with fp16 scales, fp16 KV cache ctx 1024",
+            "tensor_parallel": world, "batch": 1, "prompt_tokens": len(prompt), "greedy_steps": n70,
+            "split": "q/k/v, gate/up, lm_head by rows; o, down by columns with the partial rows exchanged over "
+                     "NVLink inside the matvec kernel (peer stores + sequence-tagged words, rank-order sum)",
+            "engine": "graph", "launches_per_token": dec.launches_per_step,
+            "weight_bytes_per_token_per_gpu": wb70 // world,
+            "kv_bytes_per_token_avg": round(kv70),
+            "achieved_GB/s_per_gpu": round((wb70 + kv70) / world / per_tok / 1e9, 1),
+            "first_tokens": toks70[:8], "device_error": err70,
+        }
+        dec.close()
+        del dec
+        torch.cuda.empty_cache()
+
     if rank != 0:
         if world > 1:
             dist.barrier()
@@ -591,6 +641,12 @@ def main():
             decode["reference_cpu_estimate_basis"] = ("weight bytes per token / the cpu_baseline matvec GB/s "
                                                       "(derived, not a measured reference decode)")
         line["decode_7b"] = decode
+    if decode70 is not None:
+        decode70["frac_of_measured_hbm"] = round(decode70["achieved_GB/s_per_gpu"] / peak, 4)
+        # every GPU streams its 1/N of the weights and KV per token at the measured copy peak
+        decode70["roofline_tokens_per_s"] = round(
+            peak * 1e9 * world / (decode70["weight_bytes_per_token_per_gpu"] * world + decode70["kv_bytes_per_token_avg"]), 2)
+        line["decode_70b"] = decode70
         line["gpu_launches_decode"] = decode["launches"] * world
     line.update(extras)
     print(json.dumps(line), flush=True)

@@ -89,6 +89,19 @@ ASMLLM_API void asm_matmul_q4_avx512_mt(const uint8_t* qweights, const float* sc
                                         const float* x, float* y, int64_t M, int64_t K,
                                         int num_threads);
 
+/* Q5_0 x fp32 matvec: ql uint8 [M][K/32][16] (weight j's low 4 bits in the
+ * low nibble of byte j, j < 16, else the high nibble of byte j - 16), qh
+ * uint8 [M][K/32][4] (weight j's fifth bit = bit j % 8 of byte j / 8), value
+ * (nibble | bit << 4) - 16 times the block scale; x stays fp32.
+ * Replaces asm_matmul_q5 (src/kernels/x86_64/matmul_q5_avx2.asm:7-23,91-210;
+ * src/kernels/arm64/matmul_q5_neon.S) and asm_matmul_q5_mt
+ * (matmul_q5_avx2.asm:241-250; num_threads ignored); layout
+ * tests/reference/ops.py:67-92. */
+ASMLLM_API void asm_matmul_q5(const uint8_t* ql, const uint8_t* qh, const float* scales,
+                              const float* x, float* y, int64_t M, int64_t K);
+ASMLLM_API void asm_matmul_q5_mt(const uint8_t* ql, const uint8_t* qh, const float* scales,
+                                 const float* x, float* y, int64_t M, int64_t K, int num_threads);
+
 /* Pool management.  init records the thread count (returned by
  * get_num_threads) and creates this device's stream and staging state;
  * shutdown releases them and all registered weights.
@@ -291,11 +304,34 @@ typedef struct asm_fused_matvec {
   int32_t max_tokens;
   int32_t n_prompt; /* ARGMAX writes tokens[p+1] only when p+1 >= n_prompt */
   int64_t M, K;
+  /* Tensor parallelism (tp > 1; RESIDUAL and ARGMAX only).  RESIDUAL: this
+   * rank's partial rows of a row-parallel projection go to every rank's
+   * exchange buffer, each rank sums the tp partials in rank order and adds
+   * them to y (the residual stream, identical on all ranks).  ARGMAX: rows are
+   * this rank's vocabulary slice starting at vocab_offset; the ranks' maxima
+   * are exchanged and every rank picks the same token.  xchg[r] = rank r's
+   * exchange buffer (asm_ipc_alloc / asm_ipc_open), 2 * tp * xchg_rows 64-bit
+   * words, zero before first use; ar_seq = this rank's call counter (zero at
+   * start, advanced by each exchanging call); ar_done zero. */
+  int32_t tp, tp_rank, xchg_rows, vocab_offset;
+  void* xchg[8];
+  uint32_t* ar_seq;
+  uint32_t* ar_done;
 } asm_fused_matvec_t;
 
 /* One fused matvec of a decode step (see above).  Q4_0 / Q8_0 weights with
  * fp16 scales; SWIGLU needs M % 64 == 0. */
 ASMLLM_API int asm_fused_matvec_async(const asm_fused_matvec_t* p, void* stream);
+
+/* Device buffers shared between the processes of a tensor-parallel group
+ * (CUDA IPC over NVLink).  asm_ipc_alloc: zeroed device buffer of `bytes` on
+ * the current device plus its 64-byte handle; asm_ipc_open: maps a peer's
+ * buffer from its handle (peer access must be possible); asm_ipc_close
+ * unmaps it; asm_ipc_free frees an own buffer. */
+ASMLLM_API int asm_ipc_alloc(int64_t bytes, void** ptr, void* handle64);
+ASMLLM_API int asm_ipc_open(const void* handle64, void** ptr);
+ASMLLM_API int asm_ipc_close(void* ptr);
+ASMLLM_API int asm_ipc_free(void* ptr);
 
 /* RoPE + KV append + attention for position *pos of one layer, one CTA per
  * query head (reference generate.py:281-296 with ops.py:119-141 RoPE):
@@ -365,6 +401,10 @@ typedef struct asm_decode_model {
 ASMLLM_API int asm_decode_create(const asm_decode_model_t* model, void** handle);
 ASMLLM_API int asm_decode_run_async(void* handle, int32_t n_steps, int32_t n_prompt, void* stream);
 ASMLLM_API int asm_decode_destroy(void* handle);
+
+/* Q5_0 x fp32 on device pointers (see asm_matmul_q5), stream ordered. */
+ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const float* scales,
+                                   const float* x, float* y, int64_t M, int64_t K, void* stream);
 
 /* Kernel-path switches for testing and tuning; returns the previous value
  * (-1 for an unknown name).  "tma": 1 = Q8_0-activation matvecs use the

@@ -281,6 +281,44 @@ static void q8f32_avx2_rows(const int8_t* qw, const float* scales, const float* 
     }
 }
 
+/* Q5_0 x fp32, AVX2 (matmul_q5_avx2.asm:91-210).  Weight j of a block:
+ * n = (ql nibble j) | (bit j of qh) << 4, value n - 16, with nibble j = low
+ * nibble of ql byte j for j < 16, high nibble of ql byte j - 16 otherwise,
+ * and bit j = bit (j % 8) of qh byte j / 8 (tests/reference/ops.py:67-92).
+ * Lane l of slice s (weights 8s .. 8s+7) accumulates into blk[l]: value
+ * formed as (float(nibble) + (bit ? 16 : 0)) - 16 (exact), then
+ * fma(value, x, blk[l]) (:133-193); per block acc[l] = fma(blk[l], scale,
+ * acc[l]) (:196-197); the row is hsum8(acc) (:201-208). */
+static void q5f32_avx2_rows(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x,
+                            float* y, int64_t r0, int64_t r1, int64_t nb) {
+    for (int64_t r = r0; r < r1; ++r) {
+        float acc[8] = {0};
+        for (int64_t b = 0; b < nb; ++b) {
+            const uint8_t* lb = ql + (r * nb + b) * 16;
+            const uint8_t* hb = qh + (r * nb + b) * 4;
+            const float* xb = x + b * QK;
+            float blk[8] = {0};
+            for (int s = 0; s < 4; ++s) {
+                for (int l = 0; l < 8; ++l) {
+                    const int j = 8 * s + l;
+                    const int nib = j < 16 ? (lb[j] & 0x0F) : (lb[j - 16] >> 4);
+                    const int bit = (hb[s] >> l) & 1;
+                    const float v = ((float)nib + (bit ? 16.0f : 0.0f)) - 16.0f;
+                    blk[l] = fmaf(v, xb[j], blk[l]);
+                }
+            }
+            const float sc = scales[r * nb + b];
+            for (int l = 0; l < 8; ++l) acc[l] = fmaf(blk[l], sc, acc[l]);
+        }
+        y[r] = hsum8(acc);
+    }
+}
+
+void ref_matmul_q5f32_avx2(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x,
+                           float* y, int64_t M, int64_t K) {
+    q5f32_avx2_rows(ql, qh, scales, x, y, 0, M, K / QK);
+}
+
 void ref_matmul_q4f32_avx2(const uint8_t* qs, const float* scales, const float* x, float* y,
                            int64_t M, int64_t K) {
     q4f32_avx2_rows(qs, scales, x, y, 0, M, K / QK);

@@ -55,6 +55,8 @@ def lib() -> ctypes.CDLL:
         L.ref_q8q8_block_sums.restype = None
         L.ref_mt_tile_rows.argtypes = [i64, ctypes.c_int]
         L.ref_mt_tile_rows.restype = i64
+        L.ref_matmul_q5f32_avx2.argtypes = [vp, vp, vp, vp, vp, i64, i64]
+        L.ref_matmul_q5f32_avx2.restype = None
         L.ref_matmul_mt.argtypes = [ctypes.c_int, vp, vp, vp, vp, i64, i64, ctypes.c_int]
         L.ref_matmul_mt.restype = ctypes.c_int
         _lib = L
@@ -138,6 +140,19 @@ def matmul_q8f32_avx2(qw, scales, x, M=None, K=None):
     M = M if M is not None else np.asarray(qw).shape[0]
     K = K if K is not None else np.asarray(x).shape[-1]
     return _matvec("ref_matmul_q8f32_avx2", np.int8, qw, scales, x, M, K)
+
+
+def matmul_q5f32_avx2(ql, qh, scales, x, M=None, K=None):
+    """asm_matmul_q5 (Q5_0 x fp32, AVX2 lane structure): ql [M, K/32, 16], qh [M, K/32, 4]."""
+    M = M if M is not None else np.asarray(ql).shape[0]
+    K = K if K is not None else np.asarray(x).shape[-1]
+    ql, pl = _c(ql, np.uint8)
+    qh, ph = _c(qh, np.uint8)
+    s, ps = _c(scales, np.float32)
+    x, px = _c(x, np.float32)
+    y = np.zeros(M, dtype=np.float32)
+    lib().ref_matmul_q5f32_avx2(pl, ph, ps, px, y.ctypes.data, M, K)
+    return y
 
 
 def matmul_q8f32_neon(qw, scales, x, M=None, K=None):

@@ -6,6 +6,7 @@ model decoded twice on the CPU."""
 from __future__ import annotations
 
 import ctypes
+import re
 
 import numpy as np
 import pytest
@@ -44,14 +45,17 @@ def test_softmax_matches_reference(glue, DO):
 
 
 def test_descriptor_layout_matches_header():
-    # asm_fused_matvec_t on LP64: 2 int32, 15 pointers, float + 3 int32, 2 int64
-    assert ctypes.sizeof(native.FusedMatvec) == 160
+    # asm_fused_matvec_t on LP64: 2 int32, 15 pointers, float + 3 int32, 2 int64,
+    # 4 int32, 8 + 2 pointers
+    assert ctypes.sizeof(native.FusedMatvec) == 256
     assert native.FusedMatvec.eps.offset == 128 and native.FusedMatvec.M.offset == 144
+    assert native.FusedMatvec.xchg.offset == 176
     text = (GOLDEN.parent.parent / "include" / "asmllm.h").read_text()
     body = text[text.index("typedef struct asm_fused_matvec"):text.index("} asm_fused_matvec_t;")]
+    body = re.sub(r"/\*.*?\*/", " ", body, flags=re.S)  # declarations only
     names = [f for f, _ in native.FusedMatvec._fields_]
     pos = [body.index(f" {n};") if f" {n};" in body else body.index(f" {n},") if f" {n}," in body
-           else body.index(f"*{n};") for n in names]
+           else body.index(f"*{n};") if f"*{n};" in body else body.index(f" {n}[") for n in names]
     assert pos == sorted(pos), "field order differs from include/asmllm.h"
 
 

@@ -208,3 +208,26 @@ def test_mt_equals_single_thread(oracle):
     for kind, w, single in ((oracle.K_Q4Q8, q4, oracle.matmul_q4q8), (oracle.K_Q8Q8, q8, oracle.matmul_q8q8),
                             (oracle.K_Q4F32, q4, oracle.matmul_q4f32_avx2), (oracle.K_Q8F32, q8, oracle.matmul_q8f32_avx2)):
         assert np.array_equal(oracle.matmul_mt(kind, w, s, x, M, K, 5), single(w, s, x))
+
+
+def test_q5_avx2_restatement_matches_reference_fixture(golden, oracle):
+    # tools/reference_gen.py:61-70: the numpy Q5_0 x fp32 expectation of the seed-42 fixture
+    y = oracle.matmul_q5f32_avx2(golden["q5_matmul_ql"], golden["q5_matmul_qh"], golden["q5_matmul_scales"],
+                                 golden["q5_matmul_x"])
+    e = golden["q5_matmul_expected"]
+    assert float(np.abs(y - e).max() / np.abs(e).max()) <= 1e-5
+
+
+def test_q5_known_answer(oracle):
+    # one block: ql byte j = j (low nibble j, high nibble 0), qh = 0xFFFFFFFF (every fifth bit set)
+    ql = np.arange(16, dtype=np.uint8).reshape(1, 1, 16)
+    qh = np.full((1, 1, 4), 0xFF, dtype=np.uint8)
+    x = np.zeros(32, dtype=np.float32)
+    x[5] = 1.0    # weight 5: (5 | 16) - 16 = 5
+    x[20] = 2.0   # weight 20: high nibble of byte 4 = 0 -> (0 | 16) - 16 = 0
+    x[31] = -1.0  # weight 31: 0 -> 0
+    y = oracle.matmul_q5f32_avx2(ql, qh, np.array([[0.5]], np.float32), x)
+    assert y[0] == 2.5
+    qh0 = np.zeros((1, 1, 4), dtype=np.uint8)  # no fifth bits: weight 5 = 5 - 16 = -11, weight 20 = -16
+    y = oracle.matmul_q5f32_avx2(ql, qh0, np.array([[1.0]], np.float32), x)
+    assert y[0] == -11.0 - 32.0 + 16.0

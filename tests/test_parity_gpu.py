@@ -371,3 +371,52 @@ def test_gguf_split(cuda, fmt, f16):
     qs, sc = ops.gguf_split_dev(fmt, dev(cuda, raw), nblk, scales_f16=f16)
     assert np.array_equal(qs.cpu().numpy().reshape(w.shape), w)
     assert np.array_equal(sc.float().cpu().numpy().reshape(s.shape), s)
+
+
+# --------------------------------------------------------------------------
+# Q5_0 x fp32 (asm_matmul_q5, row f4)
+# --------------------------------------------------------------------------
+
+def q5_weights(M, K, seed):
+    rng = np.random.default_rng(seed)
+    ql = rng.integers(0, 256, (M, K // 32, 16), dtype=np.uint8)
+    qh = rng.integers(0, 256, (M, K // 32, 4), dtype=np.uint8)
+    s = np.abs(rng.standard_normal((M, K // 32), dtype=np.float32) * np.float32(0.02))
+    return ql, qh, s.astype(np.float16).astype(np.float32)
+
+
+@pytest.mark.parametrize("M,K", [(1, 32), (37, 96), (4096, 4096), (11008, 4096), (4096, 11008)])
+def test_q5_matvec_matches_oracle(cuda, oracle, M, K):
+    torch = cuda
+    ql, qh, s = q5_weights(M, K, seed=70 + M)
+    x = synth.activation(K, seed=71)
+    ref = oracle.matmul_q5f32_avx2(ql, qh, s, x)
+    y = native_q5_dev(torch, ql, qh, s, x)
+    assert rel_err(y, ref) <= YTOL
+    yh = np.zeros(M, dtype=np.float32)  # synchronous entry, host buffers
+    native.lib().asm_matmul_q5(ql.ctypes.data, qh.ctypes.data, s.ctypes.data, x.ctypes.data, yh.ctypes.data, M, K)
+    native.check()
+    assert rel_err(yh, ref) <= YTOL
+
+
+def native_q5_dev(torch, ql, qh, s, x):
+    dl, dh, ds, dx = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (ql, qh, s, x))
+    y = torch.full((ql.shape[0],), float("nan"), device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = native.lib().asm_matmul_q5_async(dl.data_ptr(), dh.data_ptr(), ds.data_ptr(), dx.data_ptr(), y.data_ptr(),
+                                          ql.shape[0], x.shape[0], st)
+    native.check(rc)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def test_q5_rejects_bad_arguments(cuda):
+    torch = cuda
+    ql = torch.zeros((4, 1, 16), dtype=torch.uint8, device="cuda")
+    x = torch.zeros(32, device="cuda")
+    y = torch.zeros(4, device="cuda")
+    L = native.lib()
+    rc = L.asm_matmul_q5_async(ql.data_ptr(), ql.data_ptr() + 1, x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 32, None)
+    assert rc == native.ASM_E_INVALID and "aligned" in native.last_error()[1]
+    rc = L.asm_matmul_q5_async(ql.data_ptr(), ql.data_ptr(), x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 33, None)
+    assert rc == native.ASM_E_INVALID

@@ -137,6 +137,12 @@ size_t q5_smem_bytes(int64_t K);
 cudaError_t launch_q5_matvec(const uint8_t* ql, const uint8_t* qh, const float* scales, const float* x, float* y,
                              int64_t M, int64_t K, cudaStream_t stream);
 
+// Batched Q4_0 / Q8_0 x Q8_0 product on the tensor cores (prefill_gemm.cu):
+// y [N][M] from N activation-image rows (row stride img_stride bytes), fp16 scales.
+size_t gemm_smem_bytes();
+cudaError_t launch_q8act_gemm(int fmt, const void* w, const void* scales_f16, const void* images, size_t img_stride,
+                              float* y, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+
 extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
 extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch
 

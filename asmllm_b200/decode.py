@@ -208,7 +208,7 @@ class LlamaDecoder:
     """
 
     def __init__(self, shape: LlamaShape, ctx: int = 512, max_tokens: int | None = None, seed: int = 0,
-                 fmt: int = FMT_Q4_0, device=None, tp: int = 1, tp_rank: int = 0, group=None):
+                 fmt: int = FMT_Q4_0, device=None, tp: int = 1, tp_rank: int = 0, group=None, weights=None):
         import torch
 
         self.torch = torch
@@ -224,7 +224,7 @@ class LlamaDecoder:
         self.tp, self.tp_rank = tp, tp_rank
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
-        W = make_weights(s, sh, seed, fmt, dev)
+        W = weights if weights is not None else make_weights(s, sh, seed, fmt, dev)
         self.layers, self.final_norm, self.lm_head, self.embed = W["layers"], W["final_norm"], W["lm_head"], W["embed"]
         hd = s.head_dim
         nh_l, nkv_l, ffn_l = len(sh.heads), len(sh.kv_heads), len(sh.ffn)
@@ -474,6 +474,103 @@ class LlamaDecoder:
                 "attn_norm": L["attn_norm"].cpu().numpy(), "ffn_norm": L["ffn_norm"].cpu().numpy(),
             })
         return out
+
+    # ------------------------------------------------------------------ GGUF
+    @classmethod
+    def from_gguf(cls, path, ctx: int = 512, max_tokens: int | None = None, device=None):
+        """A Llama model from a GGUF file (llama.* metadata, Q4_0 or Q8_0 linear
+        weights, F32 norms; the embedding may be F32, F16, Q4_0 or Q8_0).  Each
+        linear weight is uploaded once and split on the device."""
+        import torch
+
+        from . import gguf as G
+
+        gg = G.GGUFFile(path)
+        md = gg.metadata
+        arch = md.get("general.architecture", "llama")
+        dim = int(md[f"{arch}.embedding_length"])
+        n_heads = int(md[f"{arch}.attention.head_count"])
+        shape = LlamaShape(n_layers=int(md[f"{arch}.block_count"]), dim=dim, n_heads=n_heads,
+                           n_kv_heads=int(md.get(f"{arch}.attention.head_count_kv", n_heads)),
+                           head_dim=dim // n_heads, ffn=int(md[f"{arch}.feed_forward_length"]),
+                           vocab=gg.tensors["token_embd.weight"].rows,
+                           eps=float(md.get(f"{arch}.attention.layer_norm_rms_epsilon", 1e-5)),
+                           theta=float(md.get(f"{arch}.rope.freq_base", 10000.0)))
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        types = {gg.tensors[n].type for n in gg.tensors if n.endswith(".weight") and "norm" not in n
+                 and n != "token_embd.weight"}
+        if types - {G.GGML_Q4_0, G.GGML_Q8_0} or len(types) != 1:
+            raise ValueError(f"{path}: linear weights must all be Q4_0 or all Q8_0 (types {sorted(types)})")
+        fmt = FMT_Q4_0 if types == {G.GGML_Q4_0} else FMT_Q8_0
+
+        def up(name):
+            return G.upload(gg, name, dev)
+
+        def vec(name):
+            return torch.from_numpy(gg.array(name).reshape(-1).copy()).to(dev)
+
+        layers = []
+        for i in range(shape.n_layers):
+            q, k, v = up(f"blk.{i}.attn_q.weight"), up(f"blk.{i}.attn_k.weight"), up(f"blk.{i}.attn_v.weight")
+            g, u = up(f"blk.{i}.ffn_gate.weight"), up(f"blk.{i}.ffn_up.weight")
+            layers.append({
+                "wqkv": (torch.cat([q[0], k[0], v[0]]).contiguous(), torch.cat([q[1], k[1], v[1]]).contiguous()),
+                "wo": up(f"blk.{i}.attn_output.weight"),
+                "wgu": (torch.stack([g[0], u[0]], 1).reshape(2 * shape.ffn, *g[0].shape[1:]).contiguous(),
+                        torch.stack([g[1], u[1]], 1).reshape(2 * shape.ffn, g[1].shape[1]).contiguous()),
+                "wdown": up(f"blk.{i}.ffn_down.weight"),
+                "attn_norm": vec(f"blk.{i}.attn_norm.weight"), "ffn_norm": vec(f"blk.{i}.ffn_norm.weight"),
+            })
+        et = gg.tensors["token_embd.weight"]
+        if et.type in (G.GGML_F32, G.GGML_F16):
+            embed = torch.from_numpy(gg.array("token_embd.weight")).to(dev)
+        else:  # dequantize the table once on the device: (q - 8 | q) * d
+            eq, ed = up("token_embd.weight")
+            vals = eq.float() if et.type == G.GGML_Q8_0 else torch.cat([(eq & 0x0F), (eq >> 4)], -1).float() - 8.0
+            embed = (vals * ed.float().unsqueeze(-1)).reshape(et.rows, et.cols).contiguous()
+        W = {"layers": layers, "final_norm": vec("output_norm.weight"), "lm_head": up("output.weight"),
+             "embed": embed}
+        return cls(shape, ctx=ctx, max_tokens=max_tokens, fmt=fmt, device=dev, weights=W)
+
+    def to_gguf(self, path) -> None:
+        """Writes this model (tp = 1) as a GGUF file that from_gguf reads back."""
+        from . import gguf as G
+
+        if self.tp != 1:
+            raise ValueError("to_gguf needs the whole model (tp = 1)")
+        s = self.shape
+        gt = G.GGML_Q4_0 if self.fmt == FMT_Q4_0 else G.GGML_Q8_0
+        qd, kvd = s.n_heads * s.head_dim, s.n_kv_heads * s.head_dim
+        tensors = []
+
+        def lin(name, qs, sc):
+            qs, sc = qs.cpu().numpy(), sc.float().cpu().numpy()
+            tensors.append((name, (qs.shape[1] * 32, qs.shape[0]), gt, G.blocks_from_planes(qs, sc)))
+
+        def f32(name, t):
+            a = t.float().cpu().numpy()
+            tensors.append((name, tuple(reversed(a.shape)), G.GGML_F32, a.tobytes()))
+
+        f32("token_embd.weight", self.embed)
+        for i, L in enumerate(self.layers):
+            q, sc = L["wqkv"]
+            lin(f"blk.{i}.attn_q.weight", q[:qd], sc[:qd])
+            lin(f"blk.{i}.attn_k.weight", q[qd:qd + kvd], sc[qd:qd + kvd])
+            lin(f"blk.{i}.attn_v.weight", q[qd + kvd:], sc[qd + kvd:])
+            lin(f"blk.{i}.attn_output.weight", *L["wo"])
+            gq, gs = L["wgu"]
+            lin(f"blk.{i}.ffn_gate.weight", gq[0::2], gs[0::2])
+            lin(f"blk.{i}.ffn_up.weight", gq[1::2], gs[1::2])
+            lin(f"blk.{i}.ffn_down.weight", *L["wdown"])
+            f32(f"blk.{i}.attn_norm.weight", L["attn_norm"])
+            f32(f"blk.{i}.ffn_norm.weight", L["ffn_norm"])
+        f32("output_norm.weight", self.final_norm)
+        lin("output.weight", *self.lm_head)
+        md = {"general.architecture": "llama", "llama.embedding_length": s.dim, "llama.block_count": s.n_layers,
+              "llama.feed_forward_length": s.ffn, "llama.attention.head_count": s.n_heads,
+              "llama.attention.head_count_kv": s.n_kv_heads, "llama.attention.layer_norm_rms_epsilon": float(s.eps),
+              "llama.rope.freq_base": float(s.theta), "llama.context_length": self.ctx}
+        G.write_gguf(path, md, tensors)
 
     def close(self):
         if self._handle is not None:

@@ -75,6 +75,7 @@ SIGNATURES = {
     "asm_matmul_q5": ([vp, vp, vp, vp, vp, i64, i64], None),
     "asm_matmul_q5_mt": ([vp, vp, vp, vp, vp, i64, i64, c_int], None),
     "asm_matmul_q5_async": ([vp, vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_gemm_image_async": ([c_int, vp, vp, vp, i64, vp, i64, i64, i64, vp], c_int),
     # additions
     "asm_matmul_q8q8": ([vp, vp, vp, vp, i64, i64], None),
     "asm_quantize_q8_0": ([vp, vp, vp, i64], None),

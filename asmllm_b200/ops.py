@@ -359,3 +359,28 @@ def attention_decode(qkv, k_cache, v_cache, rope_cs, pos, image_out, n_heads: in
                                       _stream_handle(stream))
     native.check(rc)
     return image_out
+
+
+def gemm_image(fmt: int, qweights, scales, images, K: int, out=None, stream=None):
+    """Y [N, M] = the matvec of every activation-image row (uint8 [N, bytes]), on the
+    tensor cores (asm_gemm_image_async).  Scales fp16 [M, K/32]."""
+    torch = _torch()
+    wdt = torch.uint8 if fmt == FMT_Q4_0 else torch.int8
+    _check_dev(qweights, (wdt,), "qweights")
+    _check_dev(scales, (torch.float16,), "scales")
+    _check_dev(images, (torch.uint8,), "images")
+    M = scales.shape[0]
+    N = images.shape[0]
+    if out is None:
+        out = torch.empty((N, M), dtype=torch.float32, device=images.device)
+    rc = native.lib().asm_gemm_image_async(fmt, _ptr(qweights), _ptr(scales), _ptr(images), images.stride(0),
+                                           _ptr(out), M, N, K, _stream_handle(stream))
+    native.check(rc)
+    return out
+
+
+def gemm(fmt: int, qweights, scales, X, out=None, stream=None):
+    """Y [N, M] = W x_n for the N rows of X fp32 [N, K]: quantize every row to Q8_0
+    (asm_act_image_q8_0_async), then the tensor-core product."""
+    img = act_image_dev(X, stream=stream)
+    return gemm_image(fmt, qweights, scales, img, X.shape[-1], out=out, stream=stream)

@@ -238,6 +238,8 @@ def main():
                     help="greedy steps of the 7B batch-1 decode timed after the matvec sweep (0: skip)")
     ap.add_argument("--decode70-steps", type=int, default=64,
                     help="greedy steps of the Llama-2-70B-shape decode, tensor-parallel over the N GPUs (0: skip)")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the batched (prefill) tensor-core product at N = 8, 64, 512 tokens")
     ap.add_argument("--mode", choices=["image", "fused"], default="fused",
                     help="image: activation-quantize pre-pass kernel + matvec (2 launches per matvec); "
                          "fused: quantize inside the matvec (1 launch)")
@@ -528,6 +530,36 @@ def main():
         del dec
         torch.cuda.empty_cache()
 
+    # ---- prefill: batched Q4_0 x Q8_0 product on the tensor cores ----
+    prefill = None
+    if not args.no_prefill:
+        gen.manual_seed(base + 33)
+        pre_shapes = [(4096, 4096), (11008, 4096), (4096, 11008)]
+        Wp = [make_q4(M, K, base + 40 + i) for i, (M, K) in enumerate(pre_shapes)]
+        prefill = {}
+        for N in (8, 64, 512):
+            row = {}
+            for (qs, d), (M, K) in zip(Wp, pre_shapes):
+                X = torch.randn((N, K), device=dev, generator=gen)
+                img = ops.act_image_dev(X)
+                out = torch.empty((N, M), device=dev)
+                for _ in range(3):
+                    ops.gemm_image(FMT_Q4_0, qs, d, img, K, out=out)
+                torch.cuda.synchronize()
+                reps = 20
+                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a0.record()
+                for _ in range(reps):
+                    ops.gemm_image(FMT_Q4_0, qs, d, img, K, out=out)
+                a1.record()
+                a1.synchronize()
+                t = a0.elapsed_time(a1) / reps / 1e3
+                row[f"{M}x{K}"] = {"us": round(t * 1e6, 2), "TOPS": round(2.0 * M * N * K / t / 1e12, 1),
+                                   "weight_GB/s": round(q4_bytes(M, K) / t / 1e9, 1)}
+            prefill[f"N={N}"] = row
+        del Wp
+        torch.cuda.empty_cache()
+
     # ---- Llama-2-70B-shape batch-1 decode, tensor-parallel over the N GPUs ----
     decode70 = None
     if args.decode70_steps > 0:
@@ -641,6 +673,15 @@ def main():
             decode["reference_cpu_estimate_basis"] = ("weight bytes per token / the cpu_baseline matvec GB/s "
                                                       "(derived, not a measured reference decode)")
         line["decode_7b"] = decode
+    if prefill is not None:
+        pk = ROOT / "MEASURED_PEAKS.json"
+        bf16 = float(json.loads(pk.read_text()).get("bf16_tflops", 0.0)) if pk.exists() else 0.0
+        line["prefill_gemm"] = {
+            "kernel": "tcgen05.mma kind::i8 (M=128 rows x N=64 tokens x K=32 per block) with the per-32-block "
+                      "scales applied from tensor memory in fp32; Q4_0 expanded to int8 in shared memory",
+            "ops": "2*M*N*K int8 multiply-adds per call", "per_shape": prefill,
+            "peak_note": f"dense int8 tensor peak = 2x the measured bf16 {bf16} TFLOP/s (MEASURED_PEAKS.json)",
+        }
     if decode70 is not None:
         decode70["frac_of_measured_hbm"] = round(decode70["achieved_GB/s_per_gpu"] / peak, 4)
         # every GPU streams its 1/N of the weights and KV per token at the measured copy peak

@@ -402,6 +402,18 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* model, void** handle)
 ASMLLM_API int asm_decode_run_async(void* handle, int32_t n_steps, int32_t n_prompt, void* stream);
 ASMLLM_API int asm_decode_destroy(void* handle);
 
+/* Batched (prefill) Q4_0 / Q8_0 x Q8_0 product on the tensor cores:
+ * y [N][M] fp32, row n = the matvec of activation row n, from N rows of
+ * Q8_0 activation images (asm_act_image_q8_0_async with N rows; row stride
+ * image_stride bytes, a multiple of 16).  Each output is the reference's
+ * NEON combine for that row and token (s = wd * xd, acc = fma(float(isum),
+ * s, acc) over the blocks in order), so it equals the Q4_0 x Q8_0 matvec of
+ * the reference semantics bit for bit.  fp16 scales.  No single counterpart
+ * in the reference (its batched work is one asm_matmul_q4 call per token). */
+ASMLLM_API int asm_gemm_image_async(int fmt, const void* qweights, const void* scales_f16, const void* images,
+                                    int64_t image_stride, float* y, int64_t M, int64_t N, int64_t K,
+                                    void* stream);
+
 /* Q5_0 x fp32 on device pointers (see asm_matmul_q5), stream ordered. */
 ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const float* scales,
                                    const float* x, float* y, int64_t M, int64_t K, void* stream);

@@ -19,8 +19,15 @@ It imports the reference's own Python (no copy of it lives in this repo):
     the decode-step glue of generate.py:255-326, on seeded inputs
     (np.random.default_rng(7)) at the 7B shapes (dim 4096, head_dim 128).
 
+  * src/runtime/generate.py:38-88 load_gguf_tensors_and_vocab -- the
+    reference's GGUF parser, run on tiny.gguf (a small GGUF v3 file written
+    here by asmllm_b200.gguf.write_gguf: metadata of several types, a token
+    list, Q4_0 / Q8_0 / F32 tensors); its tensor table, data offset and
+    vocabulary are stored in tiny_gguf_ref.json.
+
 Outputs: reference_seed42.npz (small fixture, all arrays),
-bench_recipes.npz (expected y vectors + input digests) and decode_glue.npz.
+bench_recipes.npz (expected y vectors + input digests), decode_glue.npz,
+tiny.gguf and tiny_gguf_ref.json.
 """
 from __future__ import annotations
 
@@ -113,7 +120,30 @@ def main() -> None:
     g["softmax_x"] = (8.0 * rng.standard_normal(143)).astype(np.float32)
     g["softmax_y"] = ref_softmax(g["softmax_x"])
     np.savez_compressed(HERE / "decode_glue.npz", **g)
-    print("wrote", HERE / "reference_seed42.npz", HERE / "bench_recipes.npz", "and", HERE / "decode_glue.npz")
+
+    import json
+
+    sys.path.insert(0, str(HERE.parent.parent))
+    from asmllm_b200 import gguf as G  # noqa: E402
+    from src.runtime.generate import load_gguf_tensors_and_vocab  # noqa: E402
+    rng = np.random.default_rng(5)
+    q4 = rng.integers(0, 256, (4, 2, 16), dtype=np.uint8)
+    s4 = np.abs(rng.standard_normal((4, 2))).astype(np.float16).astype(np.float32)
+    q8 = rng.integers(-127, 128, (3, 1, 32), dtype=np.int8)
+    s8 = np.abs(rng.standard_normal((3, 1))).astype(np.float16).astype(np.float32)
+    f = rng.standard_normal(32).astype(np.float32)
+    G.write_gguf(HERE / "tiny.gguf",
+                 {"general.architecture": "llama", "llama.block_count": 1, "llama.rope.freq_base": 10000.0,
+                  "general.name": "tiny", "tokenizer.ggml.tokens": ["<s>", "</s>", "a", "b"],
+                  "tokenizer.ggml.scores": [0.0, 0.5, 1.0, 1.5], "general.file_type": 2},
+                 [("blk.0.attn_q.weight", (64, 4), G.GGML_Q4_0, G.blocks_from_planes(q4, s4)),
+                  ("blk.0.attn_k.weight", (32, 3), G.GGML_Q8_0, G.blocks_from_planes(q8, s8)),
+                  ("output_norm.weight", (32,), G.GGML_F32, f.tobytes())])
+    tensors, data_offset, data, vocab = load_gguf_tensors_and_vocab(str(HERE / "tiny.gguf"))
+    with open(HERE / "tiny_gguf_ref.json", "w") as fh:
+        json.dump({"tensors": {k: [list(v[0]), v[1], v[2]] for k, v in tensors.items()},
+                   "data_offset": data_offset, "data_len": len(data), "vocab": vocab}, fh, indent=1)
+    print("wrote the fixtures in", HERE)
 
 
 if __name__ == "__main__":

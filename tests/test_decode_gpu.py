@@ -388,3 +388,25 @@ def test_persistent_engine_refuses_runs_past_the_cache(cuda):
         assert dec.position() == 7 and ops.device_error() == 0
     finally:
         dec.close()
+
+
+def test_gguf_round_trip_decodes_identically(cuda, tmp_path):
+    # the model written as GGUF (Q4_0 linear weights, F32 embedding and norms), read
+    # back with one upload + device split per tensor, decodes bit for bit the same
+    torch = cuda
+    dec = D.LlamaDecoder(SMALL_GQA, ctx=32, seed=17)
+    try:
+        prompt = [4, 8, 15]
+        toks = dec.generate(prompt, 6, engine="graph")
+        lg = dec.logits.clone()
+        dec.to_gguf(tmp_path / "m.gguf")
+    finally:
+        dec.close()
+    back = D.LlamaDecoder.from_gguf(tmp_path / "m.gguf", ctx=32)
+    try:
+        assert back.shape == SMALL_GQA and back.fmt == FMT_Q4_0
+        assert back.generate(prompt, 6, engine="graph") == toks
+        assert torch.equal(back.logits, lg)
+        assert back.generate(prompt, 6, engine="persistent") == toks
+    finally:
+        back.close()

@@ -3,11 +3,15 @@
     python -m asmllm_b200.profdrive [--fmt q4|q8] [--mode fused|image] [--launches N]
                                     [--path tma|ldg] MxK [MxK ...]
     python -m asmllm_b200.profdrive --decode N [--layers L] [--warm W]
+    python -m asmllm_b200.profdrive --gemm N [--launches L] MxK [MxK ...]
 
 For each shape it builds one weight matrix on cuda:0 (random seeded quants,
 fp16 scales, declared static like model weights), then runs N matvecs
 (default 2) on torch's current stream.  Device memory stays at the size of
 the largest matrix, so an ncu capture of it ends quickly.
+
+--gemm N runs the tensor-core batched product (N tokens, Q4_0) L times per
+shape, from one activation image of N rows.
 
 --decode N builds the random-init Llama-7B-shaped decoder (L layers, default
 32: 4.2 GB on the device), runs W greedy steps through CUDA graphs (default
@@ -27,6 +31,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("shapes", nargs="*")
     ap.add_argument("--decode", type=int, default=0)
+    ap.add_argument("--gemm", type=int, default=0)
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--warm", type=int, default=24)
     ap.add_argument("--fmt", choices=["q4", "q8"], default="q4")
@@ -49,6 +54,23 @@ def main() -> None:
         dec.close()
         raise SystemExit(1 if err else 0)
     fmt = FMT_Q4_0 if args.fmt == "q4" else FMT_Q8_0
+    if args.gemm:
+        dev = torch.device("cuda", 0)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(0)
+        for shape in args.shapes:
+            M, K = (int(v) for v in shape.lower().split("x"))
+            qs = torch.randint(0, 256, (M, K // 32, 16), dtype=torch.uint8, device=dev, generator=gen)
+            d = torch.randn((M, K // 32), device=dev, generator=gen).abs_().mul_(0.02).half()
+            img = ops.act_image_dev(torch.randn((args.gemm, K), device=dev, generator=gen))
+            out = torch.empty((args.gemm, M), device=dev)
+            for _ in range(args.launches):
+                ops.gemm_image(FMT_Q4_0, qs, d, img, K, out=out)
+            torch.cuda.synchronize()
+        err = ops.device_error()
+        print(f"profdrive: gemm N={args.gemm}, {len(args.shapes)} shape(s) x {args.launches} launch(es), "
+              f"device error word {err}")
+        raise SystemExit(1 if err else 0)
     ops.set_option("tma", 1 if args.path == "tma" else 0)
     dev = torch.device("cuda", 0)
     gen = torch.Generator(device=dev)

@@ -19,6 +19,13 @@
 // expanded to int8 (nibble - 8) in shared memory (the "in-SMEM dequantised
 // tiles"); activations are copied as they are.
 //
+// Pipelining: chunks of kKB blocks are staged into two shared-memory buffers;
+// while the tensor core and the epilogue work on chunk c, every thread holds
+// its global loads for chunk c+1 in registers and stores them (expanding the
+// nibbles) into the other buffer afterwards.  The epilogue uses the packed
+// fp32x2 multiply and fma (two IEEE fp32 operations per instruction, the
+// same rounding as the scalar ones).
+//
 // Shared-memory operand layout (no swizzle, K-major "core matrices" of 8
 // rows x 16 bytes): element (row, k) of block b at
 //   b * tile + (row / 8) * 256 + (k / 16) * 128 + (row % 8) * 16 + k % 16
@@ -109,18 +116,102 @@ __device__ __forceinline__ void q4_to_i8(uint4 q, uint4& lo, uint4& hi) {
   ex(q.w, lo.w, hi.w);
 }
 
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+
+__device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+// acc += float(d) * (wd * xd) for two tokens at once, each element rounded as
+// the scalar fmul / fma.
+__device__ __forceinline__ unsigned long long scale_acc2(unsigned long long acc, int d0, int d1, float wd,
+                                                         unsigned long long xd2) {
+  unsigned long long s, dv, r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(s) : "l"(pack2(wd, wd)), "l"(xd2));
+  dv = pack2(__int2float_rn(d0), __int2float_rn(d1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(dv), "l"(s), "l"(acc));
+  return r;
+}
+
+// Staging registers of one chunk for one thread: its row's kKB weight blocks
+// (and scales) and its share of the activation blocks.
+struct ChunkRegs {
+  uint4 a[kKB][2];
+  float wd[kKB];
+  uint4 bv[kKB * kGN * 2 / kGThreads];
+  float bxd[kKB * kGN * 2 / kGThreads];
+};
+
+template <int FMT>
+__device__ __forceinline__ void load_chunk(ChunkRegs& R, const uint8_t* __restrict__ w,
+                                           const __half* __restrict__ scales, const unsigned char* __restrict__ images,
+                                           size_t img_stride, int row, int M, int N, int nb, int n0, int c0, int kb,
+                                           int tid) {
+  constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;
+#pragma unroll
+  for (int b = 0; b < kKB; ++b) {
+    R.a[b][0] = R.a[b][1] = make_uint4(0u, 0u, 0u, 0u);
+    R.wd[b] = 0.0f;
+    if (b < kb && row < M) {
+      const uint8_t* src = w + ((size_t)row * nb + c0 + b) * UB;
+      R.a[b][0] = *reinterpret_cast<const uint4*>(src);
+      if (FMT != kFmtQ4_0) R.a[b][1] = *reinterpret_cast<const uint4*>(src + 16);
+      R.wd[b] = __half2float(scales[(size_t)row * nb + c0 + b]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kKB * kGN * 2 / kGThreads; ++j) {
+    const int i = tid + j * kGThreads;
+    const int half = i & 1, tb = i >> 1, n = tb % kGN, b = tb / kGN;
+    R.bv[j] = make_uint4(0u, 0u, 0u, 0u);
+    R.bxd[j] = 0.0f;
+    if (b < kb && n0 + n < N) {
+      const unsigned char* im = images + (size_t)(n0 + n) * img_stride;
+      R.bv[j] = __ldcg(reinterpret_cast<const uint4*>(im + (size_t)(c0 + b) * 48) + half);
+      if (half == 0) R.bxd[j] = __ldcg(reinterpret_cast<const float2*>(im + (size_t)nb * 48) + c0 + b).x;
+    }
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ void store_chunk(const ChunkRegs& R, unsigned char* sA, unsigned char* sB, float* sWd,
+                                            float* sXd, int tid) {
+  const int g = tid >> 3, r = tid & 7;
+#pragma unroll
+  for (int b = 0; b < kKB; ++b) {
+    uint4 lo = R.a[b][0], hi = R.a[b][1];
+    if (FMT == kFmtQ4_0) q4_to_i8(R.a[b][0], lo, hi);
+    unsigned char* t = sA + b * kATile + g * 256 + r * 16;
+    *reinterpret_cast<uint4*>(t) = lo;
+    *reinterpret_cast<uint4*>(t + 128) = hi;
+    sWd[b * kGM + tid] = R.wd[b];
+  }
+#pragma unroll
+  for (int j = 0; j < kKB * kGN * 2 / kGThreads; ++j) {
+    const int i = tid + j * kGThreads;
+    const int half = i & 1, tb = i >> 1, n = tb % kGN, b = tb / kGN;
+    *reinterpret_cast<uint4*>(sB + b * kBTile + (n >> 3) * 256 + half * 128 + (n & 7) * 16) = R.bv[j];
+    if (half == 0) sXd[b * kGN + n] = R.bxd[j];
+  }
+}
+
 template <int FMT>
 __global__ void __launch_bounds__(kGThreads, 1)
 q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scales,
                   const unsigned char* __restrict__ images, size_t img_stride, float* __restrict__ y, int M,
                   int N, int nb, unsigned* __restrict__ err) {
   extern __shared__ __align__(1024) unsigned char smem[];
-  unsigned char* sA = smem;                                 // [kKB][kATile]
-  unsigned char* sB = sA + kKB * kATile;                    // [kKB][kBTile]
-  float* sWd = reinterpret_cast<float*>(sB + kKB * kBTile);  // [kKB][kGM]
-  float* sXd = sWd + kKB * kGM;                             // [kKB][kGN]
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(sXd + kKB * kGN);  // [2]
+  constexpr size_t kBuf = (size_t)kKB * (kATile + kBTile) + (size_t)kKB * (kGM + kGN) * sizeof(float);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + 2 * kBuf);  // [2]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mbar + 2);
+  auto bufA = [&](int s) { return smem + s * kBuf; };
+  auto bufB = [&](int s) { return smem + s * kBuf + kKB * kATile; };
+  auto bufWd = [&](int s) { return reinterpret_cast<float*>(smem + s * kBuf + kKB * (kATile + kBTile)); };
+  auto bufXd = [&](int s) { return bufWd(s) + kKB * kGM; };
 
   const int tid = threadIdx.x, warp = tid >> 5;
   const int m0 = blockIdx.x * kGM, n0 = blockIdx.y * kGN;
@@ -144,55 +235,25 @@ q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scal
   pdl_trigger();
   pdl_wait();  // the activation images may come from the previous kernel
 
-  float acc[kGN];
+  unsigned long long acc[kGN / 2];  // token pairs
 #pragma unroll
-  for (int n = 0; n < kGN; ++n) acc[n] = 0.0f;
+  for (int n = 0; n < kGN / 2; ++n) acc[n] = 0ull;  // (+0.0f, +0.0f)
   uint32_t phase[2] = {0u, 0u};
   bool ok = true;
-  constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;
+  const int nchunks = (nb + kKB - 1) / kKB;
 
-  for (int c0 = 0; c0 < nb && ok; c0 += kKB) {
-    const int kb = min(kKB, nb - c0);
-    // ---- stage the chunk: A (this thread's row), B (tokens), scales
-    {
-      const int g = tid >> 3, r = tid & 7;
-      for (int b = 0; b < kb; ++b) {
-        uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
-        float wd = 0.0f;
-        if (row < M) {
-          const uint8_t* src = w + ((size_t)row * nb + c0 + b) * UB;
-          if (FMT == kFmtQ4_0) {
-            q4_to_i8(*reinterpret_cast<const uint4*>(src), lo, hi);
-          } else {
-            lo = *reinterpret_cast<const uint4*>(src);
-            hi = *reinterpret_cast<const uint4*>(src + 16);
-          }
-          wd = __half2float(scales[(size_t)row * nb + c0 + b]);
-        }
-        unsigned char* t = sA + b * kATile + g * 256 + r * 16;
-        *reinterpret_cast<uint4*>(t) = lo;
-        *reinterpret_cast<uint4*>(t + 128) = hi;
-        sWd[b * kGM + tid] = wd;
-      }
-      // B: kb blocks x kGN tokens, two threads per (token, block)
-      for (int i = tid; i < kb * kGN * 2; i += kGThreads) {
-        const int half = i & 1, tb = i >> 1, n = tb % kGN, b = tb / kGN;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        const int tok = n0 + n;
-        if (tok < N) {
-          const unsigned char* im = images + (size_t)tok * img_stride;
-          v = __ldcg(reinterpret_cast<const uint4*>(im + (size_t)(c0 + b) * 48) + half);
-          if (half == 0) sXd[b * kGN + n] = __ldcg(reinterpret_cast<const float2*>(im + (size_t)nb * 48) + c0 + b).x;
-        } else if (half == 0) {
-          sXd[b * kGN + n] = 0.0f;
-        }
-        *reinterpret_cast<uint4*>(sB + b * kBTile + (n >> 3) * 256 + half * 128 + (n & 7) * 16) = v;
-      }
-    }
-    fence_proxy_async();  // the generic-proxy writes above become visible to the tensor core
-    __syncthreads();
+  ChunkRegs R;
+  load_chunk<FMT>(R, w, scales, images, img_stride, row, M, N, nb, n0, 0, min(kKB, nb), tid);
+  store_chunk<FMT>(R, bufA(0), bufB(0), bufWd(0), bufXd(0), tid);
+  fence_proxy_async();  // the generic-proxy writes become visible to the tensor core
+  __syncthreads();
 
-    // ---- blocks of the chunk: MMA b+2 runs while the threads scale b
+  for (int c = 0; c < nchunks && ok; ++c) {
+    const int sb = c & 1, c0 = c * kKB, kb = min(kKB, nb - c0);
+    unsigned char* sA = bufA(sb);
+    unsigned char* sB = bufB(sb);
+    const float* sWd = bufWd(sb);
+    const float* sXd = bufXd(sb);
     auto issue = [&](int b) {
       if (tid == 0) {
         tc_fence_after();
@@ -203,6 +264,9 @@ q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scal
     };
     issue(0);
     if (kb > 1) issue(1);
+    const bool more = c + 1 < nchunks;
+    if (more)  // next chunk's loads in flight during this chunk's blocks
+      load_chunk<FMT>(R, w, scales, images, img_stride, row, M, N, nb, n0, c0 + kKB, min(kKB, nb - c0 - kKB), tid);
     for (int b = 0; b < kb; ++b) {
       const int buf = b & 1;
       const bool done = mbar_wait_bounded(smem_u32(&mbar[buf]), phase[buf]);
@@ -216,20 +280,28 @@ q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scal
       uint32_t d[kGN];
       tmem_ld64(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * kGN), d);
       const float wd = sWd[b * kGM + tid];
+      const unsigned long long* xd2 = reinterpret_cast<const unsigned long long*>(sXd + b * kGN);
 #pragma unroll
-      for (int n = 0; n < kGN; ++n)
-        acc[n] = __fmaf_rn(__int2float_rn((int)d[n]), __fmul_rn(wd, sXd[b * kGN + n]), acc[n]);
+      for (int n = 0; n < kGN / 2; ++n) acc[n] = scale_acc2(acc[n], (int)d[2 * n], (int)d[2 * n + 1], wd, xd2[n]);
       tc_fence_before();
       __syncthreads();  // every thread has read accumulator buf: it may be overwritten
-      if (b + 2 < kb && ok) issue(b + 2);
+      if (b + 2 < kb) issue(b + 2);
     }
-    __syncthreads();  // all MMAs of the chunk are done: the staging area may be refilled
+    if (more && ok) {  // chunk c-1's buffer is free (its MMAs completed): fill it with chunk c+1
+      store_chunk<FMT>(R, bufA(sb ^ 1), bufB(sb ^ 1), bufWd(sb ^ 1), bufXd(sb ^ 1), tid);
+      fence_proxy_async();
+    }
+    __syncthreads();
   }
 
   if (row < M) {
 #pragma unroll
-    for (int n = 0; n < kGN; ++n)
-      if (n0 + n < N) y[(size_t)(n0 + n) * M + row] = acc[n];
+    for (int n = 0; n < kGN / 2; ++n) {
+      float a0, a1;
+      unpack2(acc[n], a0, a1);
+      if (n0 + 2 * n < N) y[(size_t)(n0 + 2 * n) * M + row] = a0;
+      if (n0 + 2 * n + 1 < N) y[(size_t)(n0 + 2 * n + 1) * M + row] = a1;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -241,7 +313,7 @@ q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scal
 }  // namespace
 
 size_t gemm_smem_bytes() {
-  return (size_t)kKB * (kATile + kBTile) + (size_t)kKB * (kGM + kGN) * sizeof(float) + 2 * sizeof(uint64_t) + 16;
+  return 2 * ((size_t)kKB * (kATile + kBTile) + (size_t)kKB * (kGM + kGN) * sizeof(float)) + 2 * sizeof(uint64_t) + 16;
 }
 
 cudaError_t launch_q8act_gemm(int fmt, const void* w, const void* scales_f16, const void* images, size_t img_stride,

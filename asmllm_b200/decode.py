@@ -129,7 +129,7 @@ def shard_plan(shape: LlamaShape, tp: int, rank: int) -> Shard:
         raise ValueError(f"FFN {s.ffn} / {tp} is not a multiple of {FFN_UNIT}")
     if (s.n_heads // tp * s.head_dim) % 256:
         raise ValueError("each rank's n_heads * head_dim must be a multiple of 256")
-    if s.vocab % (tp * LM_UNIT):
+    if tp > 1 and s.vocab % (tp * LM_UNIT):  # one rank: the last unit may be partial
         raise ValueError(f"vocab {s.vocab} is not a multiple of {tp} * {LM_UNIT}")
     def part(n):
         return range(rank * n // tp, (rank + 1) * n // tp)
@@ -187,7 +187,9 @@ def make_weights(shape: LlamaShape, sh: Shard, seed: int, fmt: int, dev) -> dict
         layers.append(L)
     final_norm = vec(-1, _FN, s.dim)
     lm_head = cat_rows([rows(-1, _LM, c, LM_UNIT, s.dim)
-                             for c in range(sh.vocab.start // LM_UNIT, sh.vocab.stop // LM_UNIT)])
+                        for c in range(sh.vocab.start // LM_UNIT, -(-sh.vocab.stop // LM_UNIT))])
+    if lm_head[0].shape[0] != len(sh.vocab):  # partial last unit (one rank only)
+        lm_head = tuple(t[: len(sh.vocab)].contiguous() for t in lm_head)
     gen.manual_seed(_unit_seed(seed, -1, _EMB, 0))
     return {"layers": layers, "final_norm": final_norm, "lm_head": lm_head,
             "embed": torch.randn((s.vocab, s.dim), device=dev, generator=gen)}

@@ -18,6 +18,17 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200, sm_100a)")
 
 
+@pytest.fixture(autouse=True)
+def no_pending_library_error():
+    """A test that provokes a library error must read it (native.last_error());
+    one left pending would be raised by the next test's first check()."""
+    yield
+    native = sys.modules.get("asmllm_b200.native")
+    if native is not None and getattr(native, "_lib", None) is not None:
+        code, msg = native.last_error()
+        assert code == 0, f"test left a pending library error: {code} {msg}"
+
+
 @pytest.fixture(scope="session")
 def golden():
     """The reference's seed-42 fixture (tools/reference_gen.py), saved by tests/golden/make_golden.py."""

@@ -65,4 +65,4 @@ def test_gemm_rejects_bad_arguments(cuda):
     assert rc == native.ASM_E_INVALID and "image_stride" in native.last_error()[1]
     rc = L.asm_gemm_image_async(3, w.data_ptr(), s.data_ptr(), img.data_ptr(), img.stride(0), y.data_ptr(), 128, 4,
                                 256, None)
-    assert rc == native.ASM_E_INVALID
+    assert rc == native.ASM_E_INVALID and "fmt 3" in native.last_error()[1]

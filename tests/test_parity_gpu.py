@@ -419,4 +419,4 @@ def test_q5_rejects_bad_arguments(cuda):
     rc = L.asm_matmul_q5_async(ql.data_ptr(), ql.data_ptr() + 1, x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 32, None)
     assert rc == native.ASM_E_INVALID and "aligned" in native.last_error()[1]
     rc = L.asm_matmul_q5_async(ql.data_ptr(), ql.data_ptr(), x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 33, None)
-    assert rc == native.ASM_E_INVALID
+    assert rc == native.ASM_E_INVALID and "K=33" in native.last_error()[1]

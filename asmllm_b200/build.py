@@ -21,7 +21,8 @@ INCLUDE = ROOT / "include"
 LIB_DIR = ROOT / "build"
 LIB_PATH = LIB_DIR / "libasmllm.so"
 
-SOURCES = ["matvec.cu", "tma_matvec.cu", "decode.cu", "decode_persistent.cu", "q5_matvec.cu", "prefill_gemm.cu", "capi.cu"]
+SOURCES = ["matvec.cu", "tma_matvec.cu", "decode.cu", "decode_persistent.cu", "q5_matvec.cu", "prefill_gemm.cu",
+           "batch_decode.cu", "capi.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

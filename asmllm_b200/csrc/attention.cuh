@@ -18,6 +18,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "tiles.cuh"
 
 namespace asmllm {
 
@@ -96,7 +97,8 @@ __device__ __forceinline__ float attn_block_reduce(float v, float* red, bool is_
 template <int NT, class Sync>
 __device__ void attention_head(const float* qkv, __half* kc, __half* vc, const float2* rope_cs, int pos, int h,
                                int n_heads, int n_kv, float sqrt_hd, unsigned char* image, const AttnSmem& sm,
-                               int tid, Sync sync, int n_rep = 1, size_t rep_stride = 0) {
+                               int tid, Sync sync, int n_rep = 1, size_t rep_stride = 0,
+                               unsigned char* tiles = nullptr, int np = 0, int tile_row = 0) {
   static_assert(NT == 256, "attention is laid out for 256 working threads");
   constexpr int kSlices = NT / 16;  // position slices of P.V (16 groups of 8 dims each)
   const int warp = tid >> 5, lane = tid & 31;
@@ -207,7 +209,7 @@ __device__ void attention_head(const float* qkv, __half* kc, __half* vc, const f
   sync();
 
   // Quantize the head's 128 outputs (4 Q8_0 blocks, 8 lanes per block) into
-  // the image slots of blocks 4h .. 4h+3.
+  // the image slots of blocks 4h .. 4h+3 (or into row tile_row of the tiles).
   if (warp == 0) {
     const int b = lane >> 3, l8 = lane & 7;
     const float4 o = reinterpret_cast<const float4*>(sm.q)[b * 8 + l8];
@@ -216,6 +218,10 @@ __device__ void attention_head(const float* qkv, __half* kc, __half* vc, const f
     const unsigned q = quantize_quad(o, d, qsum);
     const int nb = n_heads * (kAttnHd / QK);
     const int blk = h * (kAttnHd / QK) + b;
+    if (tiles) {
+      tiles_store_quad(tiles, np, nb, tile_row, blk, l8, q, d, true);
+      return;
+    }
     for (int r = 0; r < n_rep; ++r) {  // identical replicas (see the persistent decode kernel)
       unsigned char* im = image + (size_t)r * rep_stride;
       reinterpret_cast<unsigned*>(im + (size_t)blk * 48)[l8] = q;

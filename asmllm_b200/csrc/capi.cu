@@ -28,6 +28,7 @@
 #include "../../include/asmllm.h"
 #include "decode_persistent.cuh"
 #include "matvec.cuh"
+#include "tiles.cuh"
 
 using namespace asmllm;
 
@@ -582,8 +583,160 @@ ASMLLM_API int asm_gemm_image_async(int fmt, const void* qweights, const void* s
     return rc;
   if ((uintptr_t)qweights % 16 || (uintptr_t)images % 16 || (uintptr_t)scales_f16 % 2 || (uintptr_t)y % 4)
     return set_error(ASM_E_INVALID, "%s: qweights and images must be 16-byte aligned", name);
-  const cudaError_t e = launch_q8act_gemm(fmt, qweights, scales_f16, images, (size_t)image_stride, y, M, N, K,
+  const bool st = is_static(qweights, weight_bytes(fmt, M, K)) && is_static(scales_f16, (size_t)M * (K / 32) * 2);
+  const cudaError_t e = launch_q8act_gemm(fmt, qweights, scales_f16, images, (size_t)image_stride, y, M, N, K, st,
                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int64_t asm_act_tiles_bytes(int64_t N, int64_t K) {
+  if (N <= 0 || K <= 0 || K % 32 || N > INT32_MAX) return 0;
+  return (int64_t)act_tiles_bytes(N, K);
+}
+
+ASMLLM_API int asm_act_tiles_from_image_async(const void* images, int64_t image_stride, int64_t N, int64_t K,
+                                              void* tiles, void* stream) {
+  const char* name = "asm_act_tiles_from_image_async";
+  if (N <= 0 || K <= 0 || K % 32 || N > INT32_MAX)
+    return set_error(ASM_E_INVALID, "%s: need N > 0 and K > 0 a multiple of 32", name);
+  if (image_stride < (int64_t)act_image_bytes(K / 32) || image_stride % 16)
+    return set_error(ASM_E_INVALID, "%s: image_stride %lld below the image size or not a multiple of 16", name,
+                     (long long)image_stride);
+  int rc;
+  if ((rc = require_device(name, images, "images")) || (rc = require_device(name, tiles, "tiles"))) return rc;
+  if ((uintptr_t)images % 16 || (uintptr_t)tiles % 16)
+    return set_error(ASM_E_INVALID, "%s: images and tiles must be 16-byte aligned", name);
+  const cudaError_t e =
+      launch_act_tiles_from_image(images, (size_t)image_stride, N, K, tiles, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_gemm_tiles_async(int fmt, const void* qweights, const void* scales_f16, const void* tiles,
+                                    float* y, int64_t M, int64_t N, int64_t K, void* stream) {
+  const char* name = "asm_gemm_tiles_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (M <= 0 || N <= 0 || K <= 0 || K % 32 || M > INT32_MAX || N > INT32_MAX)
+    return set_error(ASM_E_INVALID, "%s: need M, N > 0 and K > 0 a multiple of 32", name);
+  int rc;
+  if ((rc = require_device(name, qweights, "qweights")) || (rc = require_device(name, scales_f16, "scales")) ||
+      (rc = require_device(name, tiles, "tiles")) || (rc = require_device(name, y, "y")))
+    return rc;
+  if ((uintptr_t)qweights % 16 || (uintptr_t)tiles % 16 || (uintptr_t)scales_f16 % 2 || (uintptr_t)y % 4)
+    return set_error(ASM_E_INVALID, "%s: qweights and tiles must be 16-byte aligned", name);
+  const bool st = is_static(qweights, weight_bytes(fmt, M, K)) && is_static(scales_f16, (size_t)M * (K / 32) * 2);
+  const cudaError_t e =
+      launch_q8act_gemm_tiles(fmt, qweights, scales_f16, tiles, y, M, N, K, st, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Batched decode glue (batch_decode.cu)
+// ---------------------------------------------------------------------------
+ASMLLM_API int asm_rows_norm_tiles_async(const asm_rows_t* d, void* stream) {
+  const char* name = "asm_rows_norm_tiles_async";
+  if (!d) return set_error(ASM_E_INVALID, "%s: null descriptor", name);
+  if (d->rows <= 0 || d->dim <= 0 || d->dim % 32)
+    return set_error(ASM_E_INVALID, "%s: need rows > 0 and dim a positive multiple of 32", name);
+  if ((size_t)d->dim * sizeof(float) > 200 * 1024) return set_error(ASM_E_UNSUPPORTED, "%s: dim too large", name);
+  int rc;
+  if ((rc = require_device(name, d->x, "x")) || (rc = require_device(name, d->tiles, "tiles"))) return rc;
+  if (d->delta && (rc = require_device(name, d->delta, "delta"))) return rc;
+  if (d->norm_w && (rc = require_device(name, d->norm_w, "norm_w"))) return rc;
+  if (d->embed) {
+    if ((rc = require_device(name, d->embed, "embed")) || (rc = require_device(name, d->tokens, "tokens")) ||
+        (rc = require_device(name, d->pos, "pos")))
+      return rc;
+    if (d->max_tokens <= 0 || d->vocab <= 0)
+      return set_error(ASM_E_INVALID, "%s: embed needs max_tokens and vocab", name);
+  }
+  if ((uintptr_t)d->x % 16 || (uintptr_t)d->tiles % 16 || (uintptr_t)d->delta % 16 || (uintptr_t)d->norm_w % 16 ||
+      (uintptr_t)d->embed % 16)
+    return set_error(ASM_E_INVALID, "%s: misaligned buffer", name);
+  RowsArgs a;
+  a.rows = d->rows;
+  a.dim = d->dim;
+  a.x = d->x;
+  a.delta = d->delta;
+  a.embed = d->embed;
+  a.tokens = d->tokens;
+  a.pos = d->pos;
+  a.max_tokens = d->max_tokens;
+  a.vocab = d->vocab;
+  a.norm_w = d->norm_w;
+  a.eps = d->eps;
+  a.tiles = d->tiles;
+  a.np = act_tiles_tokens(d->rows);
+  const cudaError_t e = launch_rows_norm_tiles(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_rows_swiglu_tiles_async(const float* gu, int32_t rows, int32_t ffn, void* tiles, void* stream) {
+  const char* name = "asm_rows_swiglu_tiles_async";
+  if (rows <= 0 || ffn <= 0 || ffn % 32) return set_error(ASM_E_INVALID, "%s: need ffn a positive multiple of 32", name);
+  if ((size_t)ffn * sizeof(float) > 200 * 1024) return set_error(ASM_E_UNSUPPORTED, "%s: ffn too large", name);
+  int rc;
+  if ((rc = require_device(name, gu, "gu")) || (rc = require_device(name, tiles, "tiles"))) return rc;
+  if ((uintptr_t)gu % 16 || (uintptr_t)tiles % 16) return set_error(ASM_E_INVALID, "%s: misaligned buffer", name);
+  const cudaError_t e = launch_rows_swiglu_tiles(gu, rows, ffn, tiles, act_tiles_tokens(rows),
+                                                 static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_attention_batch_async(const float* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
+                                         int64_t cache_stride, const float* rope_cs, const int32_t* pos, void* tiles,
+                                         int32_t rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                         int32_t ctx, float sqrt_head_dim, void* stream) {
+  const char* name = "asm_attention_batch_async";
+  if (head_dim != 128) return set_error(ASM_E_UNSUPPORTED, "%s: head_dim %d (only 128)", name, head_dim);
+  if (rows <= 0 || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || ctx <= 0)
+    return set_error(ASM_E_INVALID, "%s: need rows > 0, n_heads a multiple of n_kv_heads and ctx > 0", name);
+  if (qkv_stride < (int64_t)(n_heads + 2 * n_kv_heads) * head_dim || qkv_stride % 4 ||
+      cache_stride < (int64_t)ctx * n_kv_heads * head_dim || cache_stride % 8)
+    return set_error(ASM_E_INVALID, "%s: qkv_stride or cache_stride too small or misaligned", name);
+  int rc;
+  if ((rc = require_device(name, qkv, "qkv")) || (rc = require_device(name, k_cache, "k_cache")) ||
+      (rc = require_device(name, v_cache, "v_cache")) || (rc = require_device(name, rope_cs, "rope_cs")) ||
+      (rc = require_device(name, pos, "pos")) || (rc = require_device(name, tiles, "tiles")))
+    return rc;
+  if ((uintptr_t)qkv % 16 || (uintptr_t)k_cache % 16 || (uintptr_t)v_cache % 16 || (uintptr_t)rope_cs % 8 ||
+      (uintptr_t)tiles % 16)
+    return set_error(ASM_E_INVALID, "%s: misaligned buffer", name);
+  const cudaError_t e = launch_attention_batch(qkv, (size_t)qkv_stride, k_cache, v_cache, (size_t)cache_stride,
+                                               rope_cs, pos, tiles, act_tiles_tokens(rows), rows, n_heads, n_kv_heads,
+                                               head_dim, ctx, sqrt_head_dim, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported) return set_error(ASM_E_UNSUPPORTED, "%s: ctx %d too long for shared memory", name, ctx);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_rows_argmax_async(const float* logits, int32_t rows, int32_t n, int64_t stride, int32_t offset,
+                                     int64_t* keys, void* stream) {
+  const char* name = "asm_rows_argmax_async";
+  if (rows <= 0 || n <= 0 || stride < n || offset < 0)
+    return set_error(ASM_E_INVALID, "%s: need rows, n > 0, stride >= n, offset >= 0", name);
+  int rc;
+  if ((rc = require_device(name, logits, "logits")) || (rc = require_device(name, keys, "keys"))) return rc;
+  const cudaError_t e = launch_rows_argmax(logits, rows, n, (size_t)stride, offset, reinterpret_cast<long long*>(keys),
+                                           static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_rows_advance_async(const int64_t* keys, int32_t rows, int32_t* tokens, int32_t max_tokens,
+                                      int32_t* pos, int32_t n_prompt, void* stream) {
+  const char* name = "asm_rows_advance_async";
+  if (rows <= 0 || max_tokens <= 0) return set_error(ASM_E_INVALID, "%s: need rows, max_tokens > 0", name);
+  int rc;
+  if ((rc = require_device(name, keys, "keys")) || (rc = require_device(name, tokens, "tokens")) ||
+      (rc = require_device(name, pos, "pos")))
+    return rc;
+  const cudaError_t e = launch_rows_advance(reinterpret_cast<const long long*>(keys), rows, tokens, max_tokens, pos,
+                                            n_prompt, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
 }
@@ -1042,6 +1195,8 @@ ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* 
 }
 
 // ctypes mirrors of the descriptor (asmllm_b200/native.py FusedMatvec) rely on this layout.
+static_assert(sizeof(asm_rows_t) == 80 && offsetof(asm_rows_t, norm_w) == 56 && offsetof(asm_rows_t, tiles) == 72,
+              "asm_rows_t layout (asmllm_b200/native.py mirrors it)");
 static_assert(sizeof(asm_fused_matvec_t) == 256 && offsetof(asm_fused_matvec_t, eps) == 128 &&
                   offsetof(asm_fused_matvec_t, M) == 144 && offsetof(asm_fused_matvec_t, xchg) == 176,
               "asm_fused_matvec_t layout");
@@ -1441,6 +1596,7 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (!name) return -1;
   if (strcmp(name, "tma") == 0) return g_opt_tma.exchange(value ? 1 : 0);
   if (strcmp(name, "pdl") == 0) return g_opt_pdl.exchange(value ? 1 : 0);
+  if (strcmp(name, "gemm_splits") == 0) return g_opt_gemm_splits.exchange(value < 0 ? 0 : value);
   set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
   return -1;
 }

@@ -138,12 +138,44 @@ cudaError_t launch_q5_matvec(const uint8_t* ql, const uint8_t* qh, const float* 
                              int64_t M, int64_t K, cudaStream_t stream);
 
 // Batched Q4_0 / Q8_0 x Q8_0 product on the tensor cores (prefill_gemm.cu):
-// y [N][M] from N activation-image rows (row stride img_stride bytes), fp16 scales.
-size_t gemm_smem_bytes();
+// y [N][M] from the N-token activation tiles (tiles.cuh), fp16 scales;
+// weights_static: the weights do not depend on the previous kernel.
+cudaError_t launch_q8act_gemm_tiles(int fmt, const void* w, const void* scales_f16, const void* tiles, float* y,
+                                    int64_t M, int64_t N, int64_t K, bool weights_static, cudaStream_t stream);
+// N activation-image rows (row stride img_stride bytes) -> activation tiles.
+cudaError_t launch_act_tiles_from_image(const void* images, size_t img_stride, int64_t N, int64_t K, void* tiles,
+                                        cudaStream_t stream);
+// The two above with stream-ordered scratch tiles.
 cudaError_t launch_q8act_gemm(int fmt, const void* w, const void* scales_f16, const void* images, size_t img_stride,
-                              float* y, int64_t M, int64_t N, int64_t K, cudaStream_t stream);
+                              float* y, int64_t M, int64_t N, int64_t K, bool weights_static, cudaStream_t stream);
+
+// Batched decode glue (batch_decode.cu): one CTA per row (token) of B rows.
+struct RowsArgs {
+  int rows = 0, dim = 0;
+  float* x = nullptr;              // [rows][dim] residual stream
+  const float* delta = nullptr;    // [rows][dim]: x += delta first (or null)
+  const float* embed = nullptr;    // [vocab][dim]: x = embed[tokens[row][pos]] first (or null)
+  const int32_t* tokens = nullptr; // [rows][max_tokens]
+  const int32_t* pos = nullptr;
+  int max_tokens = 0, vocab = 0;
+  const float* norm_w = nullptr;   // [dim]: RMSNorm (or null: quantize x as it is)
+  float eps = 1e-5f;
+  void* tiles = nullptr;           // activation tiles of the rows (tiles.cuh), np tokens
+  int np = 0;
+};
+cudaError_t launch_rows_norm_tiles(const RowsArgs& a, cudaStream_t stream);
+cudaError_t launch_rows_swiglu_tiles(const float* gu, int rows, int ffn, void* tiles, int np, cudaStream_t stream);
+cudaError_t launch_attention_batch(const float* qkv, size_t qkv_stride, void* k_cache, void* v_cache,
+                                   size_t cache_stride, const float* rope_cs, const int32_t* pos, void* tiles, int np,
+                                   int rows, int n_heads, int n_kv, int head_dim, int ctx, float sqrt_hd,
+                                   cudaStream_t stream);
+cudaError_t launch_rows_argmax(const float* logits, int rows, int n, size_t stride, int offset, long long* keys,
+                               cudaStream_t stream);
+cudaError_t launch_rows_advance(const long long* keys, int rows, int32_t* tokens, int max_tokens, int32_t* pos,
+                                int n_prompt, cudaStream_t stream);
 
 extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
 extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch
+extern std::atomic<int> g_opt_gemm_splits;  // batched product: 0 = automatic K split, else exactly this many
 
 }  // namespace asmllm

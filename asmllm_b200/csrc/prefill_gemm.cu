@@ -2,74 +2,124 @@
 // matrix product on the 5th-generation tensor cores (tcgen05, sm_100a).
 //
 // Y[n][m] = sum_b (wd[m][b] * xd[n][b]) * isum_b[m][n],
-// isum_b[m][n] = sum_{i<32} w[m][32b+i] * xq[n][32b+i]   (int32, exact)
+// isum_b[m][n] = sum_{i<32} w[m][32b+i] * xq[n][32b+i]   (an exact integer)
 // for N activation rows already quantized to Q8_0 (the activation image of
 // asm_act_image_q8_0_async, one row per token).  Per row and token this is
-// exactly the reference's NEON combine (THRISHAL12345/asmllm
+// the reference's NEON combine (THRISHAL12345/asmllm
 // src/kernels/arm64/matmul_q4_neon.S:239-255): s = wd * xd (fp32 multiply),
-// acc = fma(float(isum), s, acc), blocks in order -- so every output equals
-// the single-token Q4_0 x Q8_0 result of the reference semantics bit for bit.
+// acc = fma(float(isum), s, acc), blocks in order.  Without a split of K the
+// output equals the single-token Q4_0 x Q8_0 result bit for bit; with a split
+// (small N, see below) the split partials are added in a fixed order.
 //
-// The per-32-block scales differ for every (row, token, block), so they
-// cannot live inside the MMA: each block is one tcgen05.mma (kind::i8, M=128
-// rows, N=64 tokens, K=32) into a fresh int32 accumulator in tensor memory,
-// and the 128 epilogue threads (one per row) read it back (tcgen05.ld) and
-// apply the scales in fp32.  Two accumulators alternate so the tensor core
-// works on block b+2 while the threads scale block b.  Q4_0 weights are
-// expanded to int8 (nibble - 8) in shared memory (the "in-SMEM dequantised
-// tiles"); activations are copied as they are.
+// Exact integer sums on the fp16 tensor path.  The per-32-block scales differ
+// for every (row, token, block), so each block is its own MMA into a fresh
+// accumulator and the scales are applied afterwards by CUDA-core threads.
+// The operands are the small integers themselves, held exactly in fp16
+// (nibble - 8 in [-8, 7], int8 in [-128, 127]); every product is exact, and
+// every partial sum of a block is an integer below 2^24 in magnitude, so the
+// fp32 accumulator of kind::f16 holds the exact isum -- already a float, so
+// the epilogue needs no int -> float conversion (one packed multiply and one
+// packed fma per two outputs).  Within a block the 32 positions may be
+// visited in any order as long as A and B agree; both use the order
+//   k = 8c + j  ->  element 4c + {0, 2, 1, 3, 16, 18, 17, 19}[j],
+// which is what the nibble layout (byte i = elements i and i + 16) expands to
+// with one mask-or per two weights.
 //
-// Pipelining: chunks of kKB blocks are staged into two shared-memory buffers;
-// while the tensor core and the epilogue work on chunk c, every thread holds
-// its global loads for chunk c+1 in registers and stores them (expanding the
-// nibbles) into the other buffer afterwards.  The epilogue uses the packed
-// fp32x2 multiply and fma (two IEEE fp32 operations per instruction, the
-// same rounding as the scalar ones).
+// CTA: 128 rows x BN tokens (BN in 16, 32, 64, 128), a contiguous range of
+// K blocks.  Warp roles (14 warps):
+//   0      producer: one TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) per
+//          stage of 128 rows x 128 bytes of raw weights (8 Q4_0 or 4 Q8_0
+//          blocks) into a 4-stage ring.
+//   1      MMA issuer: two tcgen05.mma kind::f16 (K = 16 each) per block into
+//          one of kAcc tensor-memory accumulators; tcgen05.commit releases the
+//          operand slot and publishes the accumulator.
+//   2..5   expanders, one row and one token each: raw weights -> fp16 A tile,
+//          the token's Q8_0 block (read from the image in L2) -> fp16 B tile,
+//          plus the block's wd and xd, into one of 4 operand slots.
+//   6..13  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its rows)
+//          and half of the BN columns, then acc += d * (wd * xd).
+// Split K (when the tiles alone do not cover the SMs): the splits of one tile
+// form a thread-block cluster along z; each CTA leaves its partial tile in its
+// own shared memory and, after a cluster barrier, each CTA adds a slice of
+// the tile over all splits in rank order (distributed shared memory) and
+// writes y.  No workspace, no atomics, deterministic.
 //
-// Shared-memory operand layout (no swizzle, K-major "core matrices" of 8
-// rows x 16 bytes): element (row, k) of block b at
-//   b * tile + (row / 8) * 256 + (k / 16) * 128 + (row % 8) * 16 + k % 16
-// so the descriptor's leading byte offset (between the two 16-byte K halves)
-// is 128 and its stride byte offset (between 8-row groups) is 256.
+// Shared-memory operand layout (no swizzle, K-major core matrices of 8 rows
+// x 16 bytes): element (row, k) of a block tile at
+//   (row / 8) * 512 + (k / 8) * 128 + (row % 8) * 16 + (k % 8) * 2
+// so for the MMA over k in [16h, 16h + 16) the descriptor starts at h * 256,
+// its leading byte offset (K direction) is 128 and its stride byte offset
+// (8-row groups) is 512.
 //
-// Waits are bounded (the mbarrier of each MMA commit); on timeout the kernel
-// sets bit 0 of the device error word and stops issuing, then releases its
-// tensor memory.
+// Every mbarrier wait is bounded; a role that gives up sets bit 0 of the
+// device error word and stops, the roles waiting on it give up in turn, the
+// producer and the MMA issuer wait (bounded) for what they issued, and the
+// CTA releases its tensor memory.  No cluster multicast anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "common.cuh"
 #include "matvec.cuh"
 #include "pipeline.cuh"
+#include "tiles.cuh"
 
 namespace asmllm {
 
+std::atomic<int> g_opt_gemm_splits{0};
+
 namespace {
 
-constexpr int kGM = 128;       // rows per CTA (MMA M)
-constexpr int kGN = 64;        // tokens per CTA (MMA N)
-constexpr int kKB = 8;         // 32-blocks per staged chunk
-constexpr int kGThreads = 128;  // 4 warps: one row each thread
-constexpr int kTmemCols = 2 * kGN;  // two int32 accumulators of kGN columns
-constexpr int kATile = kGM * 32;    // bytes of one block of A (int8)
-constexpr int kBTile = kGN * 32;    // bytes of one block of B
+constexpr int kGM = 128;                         // rows per CTA (MMA M)
+constexpr int kStages = 6;                       // raw weight ring
+constexpr int kSlots = 6;                        // operand slots (one block each)
+constexpr int kRawBytes = kGM * 128;             // one raw stage: 128 rows x 128 bytes
+constexpr int kScaleBytes = kGM * 16;            // the stage's fp16 scales: 128 rows x 8 blocks
+constexpr int kStageBytes = kRawBytes + kScaleBytes;  // a multiple of 1024 (the swizzle period)
+constexpr int kATile = kGM * 64;                 // one block of A: 128 rows x 32 fp16
+constexpr int kThreads = 448;                    // 14 warps
+constexpr int kEpiWarps = 8;
+constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
+constexpr uint32_t kSub8 = 0x64086408u;   // 1032.0: (1024 + nibble) - 1032 = nibble - 8
+static_assert(kStageBytes % 1024 == 0, "raw stages keep the 1024-byte swizzle alignment");
+
+template <int BN>
+struct Cfg {
+  static constexpr int kBTile = BN * 64;
+  static constexpr int kSlot = kATile + kBTile + BN * 4 + kGM * 4;  // A | B | xd[BN] | wd[128]
+  static constexpr int kAcc = BN >= 128 ? 2 : 4;
+  static constexpr int kCols = BN / 2;  // accumulator columns per epilogue thread
+  static constexpr int kTmemCols = kAcc * BN < 32 ? 32 : kAcc * BN;
+  static constexpr int kBarOff = kStages * kStageBytes + kSlots * kSlot;
+  static constexpr int kSmem = kBarOff + 512 + 1024;  // barriers; room to align the ring to 1024 bytes
+  static_assert(kGM * BN * 4 <= kStages * kStageBytes, "split-K partial tile must fit the raw ring");
+  static_assert((kTmemCols & (kTmemCols - 1)) == 0, "tensor memory allocation is a power of two");
+  static_assert((2 * kStages + 2 * kSlots + 8) * 8 + 8 <= 512, "barrier area");
+};
+
+// kind::f16: D f32 (bit 4), A and B f16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
+template <int BN>
+struct IdescF16 {
+  static constexpr uint32_t value = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(kGM >> 4) << 24);
+};
 
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
-  // start address >> 4 | LBO 128 B >> 4 | SBO 256 B >> 4 | version 1 (sm_100) | no swizzle
-  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+  // start >> 4 | LBO 128 B >> 4 | SBO 512 B >> 4 | version 1 (sm_100) | no swizzle
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) |
          ((uint64_t)1 << 46);
 }
 
-// kind::i8: D s32 (c_format 2), A and B signed 8-bit, both K-major, N, M.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kGN >> 3) << 17) |
-                            ((uint32_t)(kGM >> 4) << 24);
-
-__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc) {
+template <int BN>
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(IdescF16<BN>::value), "r"(accumulate)
       : "memory");
 }
 
@@ -82,39 +132,60 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// 64 consecutive int32 columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,"
-      "%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
-      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
-        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
-        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(mbar)
       : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Expands 16 bytes of Q4_0 nibbles into the block's 32 int8 weights (nibble - 8):
-// lo = elements 0..15 (low nibbles), hi = elements 16..31 (high nibbles).
-__device__ __forceinline__ void q4_to_i8(uint4 q, uint4& lo, uint4& hi) {
-  auto ex = [](unsigned w, unsigned& l, unsigned& h) {  // per-byte n - 8, wrapping: the int8 value
-    l = __vsub4(w & 0x0F0F0F0Fu, 0x08080808u);
-    h = __vsub4((w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
-  };
-  ex(q.x, lo.x, hi.x);
-  ex(q.y, lo.y, hi.y);
-  ex(q.z, lo.z, hi.z);
-  ex(q.w, lo.w, hi.w);
+// N consecutive 32-bit columns of this thread's tensor-memory lane.
+template <int N>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]);
+
+#define ASM_TMEM_LD_8(i) "=r"(r[i]), "=r"(r[i + 1]), "=r"(r[i + 2]), "=r"(r[i + 3]), \
+                         "=r"(r[i + 4]), "=r"(r[i + 5]), "=r"(r[i + 6]), "=r"(r[i + 7])
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : ASM_TMEM_LD_8(0)
+               : "r"(taddr)
+               : "memory");
 }
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : ASM_TMEM_LD_8(0), ASM_TMEM_LD_8(8)
+      : "r"(taddr)
+      : "memory");
+}
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : ASM_TMEM_LD_8(0), ASM_TMEM_LD_8(8), ASM_TMEM_LD_8(16), ASM_TMEM_LD_8(24)
+      : "r"(taddr)
+      : "memory");
+}
+#undef ASM_TMEM_LD_8
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Chunk c (k = 8c .. 8c+7) of a Q4_0 block from word c of its 16 bytes
+// (bytes 4c..4c+3: low nibbles = elements 4c..4c+3, high = 4c+16..4c+19).
+__device__ __forceinline__ uint4 q4_chunk(uint32_t w) {
+  uint4 r;
+  r.x = tiles_hsub2((w & 0x000F000Fu) | kMagic, kSub8);          // elements 4c, 4c+2
+  r.y = tiles_hsub2(((w >> 8) & 0x000F000Fu) | kMagic, kSub8);   // 4c+1, 4c+3
+  r.z = tiles_hsub2(((w >> 4) & 0x000F000Fu) | kMagic, kSub8);   // 4c+16, 4c+18
+  r.w = tiles_hsub2(((w >> 12) & 0x000F000Fu) | kMagic, kSub8);  // 4c+17, 4c+19
+  return r;
+}
+
+__device__ __forceinline__ uint4 lds128(const unsigned char* p) { return *reinterpret_cast<const uint4*>(p); }
 
 __device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
   unsigned long long r;
@@ -126,106 +197,95 @@ __device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& 
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
 }
 
-// acc += float(d) * (wd * xd) for two tokens at once, each element rounded as
-// the scalar fmul / fma.
-__device__ __forceinline__ unsigned long long scale_acc2(unsigned long long acc, int d0, int d1, float wd,
-                                                         unsigned long long xd2) {
-  unsigned long long s, dv, r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(s) : "l"(pack2(wd, wd)), "l"(xd2));
-  dv = pack2(__int2float_rn(d0), __int2float_rn(d1));
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(dv), "l"(s), "l"(acc));
+// acc += d * (wd * xd) for two tokens, each element rounded as the scalar fmul / fma.
+__device__ __forceinline__ unsigned long long scale_acc2(unsigned long long acc, uint32_t d0, uint32_t d1,
+                                                         unsigned long long wd2, unsigned long long xd2) {
+  unsigned long long s, r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(s) : "l"(wd2), "l"(xd2));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(pack2(__uint_as_float(d0), __uint_as_float(d1))), "l"(s), "l"(acc));
   return r;
 }
 
-// Staging registers of one chunk for one thread: its row's kKB weight blocks
-// (and scales) and its share of the activation blocks.
-struct ChunkRegs {
-  uint4 a[kKB][2];
-  float wd[kKB];
-  uint4 bv[kKB * kGN * 2 / kGThreads];
-  float bxd[kKB * kGN * 2 / kGThreads];
-};
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
 
-template <int FMT>
-__device__ __forceinline__ void load_chunk(ChunkRegs& R, const uint8_t* __restrict__ w,
-                                           const __half* __restrict__ scales, const unsigned char* __restrict__ images,
-                                           size_t img_stride, int row, int M, int N, int nb, int n0, int c0, int kb,
-                                           int tid) {
-  constexpr int UB = FMT == kFmtQ4_0 ? 16 : 32;
+__device__ __forceinline__ float ld_cluster_f32(uint32_t local_saddr, uint32_t rank) {
+  uint32_t remote;
+  float v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_saddr), "r"(rank));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// Epilogue of one block for one thread: CH columns from tensor memory.
+template <int BN, int CH>
+__device__ __forceinline__ void epi_chunk(uint32_t taddr, unsigned long long* acc2, unsigned long long wd2,
+                                          const float* xd) {
+  uint32_t d[CH];
+  tmem_ld<CH>(taddr, d);
+  tmem_wait_ld();
 #pragma unroll
-  for (int b = 0; b < kKB; ++b) {
-    R.a[b][0] = R.a[b][1] = make_uint4(0u, 0u, 0u, 0u);
-    R.wd[b] = 0.0f;
-    if (b < kb && row < M) {
-      const uint8_t* src = w + ((size_t)row * nb + c0 + b) * UB;
-      R.a[b][0] = *reinterpret_cast<const uint4*>(src);
-      if (FMT != kFmtQ4_0) R.a[b][1] = *reinterpret_cast<const uint4*>(src + 16);
-      R.wd[b] = __half2float(scales[(size_t)row * nb + c0 + b]);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < kKB * kGN * 2 / kGThreads; ++j) {
-    const int i = tid + j * kGThreads;
-    const int half = i & 1, tb = i >> 1, n = tb % kGN, b = tb / kGN;
-    R.bv[j] = make_uint4(0u, 0u, 0u, 0u);
-    R.bxd[j] = 0.0f;
-    if (b < kb && n0 + n < N) {
-      const unsigned char* im = images + (size_t)(n0 + n) * img_stride;
-      R.bv[j] = __ldcg(reinterpret_cast<const uint4*>(im + (size_t)(c0 + b) * 48) + half);
-      if (half == 0) R.bxd[j] = __ldcg(reinterpret_cast<const float2*>(im + (size_t)nb * 48) + c0 + b).x;
-    }
+  for (int i = 0; i < CH / 4; ++i) {
+    const float4 x4 = *reinterpret_cast<const float4*>(xd + 4 * i);
+    acc2[2 * i] = scale_acc2(acc2[2 * i], d[4 * i], d[4 * i + 1], wd2, pack2(x4.x, x4.y));
+    acc2[2 * i + 1] = scale_acc2(acc2[2 * i + 1], d[4 * i + 2], d[4 * i + 3], wd2, pack2(x4.z, x4.w));
   }
 }
 
-template <int FMT>
-__device__ __forceinline__ void store_chunk(const ChunkRegs& R, unsigned char* sA, unsigned char* sB, float* sWd,
-                                            float* sXd, int tid) {
-  const int g = tid >> 3, r = tid & 7;
-#pragma unroll
-  for (int b = 0; b < kKB; ++b) {
-    uint4 lo = R.a[b][0], hi = R.a[b][1];
-    if (FMT == kFmtQ4_0) q4_to_i8(R.a[b][0], lo, hi);
-    unsigned char* t = sA + b * kATile + g * 256 + r * 16;
-    *reinterpret_cast<uint4*>(t) = lo;
-    *reinterpret_cast<uint4*>(t + 128) = hi;
-    sWd[b * kGM + tid] = R.wd[b];
-  }
-#pragma unroll
-  for (int j = 0; j < kKB * kGN * 2 / kGThreads; ++j) {
-    const int i = tid + j * kGThreads;
-    const int half = i & 1, tb = i >> 1, n = tb % kGN, b = tb / kGN;
-    *reinterpret_cast<uint4*>(sB + b * kBTile + (n >> 3) * 256 + half * 128 + (n & 7) * 16) = R.bv[j];
-    if (half == 0) sXd[b * kGN + n] = R.bxd[j];
-  }
-}
+template <int FMT, int BN, bool STMA>
+__global__ void __launch_bounds__(kThreads, 1)
+q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                  const __half* __restrict__ scales, const unsigned char* __restrict__ tiles, int np,
+                  float* __restrict__ y, int M, int N, int nb, int splits, int pre, unsigned* __restrict__ err) {
+  using C = Cfg<BN>;
+  constexpr int KB = FMT == kFmtQ4_0 ? 8 : 4;  // blocks per raw stage
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // the 128-byte swizzle of the raw ring repeats every 1024 bytes of shared address
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* raw = smem;
+  unsigned char* slots = smem + kStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* raw_full = bars;
+  uint64_t* raw_empty = bars + kStages;
+  uint64_t* slot_full = bars + 2 * kStages;
+  uint64_t* slot_empty = bars + 2 * kStages + kSlots;
+  uint64_t* acc_full = bars + 2 * kStages + 2 * kSlots;
+  uint64_t* acc_empty = acc_full + 4;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acc_empty + 4);
+  volatile uint32_t* s_abort = s_tmem + 1;
 
-template <int FMT>
-__global__ void __launch_bounds__(kGThreads, 1)
-q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scales,
-                  const unsigned char* __restrict__ images, size_t img_stride, float* __restrict__ y, int M,
-                  int N, int nb, unsigned* __restrict__ err) {
-  extern __shared__ __align__(1024) unsigned char smem[];
-  constexpr size_t kBuf = (size_t)kKB * (kATile + kBTile) + (size_t)kKB * (kGM + kGN) * sizeof(float);
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + 2 * kBuf);  // [2]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(mbar + 2);
-  auto bufA = [&](int s) { return smem + s * kBuf; };
-  auto bufB = [&](int s) { return smem + s * kBuf + kKB * kATile; };
-  auto bufWd = [&](int s) { return reinterpret_cast<float*>(smem + s * kBuf + kKB * (kATile + kBTile)); };
-  auto bufXd = [&](int s) { return bufWd(s) + kKB * kGM; };
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.x * kGM, n0 = blockIdx.y * BN;
+  const int z = blockIdx.z;
+  const int nst = (nb + KB - 1) / KB;
+  const int st0 = (int)((long long)z * nst / splits), st1 = (int)((long long)(z + 1) * nst / splits);
+  const int b0 = st0 * KB;
+  const int jb = min(st1 * KB, nb) - b0;  // blocks of this CTA
+  const int ns = st1 - st0;
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int m0 = blockIdx.x * kGM, n0 = blockIdx.y * kGN;
-  const int row = m0 + tid;
-
-  if (warp == 0) {
+  if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
-                 "r"((uint32_t)kTmemCols)
+                 "r"((uint32_t)C::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    mbar_init(smem_u32(&mbar[0]), 1);
-    mbar_init(smem_u32(&mbar[1]), 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&raw_full[i]), 1);
+      mbar_init(smem_u32(&raw_empty[i]), 4);
+    }
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(smem_u32(&slot_full[i]), 4 + 1);           // expander warps + the producer's tile copy
+      mbar_init(smem_u32(&slot_empty[i]), 1 + kEpiWarps);  // MMA commit + epilogue warps
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(smem_u32(&acc_full[i]), 1);
+      mbar_init(smem_u32(&acc_empty[i]), kEpiWarps);
+    }
+    *s_abort = 0u;
     fence_mbar_init();
   }
   tc_fence_before();
@@ -233,113 +293,393 @@ q8act_gemm_kernel(const uint8_t* __restrict__ w, const __half* __restrict__ scal
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   pdl_trigger();
-  pdl_wait();  // the activation images may come from the previous kernel
 
-  unsigned long long acc[kGN / 2];  // token pairs
-#pragma unroll
-  for (int n = 0; n < kGN / 2; ++n) acc[n] = 0ull;  // (+0.0f, +0.0f)
-  uint32_t phase[2] = {0u, 0u};
-  bool ok = true;
-  const int nchunks = (nb + kKB - 1) / kKB;
+  auto fail = [&]() {
+    *s_abort = 1u;
+    atomicOr(err, kErrRingTimeout);
+  };
 
-  ChunkRegs R;
-  load_chunk<FMT>(R, w, scales, images, img_stride, row, M, N, nb, n0, 0, min(kKB, nb), tid);
-  store_chunk<FMT>(R, bufA(0), bufB(0), bufWd(0), bufXd(0), tid);
-  fence_proxy_async();  // the generic-proxy writes become visible to the tensor core
-  __syncthreads();
-
-  for (int c = 0; c < nchunks && ok; ++c) {
-    const int sb = c & 1, c0 = c * kKB, kb = min(kKB, nb - c0);
-    unsigned char* sA = bufA(sb);
-    unsigned char* sB = bufB(sb);
-    const float* sWd = bufWd(sb);
-    const float* sXd = bufXd(sb);
-    auto issue = [&](int b) {
-      if (tid == 0) {
-        tc_fence_after();
-        umma_i8(tmem + (uint32_t)((b & 1) * kGN), umma_desc(smem_u32(sA + b * kATile)),
-                umma_desc(smem_u32(sB + b * kBTile)));
-        umma_commit(smem_u32(&mbar[b & 1]));
+  if (warp == 0) {
+    // ---------------- producer: raw weight stages (TMA) and activation tiles (bulk) ----------------
+    if (lane == 0) {
+      int s_issued = 0, j_issued = 0;
+      auto issue_stage = [&](int s) -> bool {
+        const int rs = s % kStages;
+        if (s >= kStages && !mbar_wait_bounded(smem_u32(&raw_empty[rs]), ((s / kStages) - 1) & 1)) return false;
+        const uint32_t full = smem_u32(&raw_full[rs]);
+        mbar_arrive_expect_tx(full, kRawBytes + (STMA ? kScaleBytes : 0));
+        tma_load_2d(smem_u32(raw + rs * kStageBytes), &wmap, (st0 + s) * 128, m0, full);
+        if (STMA) tma_load_2d(smem_u32(raw + rs * kStageBytes + kRawBytes), &smap, ((st0 + s) * KB) & ~7, m0, full);
+        return true;
+      };
+      // weights declared static do not depend on the previous kernel: their first stages go out now
+      if (pre)
+        for (; s_issued < ns && s_issued < kStages; ++s_issued) issue_stage(s_issued);  // no wait below kStages
+      pdl_wait();  // the activation tiles come from the previous kernel
+      bool ok = true;
+      for (int j = 0; j < jb && ok; ++j) {
+        while (ok && s_issued < ns && s_issued <= j / KB + kStages - 1) {
+          ok = issue_stage(s_issued);
+          if (ok) ++s_issued;
+        }
+        const int sl = j % kSlots;
+        if (ok && j >= kSlots) ok = mbar_wait_bounded(smem_u32(&slot_empty[sl]), ((j / kSlots) - 1) & 1);
+        if (!ok || *s_abort) break;
+        unsigned char* slot = slots + sl * C::kSlot;
+        const uint32_t full = smem_u32(&slot_full[sl]);
+        const size_t tb = (size_t)(b0 + j) * np + n0;  // this block's first token
+        mbar_arrive_expect_tx(full, BN * 68);
+        bulk_g2s(smem_u32(slot + kATile), tiles + tb * 64, BN * 64, full);
+        bulk_g2s(smem_u32(slot + kATile + C::kBTile), tiles + (size_t)nb * np * 64 + tb * 4, BN * 4, full);
+        j_issued = j + 1;
       }
-    };
-    issue(0);
-    if (kb > 1) issue(1);
-    const bool more = c + 1 < nchunks;
-    if (more)  // next chunk's loads in flight during this chunk's blocks
-      load_chunk<FMT>(R, w, scales, images, img_stride, row, M, N, nb, n0, c0 + kKB, min(kKB, nb - c0 - kKB), tid);
-    for (int b = 0; b < kb; ++b) {
-      const int buf = b & 1;
-      const bool done = mbar_wait_bounded(smem_u32(&mbar[buf]), phase[buf]);
-      phase[buf] ^= 1u;
-      if (__syncthreads_or(!done)) {  // one decision for the CTA
-        if (tid == 0) atomicOr(err, kErrRingTimeout);
-        ok = false;
+      if (!ok) fail();
+      // every issued copy lands before the CTA moves on (bounded)
+      for (int s = s_issued - kStages < 0 ? 0 : s_issued - kStages; s < s_issued; ++s)
+        if (!mbar_wait_bounded(smem_u32(&raw_full[s % kStages]), (s / kStages) & 1)) fail();
+      for (int j = j_issued - kSlots < 0 ? 0 : j_issued - kSlots; j < j_issued; ++j)
+        if (!mbar_wait_bounded(smem_u32(&slot_full[j % kSlots]), (j / kSlots) & 1)) fail();
+    } else {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < jb; ++j) {
+        const int sl = j % kSlots, a = j % C::kAcc;
+        if (!mbar_wait_bounded(smem_u32(&slot_full[sl]), (j / kSlots) & 1)) {
+          fail();
+          break;
+        }
+        if (j >= C::kAcc && !mbar_wait_bounded(smem_u32(&acc_empty[a]), ((j / C::kAcc) - 1) & 1)) {
+          fail();
+          break;
+        }
+        if (*s_abort) break;
+        tc_fence_after();
+        unsigned char* slot = slots + sl * C::kSlot;
+        const uint64_t ad = umma_desc(smem_u32(slot)), bd = umma_desc(smem_u32(slot + kATile));
+        const uint32_t td = tmem + (uint32_t)(a * BN);
+        umma_f16<BN>(td, ad, bd, 0u);
+        umma_f16<BN>(td, ad + (256 >> 4), bd + (256 >> 4), 1u);
+        umma_commit(smem_u32(&slot_empty[sl]));
+        umma_commit(smem_u32(&acc_full[a]));
+        issued = j + 1;
+      }
+      // the tensor core has finished everything issued before tensor memory is released
+      if (issued > 0) {
+        const int j = issued - 1;
+        if (!mbar_wait_bounded(smem_u32(&acc_full[j % C::kAcc]), (j / C::kAcc) & 1)) fail();
+      }
+    }
+  } else if (warp < 6) {
+    pdl_wait();
+    // ---------------- expanders: one weight row per thread ----------------
+    const int t = tid - 64;
+    const int row = m0 + t;
+    const bool row_ok = row < M;
+    const __half* srow = scales + (size_t)(row_ok ? row : 0) * nb;
+    float nwd = 0.0f;  // register path for the scales (rows not 16-byte aligned): next block's
+    if (!STMA && row_ok && jb > 0) nwd = __half2float(srow[b0]);
+    for (int j = 0; j < jb; ++j) {
+      const int s = j / KB, bi = j % KB, rs = s % kStages, sl = j % kSlots;
+      float wd = nwd;
+      if (!STMA && row_ok && j + 1 < jb) nwd = __half2float(srow[b0 + j + 1]);
+      bool ok = true;
+      if (bi == 0) ok = mbar_wait_bounded(smem_u32(&raw_full[rs]), (s / kStages) & 1);
+      if (ok && j >= kSlots) ok = mbar_wait_bounded(smem_u32(&slot_empty[sl]), ((j / kSlots) - 1) & 1);
+      const bool stop = __any_sync(0xFFFFFFFFu, !ok || *s_abort);  // one decision per warp
+      if (stop) {
+        if (!ok) fail();
+        break;
+      }
+      unsigned char* slot = slots + sl * C::kSlot;
+      const unsigned char* stage = raw + rs * kStageBytes;
+      const unsigned char* rrow = stage + t * 128;
+      unsigned char* adst = slot + (t >> 3) * 512 + (t & 7) * 16;
+      if (FMT == kFmtQ4_0) {
+        const uint4 q = lds128(rrow + ((bi ^ (t & 7)) << 4));
+        *reinterpret_cast<uint4*>(adst) = q4_chunk(q.x);
+        *reinterpret_cast<uint4*>(adst + 128) = q4_chunk(q.y);
+        *reinterpret_cast<uint4*>(adst + 256) = q4_chunk(q.z);
+        *reinterpret_cast<uint4*>(adst + 384) = q4_chunk(q.w);
+      } else {
+        const uint4 lo = lds128(rrow + (((2 * bi) ^ (t & 7)) << 4));
+        const uint4 hi = lds128(rrow + (((2 * bi + 1) ^ (t & 7)) << 4));
+        *reinterpret_cast<uint4*>(adst) = tiles_i8_chunk(lo.x, hi.x);
+        *reinterpret_cast<uint4*>(adst + 128) = tiles_i8_chunk(lo.y, hi.y);
+        *reinterpret_cast<uint4*>(adst + 256) = tiles_i8_chunk(lo.z, hi.z);
+        *reinterpret_cast<uint4*>(adst + 384) = tiles_i8_chunk(lo.w, hi.w);
+      }
+      if (STMA) {  // the stage's scale box: 8 blocks from ((st0 + s) * KB) & ~7
+        const int off = ((st0 + s) * KB) & 7;
+        wd = __half2float(reinterpret_cast<const __half*>(stage + kRawBytes + t * 16)[off + bi]);
+      }
+      reinterpret_cast<float*>(slot + kATile + C::kBTile + BN * 4)[t] = wd;
+      fence_proxy_async();  // generic-proxy writes become visible to the tensor core
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&slot_full[sl]));
+        if (bi == KB - 1 || j == jb - 1) mbar_arrive(smem_u32(&raw_empty[rs]));
+      }
+    }
+  } else {
+    pdl_wait();  // y may still be read by the previous kernel
+    // ---------------- epilogue: scales applied from tensor memory ----------------
+    const int e = warp - 6, q = warp & 3, ch = e >> 2;
+    const int lrow = 32 * q + lane, row = m0 + lrow;
+    const int col0 = ch * C::kCols;
+    unsigned long long acc2[C::kCols / 2];
+#pragma unroll
+    for (int i = 0; i < C::kCols / 2; ++i) acc2[i] = 0ull;  // (+0.0f, +0.0f)
+    for (int j = 0; j < jb; ++j) {
+      const int a = j % C::kAcc, sl = j % kSlots;
+      bool ok = mbar_wait_bounded(smem_u32(&acc_full[a]), (j / C::kAcc) & 1);
+      if (ok) ok = mbar_wait_bounded(smem_u32(&slot_full[sl]), (j / kSlots) & 1);
+      const bool stop = __any_sync(0xFFFFFFFFu, !ok || *s_abort);  // one decision per warp
+      if (stop) {
+        if (!ok) fail();
         break;
       }
       tc_fence_after();
-      uint32_t d[kGN];
-      tmem_ld64(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(buf * kGN), d);
-      const float wd = sWd[b * kGM + tid];
-      const unsigned long long* xd2 = reinterpret_cast<const unsigned long long*>(sXd + b * kGN);
-#pragma unroll
-      for (int n = 0; n < kGN / 2; ++n) acc[n] = scale_acc2(acc[n], (int)d[2 * n], (int)d[2 * n + 1], wd, xd2[n]);
+      const unsigned char* slot = slots + sl * C::kSlot;
+      const float* xd = reinterpret_cast<const float*>(slot + kATile + C::kBTile) + col0;
+      const float wd = reinterpret_cast<const float*>(slot + kATile + C::kBTile + BN * 4)[lrow];
+      const unsigned long long wd2 = pack2(wd, wd);
+      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * BN + col0);
+      if constexpr (C::kCols > 32) {
+        epi_chunk<BN, 32>(taddr, acc2, wd2, xd);
+        epi_chunk<BN, 32>(taddr + 32, acc2 + 16, wd2, xd + 32);
+      } else {
+        epi_chunk<BN, C::kCols>(taddr, acc2, wd2, xd);
+      }
       tc_fence_before();
-      __syncthreads();  // every thread has read accumulator buf: it may be overwritten
-      if (b + 2 < kb) issue(b + 2);
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&acc_empty[a]));
+        mbar_arrive(smem_u32(&slot_empty[sl]));
+      }
     }
-    if (more && ok) {  // chunk c-1's buffer is free (its MMAs completed): fill it with chunk c+1
-      store_chunk<FMT>(R, bufA(sb ^ 1), bufB(sb ^ 1), bufWd(sb ^ 1), bufXd(sb ^ 1), tid);
-      fence_proxy_async();
-    }
-    __syncthreads();
-  }
-
-  if (row < M) {
+    if (splits == 1) {
+      if (row < M) {
 #pragma unroll
-    for (int n = 0; n < kGN / 2; ++n) {
-      float a0, a1;
-      unpack2(acc[n], a0, a1);
-      if (n0 + 2 * n < N) y[(size_t)(n0 + 2 * n) * M + row] = a0;
-      if (n0 + 2 * n + 1 < N) y[(size_t)(n0 + 2 * n + 1) * M + row] = a1;
+        for (int i = 0; i < C::kCols / 2; ++i) {
+          float v0, v1;
+          unpack2(acc2[i], v0, v1);
+          const int n = n0 + col0 + 2 * i;
+          if (n < N) y[(size_t)n * M + row] = v0;
+          if (n + 1 < N) y[(size_t)(n + 1) * M + row] = v1;
+        }
+      }
+    } else if (!*s_abort) {
+      // Partial tile [BN][128] into the raw ring: once this warp has scaled the
+      // last block, every stage was consumed (the expanders read their raw
+      // data before publishing the slot the last MMA used).
+      float* part = reinterpret_cast<float*>(raw);
+#pragma unroll
+      for (int i = 0; i < C::kCols / 2; ++i) {
+        float v0, v1;
+        unpack2(acc2[i], v0, v1);
+        part[(col0 + 2 * i) * kGM + lrow] = v0;
+        part[(col0 + 2 * i + 1) * kGM + lrow] = v1;
+      }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)kTmemCols)
+  if (splits > 1) {
+    cluster_sync_all();  // every split's partial tile is in its shared memory
+    if (!*s_abort) {
+      const int E = kGM * BN;
+      const int e0 = (int)((long long)z * E / splits), e1 = (int)((long long)(z + 1) * E / splits);
+      const uint32_t pbase = smem_u32(raw);
+      for (int e = e0 + tid; e < e1; e += kThreads) {
+        const int n = e / kGM, r = e % kGM;
+        float s = 0.0f;
+        for (int src = 0; src < splits; ++src) s += ld_cluster_f32(pbase + 4u * (uint32_t)e, (uint32_t)src);
+        if (m0 + r < M && n0 + n < N) y[(size_t)(n0 + n) * M + m0 + r] = s;
+      }
+    }
+    cluster_sync_all();  // no CTA leaves while another reads its partial tile
+  }
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)C::kTmemCols)
                  : "memory");
+}
+
+// Activation images (asm_act_image_q8_0_async rows) -> activation tiles.
+__global__ void __launch_bounds__(256) act_tiles_from_image_kernel(const unsigned char* __restrict__ images,
+                                                                   size_t img_stride, int N, int nb, int np,
+                                                                   unsigned char* __restrict__ tiles) {
+  pdl_trigger();
+  pdl_wait();  // the images may come from the previous kernel
+  const long long total = (long long)nb * np;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total; i += (long long)gridDim.x * 256) {
+    const int b = (int)(i / np), n = (int)(i % np);
+    uint4 lo = make_uint4(0u, 0u, 0u, 0u), hi = lo;
+    float d = 0.0f;
+    if (n < N) {
+      const unsigned char* im = images + (size_t)n * img_stride;
+      lo = __ldcg(reinterpret_cast<const uint4*>(im + (size_t)b * 48));
+      hi = __ldcg(reinterpret_cast<const uint4*>(im + (size_t)b * 48 + 16));
+      d = __ldcg(reinterpret_cast<const float*>(im + (size_t)nb * 48) + 2 * b);
+    }
+    *reinterpret_cast<uint4*>(tiles + tiles_chunk_offset(np, n, b, 0)) = tiles_i8_chunk(lo.x, hi.x);
+    *reinterpret_cast<uint4*>(tiles + tiles_chunk_offset(np, n, b, 1)) = tiles_i8_chunk(lo.y, hi.y);
+    *reinterpret_cast<uint4*>(tiles + tiles_chunk_offset(np, n, b, 2)) = tiles_i8_chunk(lo.z, hi.z);
+    *reinterpret_cast<uint4*>(tiles + tiles_chunk_offset(np, n, b, 3)) = tiles_i8_chunk(lo.w, hi.w);
+    reinterpret_cast<float*>(tiles + (size_t)nb * np * 64)[i] = d;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, const void* base, uint64_t inner, uint64_t rows,
+               uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t gdim[2] = {inner, rows};
+  const cuuint64_t gstride[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estride[2] = {1u, 1u};
+  return encode(map, type, 2, const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int FMT, int BN, bool STMA>
+cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& smap, const __half* sp, const unsigned char* tiles,
+                      int np, float* y, int M, int N, int nb, int pre, cudaStream_t stream, unsigned* err) {
+  using C = Cfg<BN>;
+  auto kernel = q8act_gemm_kernel<FMT, BN, STMA>;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+  if (e != cudaSuccess) return e;
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  constexpr int KB = FMT == kFmtQ4_0 ? 8 : 4;
+  const int nst = (nb + KB - 1) / KB;
+  const long long tiles_n = (long long)((M + kGM - 1) / kGM) * ((N + BN - 1) / BN);
+  // one CTA per SM: split K while the tiles alone leave SMs idle
+  long long S = sms / tiles_n;
+  if (g_opt_gemm_splits.load() > 0) S = g_opt_gemm_splits.load();
+  if (S > 8) S = 8;
+  if (S > nst) S = nst;
+  if (S < 1) S = 1;
+  const int splits = (int)S;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((M + kGM - 1) / kGM), (unsigned)((N + BN - 1) / BN), (unsigned)splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (g_opt_pdl.load()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)splits;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kernel, wmap, smap, sp, tiles, np, y, M, N, nb, splits, pre, err);
+}
+
+template <int FMT, int BN>
+cudaError_t launch_scales(bool stma, const CUtensorMap& wmap, const CUtensorMap& smap, const __half* sp,
+                          const unsigned char* tiles, int np, float* y, int M, int N, int nb, int pre,
+                          cudaStream_t stream, unsigned* err) {
+  if (stma) return launch_bn<FMT, BN, true>(wmap, smap, sp, tiles, np, y, M, N, nb, pre, stream, err);
+  return launch_bn<FMT, BN, false>(wmap, smap, sp, tiles, np, y, M, N, nb, pre, stream, err);
+}
+
+template <int FMT>
+cudaError_t launch_fmt(bool stma, const CUtensorMap& wmap, const CUtensorMap& smap, const __half* sp,
+                       const unsigned char* tiles, int np, float* y, int M, int N, int nb, int pre,
+                       cudaStream_t stream, unsigned* err) {
+  if (N <= 16) return launch_scales<FMT, 16>(stma, wmap, smap, sp, tiles, np, y, M, N, nb, pre, stream, err);
+  if (N <= 32) return launch_scales<FMT, 32>(stma, wmap, smap, sp, tiles, np, y, M, N, nb, pre, stream, err);
+  if (N <= 64) return launch_scales<FMT, 64>(stma, wmap, smap, sp, tiles, np, y, M, N, nb, pre, stream, err);
+  return launch_scales<FMT, 128>(stma, wmap, smap, sp, tiles, np, y, M, N, nb, pre, stream, err);
 }
 
 }  // namespace
 
-size_t gemm_smem_bytes() {
-  return 2 * ((size_t)kKB * (kATile + kBTile) + (size_t)kKB * (kGM + kGN) * sizeof(float)) + 2 * sizeof(uint64_t) + 16;
+cudaError_t launch_q8act_gemm_tiles(int fmt, const void* w, const void* scales_f16, const void* tiles, float* y,
+                                    int64_t M, int64_t N, int64_t K, bool weights_static, cudaStream_t stream) {
+  const int nb = (int)(K / QK);
+  const int ub = fmt == kFmtQ4_0 ? 16 : 32;
+  // raw weights as a 2-D byte array [M rows][nb * ub bytes]; box 128 x 128 bytes, 128-byte swizzle
+  CUtensorMap wmap, smap;
+  if (!encode_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)nb * ub, (uint64_t)M, (uint64_t)nb * ub, 128u,
+                 (uint32_t)kGM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  // fp16 scales [M][nb] by TMA when their rows are 16-byte multiples: box 8 blocks x 128 rows
+  bool stma = nb % 8 == 0 && (uintptr_t)scales_f16 % 16 == 0;
+  if (stma && !encode_2d(&smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, scales_f16, (uint64_t)nb, (uint64_t)M,
+                         (uint64_t)nb * 2, 8u, (uint32_t)kGM, CU_TENSOR_MAP_SWIZZLE_NONE))
+    stma = false;
+  if (!stma) smap = wmap;  // unused
+  unsigned* err = device_error_word();
+  if (!err) return cudaErrorUnknown;
+  const __half* sp = static_cast<const __half*>(scales_f16);
+  const unsigned char* tp = static_cast<const unsigned char*>(tiles);
+  const int np = act_tiles_tokens(N), pre = weights_static ? 1 : 0;
+  if (fmt == kFmtQ4_0)
+    return launch_fmt<kFmtQ4_0>(stma, wmap, smap, sp, tp, np, y, (int)M, (int)N, nb, pre, stream, err);
+  return launch_fmt<kFmtQ8_0>(stma, wmap, smap, sp, tp, np, y, (int)M, (int)N, nb, pre, stream, err);
 }
 
-cudaError_t launch_q8act_gemm(int fmt, const void* w, const void* scales_f16, const void* images, size_t img_stride,
-                              float* y, int64_t M, int64_t N, int64_t K, cudaStream_t stream) {
-  const int nb = (int)(K / QK);
-  const size_t smem = gemm_smem_bytes();
-  auto kernel = fmt == kFmtQ4_0 ? q8act_gemm_kernel<kFmtQ4_0> : q8act_gemm_kernel<kFmtQ8_0>;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+cudaError_t launch_act_tiles_from_image(const void* images, size_t img_stride, int64_t N, int64_t K, void* tiles,
+                                        cudaStream_t stream) {
+  const int nb = (int)(K / QK), np = act_tiles_tokens(N);
+  const long long total = (long long)nb * np;
+  long long grid = (total + 255) / 256;
+  if (grid > 4096) grid = 4096;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((M + kGM - 1) / kGM), (unsigned)((N + kGN - 1) / kGN));
-  cfg.blockDim = dim3(kGThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(256);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = g_opt_pdl.load() ? 1 : 0;
-  const uint8_t* wp = static_cast<const uint8_t*>(w);
-  const __half* sp = static_cast<const __half*>(scales_f16);
-  const unsigned char* ip = static_cast<const unsigned char*>(images);
-  int Mi = (int)M, Ni = (int)N;
-  unsigned* err = device_error_word();
-  if (!err) return cudaErrorUnknown;
-  return cudaLaunchKernelEx(&cfg, kernel, wp, sp, ip, img_stride, y, Mi, Ni, nb, err);
+  return cudaLaunchKernelEx(&cfg, act_tiles_from_image_kernel, static_cast<const unsigned char*>(images), img_stride,
+                            (int)N, nb, np, static_cast<unsigned char*>(tiles));
+}
+
+// Images -> tiles (stream-ordered scratch from the device's default pool) -> product.
+cudaError_t launch_q8act_gemm(int fmt, const void* w, const void* scales_f16, const void* images, size_t img_stride,
+                              float* y, int64_t M, int64_t N, int64_t K, bool weights_static, cudaStream_t stream) {
+  void* tiles = nullptr;
+  cudaError_t e = cudaMallocAsync(&tiles, act_tiles_bytes(N, K), stream);
+  if (e != cudaSuccess) return e;
+  e = launch_act_tiles_from_image(images, img_stride, N, K, tiles, stream);
+  if (e == cudaSuccess) e = launch_q8act_gemm_tiles(fmt, w, scales_f16, tiles, y, M, N, K, weights_static, stream);
+  const cudaError_t f = cudaFreeAsync(tiles, stream);
+  return e != cudaSuccess ? e : f;
 }
 
 }  // namespace asmllm

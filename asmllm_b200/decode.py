@@ -108,6 +108,12 @@ def _unit_seed(seed: int, layer: int, kind: int, index: int) -> int:
 _Q, _K, _V, _O, _G, _U, _D, _NA, _NF, _LM, _FN, _EMB = range(12)
 
 
+def _f32_short(v) -> float:
+    """A float32 metadata value as the shortest decimal that rounds to it
+    (GGUF stores 1e-5 as float32 9.99999974e-06; the model shape keeps 1e-05)."""
+    return float(str(np.float32(v)))
+
+
 @dataclass(frozen=True)
 class Shard:
     """This rank's slice of a tensor-parallel model (Megatron-style split)."""
@@ -496,7 +502,7 @@ class LlamaDecoder:
                            n_kv_heads=int(md.get(f"{arch}.attention.head_count_kv", n_heads)),
                            head_dim=dim // n_heads, ffn=int(md[f"{arch}.feed_forward_length"]),
                            vocab=gg.tensors["token_embd.weight"].rows,
-                           eps=float(md.get(f"{arch}.attention.layer_norm_rms_epsilon", 1e-5)),
+                           eps=_f32_short(md.get(f"{arch}.attention.layer_norm_rms_epsilon", 1e-5)),
                            theta=float(md.get(f"{arch}.rope.freq_base", 10000.0)))
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         types = {gg.tensors[n].type for n in gg.tensors if n.endswith(".weight") and "norm" not in n

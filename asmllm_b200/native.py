@@ -59,6 +59,12 @@ class DecodeModel(ctypes.Structure):
                                      "h", "img_h", "counters", "logits", "best", "tokens", "pos")])
 
 
+class Rows(ctypes.Structure):
+    """asm_rows_t (include/asmllm.h): one batched RMSNorm / embed / residual step."""
+    _fields_ = [("rows", i32), ("dim", i32), ("x", vp), ("delta", vp), ("embed", vp), ("tokens", vp), ("pos", vp),
+                ("max_tokens", i32), ("vocab", i32), ("norm_w", vp), ("eps", f32), ("reserved", i32), ("tiles", vp)]
+
+
 # name -> (argtypes, restype); every symbol include/asmllm.h declares.
 SIGNATURES = {
     # reference ABI
@@ -76,6 +82,14 @@ SIGNATURES = {
     "asm_matmul_q5_mt": ([vp, vp, vp, vp, vp, i64, i64, c_int], None),
     "asm_matmul_q5_async": ([vp, vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_gemm_image_async": ([c_int, vp, vp, vp, i64, vp, i64, i64, i64, vp], c_int),
+    "asm_act_tiles_bytes": ([i64, i64], i64),
+    "asm_act_tiles_from_image_async": ([vp, i64, i64, i64, vp, vp], c_int),
+    "asm_gemm_tiles_async": ([c_int, vp, vp, vp, vp, i64, i64, i64, vp], c_int),
+    "asm_rows_norm_tiles_async": ([ctypes.POINTER(Rows), vp], c_int),
+    "asm_rows_swiglu_tiles_async": ([vp, i32, i32, vp, vp], c_int),
+    "asm_attention_batch_async": ([vp, i64, vp, vp, i64, vp, vp, vp, i32, i32, i32, i32, i32, f32, vp], c_int),
+    "asm_rows_argmax_async": ([vp, i32, i32, i64, i32, vp, vp], c_int),
+    "asm_rows_advance_async": ([vp, i32, vp, i32, vp, i32, vp], c_int),
     # additions
     "asm_matmul_q8q8": ([vp, vp, vp, vp, i64, i64], None),
     "asm_quantize_q8_0": ([vp, vp, vp, i64], None),

@@ -205,7 +205,8 @@ def unmark_static(*tensors) -> None:
 
 
 def set_option(name: str, value: int) -> int:
-    """asm_set_option: "tma" / "pdl" kernel-path switches; returns the previous value."""
+    """asm_set_option: "tma" / "pdl" kernel-path switches, "gemm_splits" (0 = automatic
+    K split of the batched product, S = exactly S); returns the previous value."""
     prev = int(native.lib().asm_set_option(name.encode(), int(value)))
     if prev < 0:
         native.check()
@@ -384,3 +385,91 @@ def gemm(fmt: int, qweights, scales, X, out=None, stream=None):
     (asm_act_image_q8_0_async), then the tensor-core product."""
     img = act_image_dev(X, stream=stream)
     return gemm_image(fmt, qweights, scales, img, X.shape[-1], out=out, stream=stream)
+
+
+def act_tiles_bytes(N: int, K: int) -> int:
+    """Bytes of the activation tiles of N rows of K values (asm_act_tiles_bytes)."""
+    n = int(native.lib().asm_act_tiles_bytes(N, K))
+    if n <= 0:
+        raise ValueError(f"no activation tiles for N={N}, K={K}")
+    return n
+
+
+def act_tiles_from_image(images, K: int, out=None, stream=None):
+    """Activation tiles (uint8) of the N activation-image rows (asm_act_tiles_from_image_async)."""
+    torch = _torch()
+    _check_dev(images, (torch.uint8,), "images")
+    N = images.shape[0]
+    if out is None:
+        out = torch.empty(act_tiles_bytes(N, K), dtype=torch.uint8, device=images.device)
+    native.check(native.lib().asm_act_tiles_from_image_async(_ptr(images), images.stride(0), N, K, _ptr(out),
+                                                             _stream_handle(stream)))
+    return out
+
+
+def gemm_tiles(fmt: int, qweights, scales, tiles, N: int, out=None, stream=None):
+    """Y [N, M] from N rows of activation tiles on the tensor cores (asm_gemm_tiles_async)."""
+    torch = _torch()
+    wdt = torch.uint8 if fmt == FMT_Q4_0 else torch.int8
+    _check_dev(qweights, (wdt,), "qweights")
+    _check_dev(scales, (torch.float16,), "scales")
+    _check_dev(tiles, (torch.uint8,), "tiles")
+    M, K = scales.shape[0], scales.shape[1] * 32
+    if tiles.numel() < act_tiles_bytes(N, K):
+        raise ValueError("tiles buffer too small")
+    if out is None:
+        out = torch.empty((N, M), dtype=torch.float32, device=tiles.device)
+    native.check(native.lib().asm_gemm_tiles_async(fmt, _ptr(qweights), _ptr(scales), _ptr(tiles), _ptr(out), M, N,
+                                                   K, _stream_handle(stream)))
+    return out
+
+
+def rows_norm_tiles(x, tiles, norm_w=None, eps: float = 1e-5, delta=None, embed=None, tokens=None, pos=None,
+                    stream=None):
+    """asm_rows_norm_tiles_async on x fp32 [B, dim] (updated in place when embed or delta is given)."""
+    d = native.Rows()
+    d.rows, d.dim = x.shape[0], x.shape[1]
+    d.eps = eps
+    for name, t in (("x", x), ("delta", delta), ("embed", embed), ("tokens", tokens), ("pos", pos),
+                    ("norm_w", norm_w), ("tiles", tiles)):
+        if t is not None:
+            setattr(d, name, t.data_ptr())
+    if embed is not None:
+        d.vocab, d.max_tokens = embed.shape[0], tokens.shape[1]
+    native.check(native.lib().asm_rows_norm_tiles_async(ctypes.byref(d), _stream_handle(stream)))
+    return tiles
+
+
+def rows_swiglu_tiles(gu, tiles, stream=None):
+    """asm_rows_swiglu_tiles_async: gu fp32 [B, 2*ffn] (gate/up pairs) -> tiles of h [B, ffn]."""
+    native.check(native.lib().asm_rows_swiglu_tiles_async(_ptr(gu), gu.shape[0], gu.shape[1] // 2, _ptr(tiles),
+                                                          _stream_handle(stream)))
+    return tiles
+
+
+def attention_batch(qkv, k_cache, v_cache, rope_cs, pos, tiles, n_heads: int, n_kv_heads: int, ctx: int,
+                    sqrt_head_dim: float, stream=None):
+    """asm_attention_batch_async: qkv fp32 [B, (nh + 2 nkv) * 128], caches fp16 [B, ctx, nkv, 128]."""
+    rows = qkv.shape[0]
+    native.check(native.lib().asm_attention_batch_async(
+        _ptr(qkv), qkv.stride(0), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), _ptr(rope_cs), _ptr(pos),
+        _ptr(tiles), rows, n_heads, n_kv_heads, 128, ctx, sqrt_head_dim, _stream_handle(stream)))
+    return tiles
+
+
+def rows_argmax(logits, keys, offset: int = 0, stream=None):
+    """asm_rows_argmax_async: keys int64 [B] = signed-orderable (value, offset + index) maxima."""
+    native.check(native.lib().asm_rows_argmax_async(_ptr(logits), logits.shape[0], logits.shape[1],
+                                                    logits.stride(0), offset, _ptr(keys), _stream_handle(stream)))
+    return keys
+
+
+def rows_advance(keys, tokens, pos, n_prompt: int, stream=None):
+    """asm_rows_advance_async: tokens[r][pos + 1] = argmax index of keys[r] after the prompt; pos += 1."""
+    native.check(native.lib().asm_rows_advance_async(_ptr(keys), keys.shape[0], _ptr(tokens), tokens.shape[1],
+                                                     _ptr(pos), n_prompt, _stream_handle(stream)))
+
+
+def key_index(keys):
+    """Index part of signed-orderable argmax keys (host or device int64 tensor)."""
+    return ((keys ^ (-(1 << 63))) & 0xFFFFFFFF).neg().add(0xFFFFFFFF)

@@ -408,11 +408,84 @@ ASMLLM_API int asm_decode_destroy(void* handle);
  * image_stride bytes, a multiple of 16).  Each output is the reference's
  * NEON combine for that row and token (s = wd * xd, acc = fma(float(isum),
  * s, acc) over the blocks in order), so it equals the Q4_0 x Q8_0 matvec of
- * the reference semantics bit for bit.  fp16 scales.  No single counterpart
- * in the reference (its batched work is one asm_matmul_q4 call per token). */
+ * the reference semantics bit for bit -- when K is not split.  When the
+ * 128-row x token tiles alone would leave SMs idle (small N), K is split into
+ * S <= 8 contiguous ranges of blocks, each an fma chain from zero, and the S
+ * partials are added in range order ((0 + p0) + p1) + ...: deterministic,
+ * within fp32 rounding of the unsplit result ("gemm_splits" option below).
+ * fp16 scales; qweights 16-byte aligned.  No single counterpart in the
+ * reference (its batched work is one asm_matmul_q4 call per token). */
 ASMLLM_API int asm_gemm_image_async(int fmt, const void* qweights, const void* scales_f16, const void* images,
                                     int64_t image_stride, float* y, int64_t M, int64_t N, int64_t K,
                                     void* stream);
+
+/* Activation tiles: N Q8_0-quantized rows of K values laid out as the fp16
+ * operand of the tensor-core product (the int8 quants are exact in fp16).
+ * np = N rounded up to 16, 32, 64 or a multiple of 128; plane B (K/32 * np *
+ * 64 bytes): block b, token n, position k at b*np*64 + (n/8)*512 + (k/8)*128
+ * + (n%8)*16 + (k%8)*2 holds the quant of element 32b + perm(k), perm(8c+j)
+ * = 4c + {0,2,1,3,16,18,17,19}[j]; plane D (K/32 * np floats) after it: the
+ * block scale of (b, n) at b*np + n.  Rows n >= N are zero.
+ * asm_act_tiles_bytes returns the size (0 for invalid N, K).
+ * asm_gemm_image_async is asm_act_tiles_from_image_async into stream-ordered
+ * scratch followed by asm_gemm_tiles_async; callers that produce tiles
+ * directly (the batched decode glue below) skip the conversion. */
+ASMLLM_API int64_t asm_act_tiles_bytes(int64_t N, int64_t K);
+ASMLLM_API int asm_act_tiles_from_image_async(const void* images, int64_t image_stride, int64_t N, int64_t K,
+                                              void* tiles, void* stream);
+ASMLLM_API int asm_gemm_tiles_async(int fmt, const void* qweights, const void* scales_f16, const void* tiles,
+                                    float* y, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Batched decode glue: B sequences in lockstep at one position (the
+ * reference's AsmEngineForward.forward_token, src/runtime/generate.py:255-326,
+ * run for B token rows at once; its matvecs become asm_gemm_tiles_async).
+ * One row per sequence; every kernel is stream-ordered and reads what the
+ * previous one wrote.
+ *   asm_rows_norm_tiles_async: per row, x <- embed[tokens[row][*pos]] (when
+ *     embed is set) or x + delta (when delta is set), written back to x; then
+ *     RMSNorm (x / sqrt(mean(x^2) + eps)) * norm_w (tests/reference/ops.py:
+ *     103-116; plain x when norm_w is NULL), quantized to Q8_0 into row `row`
+ *     of the rows' activation tiles.  Out-of-range token ids read row 0 and
+ *     set ASM_DEVERR_RANGE.
+ *   asm_rows_swiglu_tiles_async: gu [rows][2*ffn] with (gate_i, up_i) pairs
+ *     (the gate/up product of interleaved weight rows) -> h = (g / (1 +
+ *     exp(-g))) * u (generate.py:370) -> tiles of [rows][ffn].
+ *   asm_attention_batch_async: asm_attention_decode_async per row: q/k/v of
+ *     row r at qkv + r*qkv_stride (floats), its KV cache at k_cache/v_cache +
+ *     r*cache_stride (halves); output quantized into the tiles of [rows]
+ *     [n_heads*128].
+ *   asm_rows_argmax_async: keys[r] = the first maximum of logits row r
+ *     (n values at r*stride; NaN ignored) as a signed-orderable 64-bit key of
+ *     (value, offset + index): the max over int64 of the keys of several
+ *     vocabulary slices is the key of their combined argmax.
+ *   asm_rows_advance_async: tokens[r][*pos + 1] = the index of keys[r] when
+ *     *pos + 1 >= n_prompt (and < max_tokens); then *pos += 1. */
+typedef struct asm_rows {
+  int32_t rows;          /* B */
+  int32_t dim;           /* values per row, a multiple of 32 */
+  float* x;              /* [rows][dim] residual stream */
+  const float* delta;    /* [rows][dim] or NULL */
+  const float* embed;    /* [vocab][dim] or NULL */
+  const int32_t* tokens; /* [rows][max_tokens] (embed) */
+  const int32_t* pos;    /* [1] (embed) */
+  int32_t max_tokens;
+  int32_t vocab;
+  const float* norm_w;   /* [dim] or NULL */
+  float eps;
+  int32_t reserved;
+  void* tiles;           /* asm_act_tiles_bytes(rows, dim) */
+} asm_rows_t;
+
+ASMLLM_API int asm_rows_norm_tiles_async(const asm_rows_t* d, void* stream);
+ASMLLM_API int asm_rows_swiglu_tiles_async(const float* gu, int32_t rows, int32_t ffn, void* tiles, void* stream);
+ASMLLM_API int asm_attention_batch_async(const float* qkv, int64_t qkv_stride, void* k_cache, void* v_cache,
+                                         int64_t cache_stride, const float* rope_cs, const int32_t* pos, void* tiles,
+                                         int32_t rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                         int32_t ctx, float sqrt_head_dim, void* stream);
+ASMLLM_API int asm_rows_argmax_async(const float* logits, int32_t rows, int32_t n, int64_t stride, int32_t offset,
+                                     int64_t* keys, void* stream);
+ASMLLM_API int asm_rows_advance_async(const int64_t* keys, int32_t rows, int32_t* tokens, int32_t max_tokens,
+                                      int32_t* pos, int32_t n_prompt, void* stream);
 
 /* Q5_0 x fp32 on device pointers (see asm_matmul_q5), stream ordered. */
 ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const float* scales,
@@ -422,7 +495,10 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * (-1 for an unknown name).  "tma": 1 = Q8_0-activation matvecs use the
  * bulk-copy pipeline kernel where the shape allows (default), 0 = the
  * register-streaming kernels.  "pdl": programmatic dependent launch on/off.
- * Results are identical either way up to fp32 summation order. */
+ * "gemm_splits": 0 = the batched product picks its K split (default),
+ * S >= 1 = exactly S ranges (clamped to [1, 8] and to the number of 128-byte
+ * weight stages).  Results are identical either way up to fp32 summation
+ * order. */
 ASMLLM_API int asm_set_option(const char* name, int value);
 
 /* Largest K each matvec family supports (shared-memory staging of x). */

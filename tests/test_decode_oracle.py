@@ -59,6 +59,18 @@ def test_descriptor_layout_matches_header():
     assert pos == sorted(pos), "field order differs from include/asmllm.h"
 
 
+def test_rows_descriptor_layout_matches_header():
+    # asm_rows_t on LP64: 2 int32, 5 pointers, 2 int32, pointer, float + int32, pointer
+    assert ctypes.sizeof(native.Rows) == 80
+    assert native.Rows.norm_w.offset == 56 and native.Rows.tiles.offset == 72
+    text = (GOLDEN.parent.parent / "include" / "asmllm.h").read_text()
+    body = text[text.index("typedef struct asm_rows {"):text.index("} asm_rows_t;")]
+    body = re.sub(r"/\*.*?\*/", " ", body, flags=re.S)
+    names = [f for f, _ in native.Rows._fields_]
+    pos = [body.index(f" {n};") if f" {n};" in body else body.index(f"*{n};") for n in names]
+    assert pos == sorted(pos), "field order differs from include/asmllm.h"
+
+
 def test_shape_bytes():
     assert D.LLAMA_7B.weight_bytes() == 3_716_481_024
     assert D.LLAMA2_70B.weight_bytes() == 38_651_166_720

@@ -46,12 +46,15 @@ class BatchDecoder:
         self.tp, self.tp_rank, self.group = tp, tp_rank, group
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
+        # weights handed in (e.g. a batch-1 decoder's) stay under their owner's static declaration
+        self._owns = weights is None
         W = weights if weights is not None else make_weights(s, sh, seed, fmt, dev)
         self.layers, self.final_norm, self.lm_head, self.embed = W["layers"], W["final_norm"], W["lm_head"], W["embed"]
-        for L in self.layers:
-            for k in ("wqkv", "wo", "wgu", "wdown"):
-                ops.mark_static(*L[k])
-        ops.mark_static(*self.lm_head)
+        if self._owns:
+            for L in self.layers:
+                for k in ("wqkv", "wo", "wgu", "wdown"):
+                    ops.mark_static(*L[k])
+            ops.mark_static(*self.lm_head)
         hd = s.head_dim
         self.nh, self.nkv, self.ffn = len(sh.heads), len(sh.kv_heads), len(sh.ffn)
         self.vocab_l = len(sh.vocab)
@@ -177,7 +180,8 @@ class BatchDecoder:
 
     def close(self) -> None:
         self._graphs = {}
-        for L in self.layers:
-            for k in ("wqkv", "wo", "wgu", "wdown"):
-                ops.unmark_static(*L[k])
-        ops.unmark_static(*self.lm_head)
+        if self._owns:
+            for L in self.layers:
+                for k in ("wqkv", "wo", "wgu", "wdown"):
+                    ops.unmark_static(*L[k])
+            ops.unmark_static(*self.lm_head)

@@ -26,18 +26,25 @@
 // with one mask-or per two weights.
 //
 // CTA: 128 rows x BN tokens (BN in 16, 32, 64, 128), a contiguous range of
-// K blocks.  Warp roles (14 warps):
+// K blocks.  Warp roles (15 warps):
 //   0      producer: one TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) per
 //          stage of 128 rows x 128 bytes of raw weights (8 Q4_0 or 4 Q8_0
-//          blocks) into a 4-stage ring.
+//          blocks) plus the stage's fp16 scales, into a 4-stage ring.
+//   14     tile loader: per block the activation tile (fp16, already in
+//          operand layout, tiles.cuh) and its xd, by 16-byte LSU async copies
+//          (cp.async + cp.async.mbarrier.arrive).  (Through the TMA unit these
+//          small L2-resident copies queued behind the weight stages' HBM
+//          latency: ~1.5k cycles each.)
 //   1      MMA issuer: two tcgen05.mma kind::f16 (K = 16 each) per block into
-//          one of kAcc tensor-memory accumulators; tcgen05.commit releases the
-//          operand slot and publishes the accumulator.
-//   2..5   expanders, one row and one token each: raw weights -> fp16 A tile,
-//          the token's Q8_0 block (read from the image in L2) -> fp16 B tile,
-//          plus the block's wd and xd, into one of 4 operand slots.
-//   6..13  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its rows)
-//          and half of the BN columns, then acc += d * (wd * xd).
+//          the block's tensor-memory accumulator; one tcgen05.commit per group.
+//   2..    expanders (4 warps, or 8 with two threads per row for narrow tiles):
+//          raw weights -> fp16 A tiles and each block's wd.
+//   ..13   epilogue (8 warps, or 4): warp w reads tensor-memory lanes
+//          32*(w%4).. (its rows) and its share of the BN columns, then
+//          acc += d * (wd * xd) block by block.
+// The roles hand over groups of G blocks (one mbarrier handoff and one commit
+// per group): measured with a %clock64 trace of one CTA, a handoff costs a
+// few hundred cycles, which per single block made the kernel latency-bound.
 // Split K (when the tiles alone do not cover the SMs): the splits of one tile
 // form a thread-block cluster along z; each CTA leaves its partial tile in its
 // own shared memory and, after a cluster barrier, each CTA adds a slice of
@@ -76,30 +83,44 @@ std::atomic<int> g_opt_gemm_splits{0};
 namespace {
 
 constexpr int kGM = 128;                         // rows per CTA (MMA M)
-constexpr int kStages = 6;                       // raw weight ring
-constexpr int kSlots = 6;                        // operand slots (one block each)
+constexpr int kStages = 4;                       // raw weight ring
 constexpr int kRawBytes = kGM * 128;             // one raw stage: 128 rows x 128 bytes
 constexpr int kScaleBytes = kGM * 16;            // the stage's fp16 scales: 128 rows x 8 blocks
 constexpr int kStageBytes = kRawBytes + kScaleBytes;  // a multiple of 1024 (the swizzle period)
 constexpr int kATile = kGM * 64;                 // one block of A: 128 rows x 32 fp16
-constexpr int kThreads = 448;                    // 14 warps
-constexpr int kEpiWarps = 8;
+constexpr int kASlot = kATile + kGM * 4;         // A tile | wd[128]
+constexpr int kThreads = 480;                    // 15 warps
 constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
 constexpr uint32_t kSub8 = 0x64086408u;   // 1032.0: (1024 + nibble) - 1032 = nibble - 8
 static_assert(kStageBytes % 1024 == 0, "raw stages keep the 1024-byte swizzle alignment");
 
+// Rings.  Every handoff between roles costs a few hundred cycles (mbarrier
+// waits and arrivals, proxy fences, tcgen05 commits from one thread), so the
+// roles hand over groups of G blocks: R groups in flight, each with G A slots
+// (expanded weights + wd), G B entries (activation tile + xd) and G
+// tensor-memory accumulators of BN columns.
 template <int BN>
 struct Cfg {
   static constexpr int kBTile = BN * 64;
-  static constexpr int kSlot = kATile + kBTile + BN * 4 + kGM * 4;  // A | B | xd[BN] | wd[128]
-  static constexpr int kAcc = BN >= 128 ? 2 : 4;
-  static constexpr int kCols = BN / 2;  // accumulator columns per epilogue thread
-  static constexpr int kTmemCols = kAcc * BN < 32 ? 32 : kAcc * BN;
-  static constexpr int kBarOff = kStages * kStageBytes + kSlots * kSlot;
-  static constexpr int kSmem = kBarOff + 512 + 1024;  // barriers; room to align the ring to 1024 bytes
+  static constexpr int kBEntry = kBTile + BN * 4;  // B tile | xd[BN]
+  static constexpr int kG = BN >= 128 ? 1 : BN >= 64 ? 2 : 4;  // blocks per group
+  static constexpr int kR = BN >= 128 ? 4 : 3;                   // groups in flight
+  // warps 2 .. 13: expanders then epilogue.  Narrow tiles (decode batches) are
+  // bound by the weight expansion, wide ones by the epilogue.
+  static constexpr int kXW = BN >= 64 ? 4 : 8;  // expander warps (8: two threads per row)
+  static constexpr int kEW = 12 - kXW;           // epilogue warps (8: two column halves)
+  static constexpr int kCols = BN * 4 / kEW;     // accumulator columns per epilogue thread
+  static constexpr int kAccCols = kR * kG * BN;
+  static constexpr int kTmemCols = kAccCols <= 32 ? 32 : kAccCols <= 64 ? 64 : kAccCols <= 128 ? 128
+                                   : kAccCols <= 256 ? 256 : 512;
+  static constexpr int kAOff = kStages * kStageBytes;
+  static constexpr int kBOff = kAOff + kR * kG * kASlot;
+  static constexpr int kBarOff = kBOff + kR * kG * kBEntry;
+  static constexpr int kNBars = 2 * kStages + 3 * kR;
+  static constexpr int kSmem = kBarOff + kNBars * 8 + 16 + 1024;  // barriers, tmem word, abort; 1024-byte alignment
   static_assert(kGM * BN * 4 <= kStages * kStageBytes, "split-K partial tile must fit the raw ring");
-  static_assert((kTmemCols & (kTmemCols - 1)) == 0, "tensor memory allocation is a power of two");
-  static_assert((2 * kStages + 2 * kSlots + 8) * 8 + 8 <= 512, "barrier area");
+  static_assert(kAccCols <= 512, "tensor memory");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
 // kind::f16: D f32 (bit 4), A and B f16, both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
@@ -235,6 +256,46 @@ __device__ __forceinline__ void epi_chunk(uint32_t taddr, unsigned long long* ac
   }
 }
 
+// Epilogue of one group of G blocks for one thread: CH columns of each
+// block's accumulator, scaled in block order (the NEON combine order).  The
+// tensor-memory loads of several blocks go out together (one wait::ld), at
+// most 64 staging registers at a time (32 for wide rows).
+template <int BN, int G, int CH>
+__device__ __forceinline__ void epi_group(uint32_t taddr, int nblk, unsigned long long* acc2,
+                                          const unsigned char* aslots, const unsigned char* bentries, int lrow,
+                                          int col0) {
+  constexpr int kBEntry = BN * 64 + BN * 4;
+  constexpr int LC = CH < 32 ? CH : 32;         // columns per load
+  constexpr int NC = CH / LC;                   // loads per block
+  constexpr int NL = G * NC;                    // loads per group
+  constexpr int BATCH = (CH >= 64 ? 32 : 64) / LC;
+#pragma unroll
+  for (int l0 = 0; l0 < NL; l0 += BATCH) {
+    uint32_t d[BATCH][LC];
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) {
+      const int l = l0 + i, b = l / NC, c = l % NC;
+      if (l < NL && b < nblk) tmem_ld<LC>(taddr + (uint32_t)(b * BN + c * LC), d[i]);
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < BATCH; ++i) {
+      const int l = l0 + i, b = l / NC, c = l % NC;
+      if (l >= NL || b >= nblk) break;
+      const float wd = reinterpret_cast<const float*>(aslots + b * kASlot + kATile)[lrow];
+      const unsigned long long wd2 = pack2(wd, wd);
+      const float* xd = reinterpret_cast<const float*>(bentries + b * kBEntry + BN * 64) + col0 + c * LC;
+      unsigned long long* a2 = acc2 + c * (LC / 2);
+#pragma unroll
+      for (int k = 0; k < LC / 4; ++k) {
+        const float4 x4 = *reinterpret_cast<const float4*>(xd + 4 * k);
+        a2[2 * k] = scale_acc2(a2[2 * k], d[i][4 * k], d[i][4 * k + 1], wd2, pack2(x4.x, x4.y));
+        a2[2 * k + 1] = scale_acc2(a2[2 * k + 1], d[i][4 * k + 2], d[i][4 * k + 3], wd2, pack2(x4.z, x4.w));
+      }
+    }
+  }
+}
+
 template <int FMT, int BN, bool STMA>
 __global__ void __launch_bounds__(kThreads, 1)
 q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
@@ -242,19 +303,20 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
                   float* __restrict__ y, int M, int N, int nb, int splits, int pre, unsigned* __restrict__ err) {
   using C = Cfg<BN>;
   constexpr int KB = FMT == kFmtQ4_0 ? 8 : 4;  // blocks per raw stage
+  constexpr int G = C::kG, R = C::kR;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // the 128-byte swizzle of the raw ring repeats every 1024 bytes of shared address
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   unsigned char* raw = smem;
-  unsigned char* slots = smem + kStages * kStageBytes;
+  unsigned char* aring = smem + C::kAOff;
+  unsigned char* bring = smem + C::kBOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* raw_full = bars;
-  uint64_t* raw_empty = bars + kStages;
-  uint64_t* slot_full = bars + 2 * kStages;
-  uint64_t* slot_empty = bars + 2 * kStages + kSlots;
-  uint64_t* acc_full = bars + 2 * kStages + 2 * kSlots;
-  uint64_t* acc_empty = acc_full + 4;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(acc_empty + 4);
+  uint64_t* raw_empty = raw_full + kStages;
+  uint64_t* in_full = raw_empty + kStages;  // a group's A tiles (expanders) and B entries (tile loader)
+  uint64_t* mma_done = in_full + R;         // the group's MMAs completed (tcgen05.commit)
+  uint64_t* grp_done = mma_done + R;        // the epilogue finished the group: its slots may be reused
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(grp_done + R);
   volatile uint32_t* s_abort = s_tmem + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -265,6 +327,7 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
   const int b0 = st0 * KB;
   const int jb = min(st1 * KB, nb) - b0;  // blocks of this CTA
   const int ns = st1 - st0;
+  const int ng = (jb + G - 1) / G;        // groups of this CTA
 
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(s_tmem)),
@@ -275,15 +338,12 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&raw_full[i]), 1);
-      mbar_init(smem_u32(&raw_empty[i]), 4);
+      mbar_init(smem_u32(&raw_empty[i]), C::kXW);  // expander warps
     }
-    for (int i = 0; i < kSlots; ++i) {
-      mbar_init(smem_u32(&slot_full[i]), 4 + 1);           // expander warps + the producer's tile copy
-      mbar_init(smem_u32(&slot_empty[i]), 1 + kEpiWarps);  // MMA commit + epilogue warps
-    }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(smem_u32(&acc_full[i]), 1);
-      mbar_init(smem_u32(&acc_empty[i]), kEpiWarps);
+    for (int i = 0; i < R; ++i) {
+      mbar_init(smem_u32(&in_full[i]), C::kXW + 32);  // expander warps + the tile loader's lanes
+      mbar_init(smem_u32(&mma_done[i]), 1);
+      mbar_init(smem_u32(&grp_done[i]), C::kEW);
     }
     *s_abort = 0u;
     fence_mbar_init();
@@ -300,9 +360,9 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
   };
 
   if (warp == 0) {
-    // ---------------- producer: raw weight stages (TMA) and activation tiles (bulk) ----------------
+    // ---------------- producer: raw weight stages (TMA) ----------------
     if (lane == 0) {
-      int s_issued = 0, j_issued = 0;
+      int s_issued = 0;
       auto issue_stage = [&](int s) -> bool {
         const int rs = s % kStages;
         if (s >= kStages && !mbar_wait_bounded(smem_u32(&raw_empty[rs]), ((s / kStages) - 1) & 1)) return false;
@@ -315,152 +375,179 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       // weights declared static do not depend on the previous kernel: their first stages go out now
       if (pre)
         for (; s_issued < ns && s_issued < kStages; ++s_issued) issue_stage(s_issued);  // no wait below kStages
-      pdl_wait();  // the activation tiles come from the previous kernel
+      pdl_wait();
       bool ok = true;
-      for (int j = 0; j < jb && ok; ++j) {
-        while (ok && s_issued < ns && s_issued <= j / KB + kStages - 1) {
-          ok = issue_stage(s_issued);
-          if (ok) ++s_issued;
-        }
-        const int sl = j % kSlots;
-        if (ok && j >= kSlots) ok = mbar_wait_bounded(smem_u32(&slot_empty[sl]), ((j / kSlots) - 1) & 1);
-        if (!ok || *s_abort) break;
-        unsigned char* slot = slots + sl * C::kSlot;
-        const uint32_t full = smem_u32(&slot_full[sl]);
-        const size_t tb = (size_t)(b0 + j) * np + n0;  // this block's first token
-        mbar_arrive_expect_tx(full, BN * 68);
-        bulk_g2s(smem_u32(slot + kATile), tiles + tb * 64, BN * 64, full);
-        bulk_g2s(smem_u32(slot + kATile + C::kBTile), tiles + (size_t)nb * np * 64 + tb * 4, BN * 4, full);
-        j_issued = j + 1;
+      while (ok && s_issued < ns && !*s_abort) {
+        ok = issue_stage(s_issued);
+        if (ok) ++s_issued;
       }
       if (!ok) fail();
       // every issued copy lands before the CTA moves on (bounded)
       for (int s = s_issued - kStages < 0 ? 0 : s_issued - kStages; s < s_issued; ++s)
         if (!mbar_wait_bounded(smem_u32(&raw_full[s % kStages]), (s / kStages) & 1)) fail();
-      for (int j = j_issued - kSlots < 0 ? 0 : j_issued - kSlots; j < j_issued; ++j)
-        if (!mbar_wait_bounded(smem_u32(&slot_full[j % kSlots]), (j / kSlots) & 1)) fail();
     } else {
       pdl_wait();
     }
+  } else if (warp == 14) {
+    // ---------------- tile loader: activation tiles by LSU async copies (not the TMA
+    // queue, where they would wait behind the weight stages' HBM latency) ----------------
+    pdl_wait();  // the activation tiles come from the previous kernel
+    for (int g = 0; g < ng; ++g) {
+      const int r = g % R;
+      bool ok = true;
+      if (g >= R) ok = mbar_wait_bounded(smem_u32(&grp_done[r]), ((g / R) - 1) & 1);
+      if (__any_sync(0xFFFFFFFFu, !ok || *s_abort)) {  // one decision per warp
+        if (!ok) fail();
+        break;
+      }
+      for (int b = 0; b < G && g * G + b < jb; ++b) {
+        unsigned char* be = bring + (r * G + b) * C::kBEntry;
+        const size_t tb = (size_t)(b0 + g * G + b) * np + n0;  // the block's first token
+        const unsigned char* st = tiles + tb * 64;
+        const unsigned char* sx = tiles + (size_t)nb * np * 64 + tb * 4;
+        for (int c = lane; c < C::kBTile / 16; c += 32) cp_async16(be + 16 * c, st + 16 * c);
+        for (int c = lane; c < BN * 4 / 16; c += 32) cp_async16(be + C::kBTile + 16 * c, sx + 16 * c);
+      }
+      // this lane's arrival on in_full happens when its copies have landed
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&in_full[r])) : "memory");
+    }
+    cp_async_wait_all();  // nothing in flight when the CTA moves on
   } else if (warp == 1) {
     pdl_wait();
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer: one handoff per group of G blocks ----------------
     if (lane == 0) {
       int issued = 0;
-      for (int j = 0; j < jb; ++j) {
-        const int sl = j % kSlots, a = j % C::kAcc;
-        if (!mbar_wait_bounded(smem_u32(&slot_full[sl]), (j / kSlots) & 1)) {
-          fail();
-          break;
-        }
-        if (j >= C::kAcc && !mbar_wait_bounded(smem_u32(&acc_empty[a]), ((j / C::kAcc) - 1) & 1)) {
+      for (int g = 0; g < ng; ++g) {
+        const int r = g % R;
+        bool ok = mbar_wait_bounded(smem_u32(&in_full[r]), (g / R) & 1);
+        if (ok && g >= R) ok = mbar_wait_bounded(smem_u32(&grp_done[r]), ((g / R) - 1) & 1);  // accumulators free
+        if (!ok) {
           fail();
           break;
         }
         if (*s_abort) break;
+        fence_proxy_async();  // the B entries were written by generic-proxy async copies
         tc_fence_after();
-        unsigned char* slot = slots + sl * C::kSlot;
-        const uint64_t ad = umma_desc(smem_u32(slot)), bd = umma_desc(smem_u32(slot + kATile));
-        const uint32_t td = tmem + (uint32_t)(a * BN);
-        umma_f16<BN>(td, ad, bd, 0u);
-        umma_f16<BN>(td, ad + (256 >> 4), bd + (256 >> 4), 1u);
-        umma_commit(smem_u32(&slot_empty[sl]));
-        umma_commit(smem_u32(&acc_full[a]));
-        issued = j + 1;
+        for (int b = 0; b < G && g * G + b < jb; ++b) {
+          const uint64_t ad = umma_desc(smem_u32(aring + (r * G + b) * kASlot));
+          const uint64_t bd = umma_desc(smem_u32(bring + (r * G + b) * C::kBEntry));
+          const uint32_t td = tmem + (uint32_t)((r * G + b) * BN);
+          umma_f16<BN>(td, ad, bd, 0u);
+          umma_f16<BN>(td, ad + (256 >> 4), bd + (256 >> 4), 1u);
+        }
+        umma_commit(smem_u32(&mma_done[r]));
+        issued = g + 1;
       }
       // the tensor core has finished everything issued before tensor memory is released
       if (issued > 0) {
-        const int j = issued - 1;
-        if (!mbar_wait_bounded(smem_u32(&acc_full[j % C::kAcc]), (j / C::kAcc) & 1)) fail();
+        const int g = issued - 1;
+        if (!mbar_wait_bounded(smem_u32(&mma_done[g % R]), (g / R) & 1)) fail();
       }
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + C::kXW) {
     pdl_wait();
-    // ---------------- expanders: one weight row per thread ----------------
-    const int t = tid - 64;
+    // ---------------- expanders: one weight row per thread (two with 8 warps) ----------------
+    constexpr int kParts = C::kXW / 4;  // threads per row
+    constexpr int kCh = 4 / kParts;     // 16-byte chunks of the A row each writes
+    const int tx = tid - 64;
+    const int t = tx & 127, part = tx >> 7;
     const int row = m0 + t;
     const bool row_ok = row < M;
     const __half* srow = scales + (size_t)(row_ok ? row : 0) * nb;
-    float nwd = 0.0f;  // register path for the scales (rows not 16-byte aligned): next block's
-    if (!STMA && row_ok && jb > 0) nwd = __half2float(srow[b0]);
-    for (int j = 0; j < jb; ++j) {
-      const int s = j / KB, bi = j % KB, rs = s % kStages, sl = j % kSlots;
-      float wd = nwd;
-      if (!STMA && row_ok && j + 1 < jb) nwd = __half2float(srow[b0 + j + 1]);
+    for (int g = 0; g < ng; ++g) {
+      const int r = g % R;
       bool ok = true;
-      if (bi == 0) ok = mbar_wait_bounded(smem_u32(&raw_full[rs]), (s / kStages) & 1);
-      if (ok && j >= kSlots) ok = mbar_wait_bounded(smem_u32(&slot_empty[sl]), ((j / kSlots) - 1) & 1);
-      const bool stop = __any_sync(0xFFFFFFFFu, !ok || *s_abort);  // one decision per warp
-      if (stop) {
+      if (g >= R) ok = mbar_wait_bounded(smem_u32(&grp_done[r]), ((g / R) - 1) & 1);
+      if (__any_sync(0xFFFFFFFFu, !ok || *s_abort)) {  // one decision per warp
         if (!ok) fail();
         break;
       }
-      unsigned char* slot = slots + sl * C::kSlot;
-      const unsigned char* stage = raw + rs * kStageBytes;
-      const unsigned char* rrow = stage + t * 128;
-      unsigned char* adst = slot + (t >> 3) * 512 + (t & 7) * 16;
-      if (FMT == kFmtQ4_0) {
-        const uint4 q = lds128(rrow + ((bi ^ (t & 7)) << 4));
-        *reinterpret_cast<uint4*>(adst) = q4_chunk(q.x);
-        *reinterpret_cast<uint4*>(adst + 128) = q4_chunk(q.y);
-        *reinterpret_cast<uint4*>(adst + 256) = q4_chunk(q.z);
-        *reinterpret_cast<uint4*>(adst + 384) = q4_chunk(q.w);
-      } else {
-        const uint4 lo = lds128(rrow + (((2 * bi) ^ (t & 7)) << 4));
-        const uint4 hi = lds128(rrow + (((2 * bi + 1) ^ (t & 7)) << 4));
-        *reinterpret_cast<uint4*>(adst) = tiles_i8_chunk(lo.x, hi.x);
-        *reinterpret_cast<uint4*>(adst + 128) = tiles_i8_chunk(lo.y, hi.y);
-        *reinterpret_cast<uint4*>(adst + 256) = tiles_i8_chunk(lo.z, hi.z);
-        *reinterpret_cast<uint4*>(adst + 384) = tiles_i8_chunk(lo.w, hi.w);
+      bool stop = false;
+      for (int b = 0; b < G && g * G + b < jb; ++b) {
+        const int j = g * G + b;
+        const int s = j / KB, bi = j % KB, rs = s % kStages;
+        if (bi == 0) {
+          const bool okr = mbar_wait_bounded(smem_u32(&raw_full[rs]), (s / kStages) & 1);
+          if (__any_sync(0xFFFFFFFFu, !okr || *s_abort)) {
+            if (!okr) fail();
+            stop = true;
+            break;
+          }
+        }
+        unsigned char* slot = aring + (r * G + b) * kASlot;
+        const unsigned char* stage = raw + rs * kStageBytes;
+        const unsigned char* rrow = stage + t * 128;
+        unsigned char* adst = slot + (t >> 3) * 512 + (t & 7) * 16 + part * kCh * 128;
+        if (kParts == 1) {
+          if (FMT == kFmtQ4_0) {
+            const uint4 q = lds128(rrow + ((bi ^ (t & 7)) << 4));
+            *reinterpret_cast<uint4*>(adst) = q4_chunk(q.x);
+            *reinterpret_cast<uint4*>(adst + 128) = q4_chunk(q.y);
+            *reinterpret_cast<uint4*>(adst + 256) = q4_chunk(q.z);
+            *reinterpret_cast<uint4*>(adst + 384) = q4_chunk(q.w);
+          } else {
+            const uint4 lo = lds128(rrow + (((2 * bi) ^ (t & 7)) << 4));
+            const uint4 hi = lds128(rrow + (((2 * bi + 1) ^ (t & 7)) << 4));
+            *reinterpret_cast<uint4*>(adst) = tiles_i8_chunk(lo.x, hi.x);
+            *reinterpret_cast<uint4*>(adst + 128) = tiles_i8_chunk(lo.y, hi.y);
+            *reinterpret_cast<uint4*>(adst + 256) = tiles_i8_chunk(lo.z, hi.z);
+            *reinterpret_cast<uint4*>(adst + 384) = tiles_i8_chunk(lo.w, hi.w);
+          }
+        } else {  // half a row: words 2*part, 2*part + 1 -> chunks 2*part, 2*part + 1
+          if (FMT == kFmtQ4_0) {
+            const uint2 q = *reinterpret_cast<const uint2*>(rrow + ((bi ^ (t & 7)) << 4) + part * 8);
+            *reinterpret_cast<uint4*>(adst) = q4_chunk(q.x);
+            *reinterpret_cast<uint4*>(adst + 128) = q4_chunk(q.y);
+          } else {
+            const uint2 lo = *reinterpret_cast<const uint2*>(rrow + (((2 * bi) ^ (t & 7)) << 4) + part * 8);
+            const uint2 hi = *reinterpret_cast<const uint2*>(rrow + (((2 * bi + 1) ^ (t & 7)) << 4) + part * 8);
+            *reinterpret_cast<uint4*>(adst) = tiles_i8_chunk(lo.x, hi.x);
+            *reinterpret_cast<uint4*>(adst + 128) = tiles_i8_chunk(lo.y, hi.y);
+          }
+        }
+        float wd;
+        if (STMA) {  // the stage's scale box: 8 blocks from ((st0 + s) * KB) & ~7
+          const int off = ((st0 + s) * KB) & 7;
+          wd = __half2float(reinterpret_cast<const __half*>(stage + kRawBytes + t * 16)[off + bi]);
+        } else {
+          wd = row_ok ? __half2float(srow[b0 + j]) : 0.0f;
+        }
+        if (part == 0) reinterpret_cast<float*>(slot + kATile)[t] = wd;
+        if (bi == KB - 1 || j == jb - 1) {  // this warp is done with the raw stage
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&raw_empty[rs]));
+        }
       }
-      if (STMA) {  // the stage's scale box: 8 blocks from ((st0 + s) * KB) & ~7
-        const int off = ((st0 + s) * KB) & 7;
-        wd = __half2float(reinterpret_cast<const __half*>(stage + kRawBytes + t * 16)[off + bi]);
-      }
-      reinterpret_cast<float*>(slot + kATile + C::kBTile + BN * 4)[t] = wd;
+      if (stop) break;
       fence_proxy_async();  // generic-proxy writes become visible to the tensor core
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(&slot_full[sl]));
-        if (bi == KB - 1 || j == jb - 1) mbar_arrive(smem_u32(&raw_empty[rs]));
-      }
+      if (lane == 0) mbar_arrive(smem_u32(&in_full[r]));
     }
   } else {
     pdl_wait();  // y may still be read by the previous kernel
     // ---------------- epilogue: scales applied from tensor memory ----------------
-    const int e = warp - 6, q = warp & 3, ch = e >> 2;
+    const int ew = warp - 2 - C::kXW, q = warp & 3, ch = ew >> 2;
     const int lrow = 32 * q + lane, row = m0 + lrow;
     const int col0 = ch * C::kCols;
     unsigned long long acc2[C::kCols / 2];
 #pragma unroll
     for (int i = 0; i < C::kCols / 2; ++i) acc2[i] = 0ull;  // (+0.0f, +0.0f)
-    for (int j = 0; j < jb; ++j) {
-      const int a = j % C::kAcc, sl = j % kSlots;
-      bool ok = mbar_wait_bounded(smem_u32(&acc_full[a]), (j / C::kAcc) & 1);
-      if (ok) ok = mbar_wait_bounded(smem_u32(&slot_full[sl]), (j / kSlots) & 1);
-      const bool stop = __any_sync(0xFFFFFFFFu, !ok || *s_abort);  // one decision per warp
-      if (stop) {
+    for (int g = 0; g < ng; ++g) {
+      const int r = g % R;
+      bool ok = mbar_wait_bounded(smem_u32(&mma_done[r]), (g / R) & 1);
+      // (the MMA saw in_full complete; this wait gives this warp the expanders' and copies' writes)
+      if (ok) ok = mbar_wait_bounded(smem_u32(&in_full[r]), (g / R) & 1);
+      if (__any_sync(0xFFFFFFFFu, !ok || *s_abort)) {  // one decision per warp
         if (!ok) fail();
         break;
       }
       tc_fence_after();
-      const unsigned char* slot = slots + sl * C::kSlot;
-      const float* xd = reinterpret_cast<const float*>(slot + kATile + C::kBTile) + col0;
-      const float wd = reinterpret_cast<const float*>(slot + kATile + C::kBTile + BN * 4)[lrow];
-      const unsigned long long wd2 = pack2(wd, wd);
-      const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(a * BN + col0);
-      if constexpr (C::kCols > 32) {
-        epi_chunk<BN, 32>(taddr, acc2, wd2, xd);
-        epi_chunk<BN, 32>(taddr + 32, acc2 + 16, wd2, xd + 32);
-      } else {
-        epi_chunk<BN, C::kCols>(taddr, acc2, wd2, xd);
-      }
+      const int nblk = min(G, jb - g * G);
+      epi_group<BN, G, C::kCols>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(r * G * BN + col0), nblk, acc2,
+                       aring + r * G * kASlot, bring + r * G * C::kBEntry, lrow, col0);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(&acc_empty[a]));
-        mbar_arrive(smem_u32(&slot_empty[sl]));
-      }
+      if (lane == 0) mbar_arrive(smem_u32(&grp_done[r]));
     }
     if (splits == 1) {
       if (row < M) {
@@ -475,8 +562,8 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       }
     } else if (!*s_abort) {
       // Partial tile [BN][128] into the raw ring: once this warp has scaled the
-      // last block, every stage was consumed (the expanders read their raw
-      // data before publishing the slot the last MMA used).
+      // last group, every stage was consumed (the expanders read their raw
+      // data before publishing the group the last MMAs used).
       float* part = reinterpret_cast<float*>(raw);
 #pragma unroll
       for (int i = 0; i < C::kCols / 2; ++i) {
@@ -496,10 +583,10 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       const int e0 = (int)((long long)z * E / splits), e1 = (int)((long long)(z + 1) * E / splits);
       const uint32_t pbase = smem_u32(raw);
       for (int e = e0 + tid; e < e1; e += kThreads) {
-        const int n = e / kGM, r = e % kGM;
+        const int n = e / kGM, rr = e % kGM;
         float s = 0.0f;
         for (int src = 0; src < splits; ++src) s += ld_cluster_f32(pbase + 4u * (uint32_t)e, (uint32_t)src);
-        if (m0 + r < M && n0 + n < N) y[(size_t)(n0 + n) * M + m0 + r] = s;
+        if (m0 + rr < M && n0 + n < N) y[(size_t)(n0 + n) * M + m0 + rr] = s;
       }
     }
     cluster_sync_all();  // no CTA leaves while another reads its partial tile

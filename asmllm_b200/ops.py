@@ -380,11 +380,16 @@ def gemm_image(fmt: int, qweights, scales, images, K: int, out=None, stream=None
     return out
 
 
-def gemm(fmt: int, qweights, scales, X, out=None, stream=None):
+def gemm(fmt: int, qweights, scales, X, out=None, stream=None, tiles=None):
     """Y [N, M] = W x_n for the N rows of X fp32 [N, K]: quantize every row to Q8_0
-    (asm_act_image_q8_0_async), then the tensor-core product."""
-    img = act_image_dev(X, stream=stream)
-    return gemm_image(fmt, qweights, scales, img, X.shape[-1], out=out, stream=stream)
+    into activation tiles (asm_rows_norm_tiles_async without a norm), then the
+    tensor-core product (asm_gemm_tiles_async)."""
+    torch = _torch()
+    N, K = X.shape
+    if tiles is None:
+        tiles = torch.empty(act_tiles_bytes(N, K), dtype=torch.uint8, device=X.device)
+    rows_norm_tiles(X, tiles, stream=stream)
+    return gemm_tiles(fmt, qweights, scales, tiles, N, out=out, stream=stream)
 
 
 def act_tiles_bytes(N: int, K: int) -> int:

@@ -238,6 +238,8 @@ def main():
                     help="greedy steps of the 7B batch-1 decode timed after the matvec sweep (0: skip)")
     ap.add_argument("--decode70-steps", type=int, default=64,
                     help="greedy steps of the Llama-2-70B-shape decode, tensor-parallel over the N GPUs (0: skip)")
+    ap.add_argument("--decode70-batch", type=int, default=32,
+                    help="rows of the batched Llama-2-70B-shape decode timed after the batch-1 one (0: skip)")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the batched (prefill) tensor-core product at N = 8, 64, 512 tokens")
     ap.add_argument("--mode", choices=["image", "fused"], default="fused",
@@ -535,28 +537,40 @@ def main():
     if not args.no_prefill:
         gen.manual_seed(base + 33)
         pre_shapes = [(4096, 4096), (11008, 4096), (4096, 11008)]
-        Wp = [make_q4(M, K, base + 40 + i) for i, (M, K) in enumerate(pre_shapes)]
+        # three copies of each matrix, used in turn: 180 MB of weights > the 126 MB L2
+        Wp = [[make_q4(M, K, base + 40 + 10 * c + i) for i, (M, K) in enumerate(pre_shapes)] for c in range(3)]
+        for row in Wp:
+            for qs, d in row:
+                ops.mark_static(qs, d)
         prefill = {}
         for N in (8, 64, 512):
             row = {}
-            for (qs, d), (M, K) in zip(Wp, pre_shapes):
+            for i, (M, K) in enumerate(pre_shapes):
                 X = torch.randn((N, K), device=dev, generator=gen)
-                img = ops.act_image_dev(X)
+                tiles = torch.empty(ops.act_tiles_bytes(N, K), dtype=torch.uint8, device=dev)
                 out = torch.empty((N, M), device=dev)
-                for _ in range(3):
-                    ops.gemm_image(FMT_Q4_0, qs, d, img, K, out=out)
+                for c in range(3):
+                    ops.gemm(FMT_Q4_0, *Wp[c][i], X, out=out, tiles=tiles)
                 torch.cuda.synchronize()
-                reps = 20
-                a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 30
+                a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 a0.record()
-                for _ in range(reps):
-                    ops.gemm_image(FMT_Q4_0, qs, d, img, K, out=out)
+                for r in range(reps):  # the product alone, from the activation tiles
+                    ops.gemm_tiles(FMT_Q4_0, *Wp[r % 3][i], tiles, N, out=out)
                 a1.record()
-                a1.synchronize()
+                for r in range(reps):  # quantize the fp32 rows into tiles, then the product
+                    ops.gemm(FMT_Q4_0, *Wp[r % 3][i], X, out=out, tiles=tiles)
+                a2.record()
+                a2.synchronize()
                 t = a0.elapsed_time(a1) / reps / 1e3
+                tq = a1.elapsed_time(a2) / reps / 1e3
                 row[f"{M}x{K}"] = {"us": round(t * 1e6, 2), "TOPS": round(2.0 * M * N * K / t / 1e12, 1),
-                                   "weight_GB/s": round(q4_bytes(M, K) / t / 1e9, 1)}
+                                   "weight_GB/s": round(q4_bytes(M, K) / t / 1e9, 1),
+                                   "us_with_quantize": round(tq * 1e6, 2)}
             prefill[f"N={N}"] = row
+        for row in Wp:
+            for qs, d in row:
+                ops.unmark_static(qs, d)
         del Wp
         torch.cuda.empty_cache()
 
@@ -604,6 +618,44 @@ def main():
             "achieved_GB/s_per_gpu": round((wb70 + kv70) / world / per_tok / 1e9, 1),
             "first_tokens": toks70[:8], "device_error": err70,
         }
+        # batch 32 on the same weights: every projection one tensor-core product over the 32 rows,
+        # an NCCL all-reduce after o and down when tensor-parallel
+        if args.decode70_batch > 0:
+            from asmllm_b200 import batch_decode as BD
+
+            B70 = args.decode70_batch
+            W70 = {"layers": dec.layers, "final_norm": dec.final_norm, "lm_head": dec.lm_head, "embed": dec.embed}
+            bd = BD.BatchDecoder(shape70, B70, ctx=1024, seed=70, tp=world, tp_rank=rank, group=None, weights=W70)
+            prompts = np.random.default_rng(2).integers(0, shape70.vocab, (B70, 16))  # same on every rank
+            bd.generate(prompts, n70)  # warm-up and graph capture
+            bd.reset(prompts)
+            bd.run(prompts.shape[1] - 1)
+            barrier()
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record()
+            bd.run(n70)
+            b1.record()
+            b1.synchronize()
+            barrier()
+            tb = b0.elapsed_time(b1)
+            if world > 1:
+                tt = torch.tensor([tb], device=dev, dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                tb = float(tt.item())
+            kvb = B70 * kv70
+            decode70["batch"] = {
+                "batch": B70, "tokens_per_s": round(B70 * n70 / (tb / 1e3), 1),
+                "ms_per_step": round(tb / n70, 4), "greedy_steps": n70, "prompt_tokens": 16,
+                "engine": "CUDA graphs of per-operation launches; tcgen05 batched product per projection, "
+                          + ("NCCL all-reduce after o and down, max all-reduce of the argmax keys"
+                             if world > 1 else "no collective (one GPU)"),
+                "launches_per_step": bd.launches_per_step,
+                "kv_bytes_per_step_avg": round(kvb),
+                "achieved_GB/s_per_gpu": round((wb70 + kvb) / world / (tb / 1e3 / n70) / 1e9, 1),
+                "first_tokens_row0": bd.tokens[0, 16:24].cpu().tolist(), "device_error": ops.device_error(),
+            }
+            bd.close()
+            del bd
         dec.close()
         del dec
         torch.cuda.empty_cache()
@@ -673,22 +725,33 @@ def main():
             decode["reference_cpu_estimate_basis"] = ("weight bytes per token / the cpu_baseline matvec GB/s "
                                                       "(derived, not a measured reference decode)")
         line["decode_7b"] = decode
+        line["gpu_launches_decode"] = decode["launches"] * world
     if prefill is not None:
         pk = ROOT / "MEASURED_PEAKS.json"
         bf16 = float(json.loads(pk.read_text()).get("bf16_tflops", 0.0)) if pk.exists() else 0.0
         line["prefill_gemm"] = {
-            "kernel": "tcgen05.mma kind::i8 (M=128 rows x N=64 tokens x K=32 per block) with the per-32-block "
-                      "scales applied from tensor memory in fp32; Q4_0 expanded to int8 in shared memory",
-            "ops": "2*M*N*K int8 multiply-adds per call", "per_shape": prefill,
-            "peak_note": f"dense int8 tensor peak = 2x the measured bf16 {bf16} TFLOP/s (MEASURED_PEAKS.json)",
+            "kernel": "warp-specialized tcgen05.mma kind::f16 (M=128 rows x N<=128 tokens, two K=16 MMAs per "
+                      "32-block) on the exact small integers (nibble-8, int8 quants in fp16), per-32-block scales "
+                      "applied in fp32 from tensor memory; Q4_0 stages by TMA (tensor map, 128-byte swizzle), "
+                      "activation tiles by bulk copy; K split over a cluster (DSMEM reduction) when N is small",
+            "ops": "2*M*N*K multiply-adds per call; 'us' = the product from activation tiles, 'us_with_quantize' "
+                   "= quantizing the fp32 rows into tiles plus the product",
+            "l2": "three weight copies per shape used in turn (> 126 MB L2)", "per_shape": prefill,
+            "peak_note": f"dense int8 tensor peak = 2x the measured bf16 {bf16} TFLOP/s (MEASURED_PEAKS.json); "
+                         f"the fp16 path's own dense peak is the bf16 figure",
         }
     if decode70 is not None:
         decode70["frac_of_measured_hbm"] = round(decode70["achieved_GB/s_per_gpu"] / peak, 4)
         # every GPU streams its 1/N of the weights and KV per token at the measured copy peak
         decode70["roofline_tokens_per_s"] = round(
             peak * 1e9 * world / (decode70["weight_bytes_per_token_per_gpu"] * world + decode70["kv_bytes_per_token_avg"]), 2)
+        if "batch" in decode70:
+            bt = decode70["batch"]
+            bt["frac_of_measured_hbm"] = round(bt["achieved_GB/s_per_gpu"] / peak, 4)
+            bt["roofline_tokens_per_s"] = round(bt["batch"] * peak * 1e9 * world
+                                                / (decode70["weight_bytes_per_token_per_gpu"] * world
+                                                   + bt["kv_bytes_per_step_avg"]), 1)
         line["decode_70b"] = decode70
-        line["gpu_launches_decode"] = decode["launches"] * world
     line.update(extras)
     print(json.dumps(line), flush=True)
     if world > 1:

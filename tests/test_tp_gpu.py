@@ -58,7 +58,38 @@ def _worker(rank, world, port, shape_args, seq, q):
         dist.destroy_process_group()
 
 
-def _run(shape_args, seq):
+def _batch_worker(rank, world, port, shape_args, prompts, q):
+    import torch
+    import torch.distributed as dist
+
+    from asmllm_b200 import batch_decode as BD
+    from asmllm_b200 import decode as D
+    from asmllm_b200 import ops
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        shape = D.LlamaShape(**shape_args)
+        dec = BD.BatchDecoder(shape, len(prompts), ctx=32, seed=21, tp=world, tp_rank=rank, group=None)
+        toks = dec.generate(np.array(prompts), 1)
+        out = (toks, dec.logits.cpu().numpy(), ops.device_error())
+        dec.close()
+        gathered = [None] * world
+        dist.all_gather_object(gathered, out)
+        dist.barrier()
+        if rank == 0:
+            ref = BD.BatchDecoder(shape, len(prompts), ctx=32, seed=21)
+            rt = ref.generate(np.array(prompts), 1)
+            q.put((gathered, rt, ref.logits.cpu().numpy(), ops.device_error()))
+            ref.close()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(shape_args, seq, worker=None):
     import torch
     import torch.multiprocessing as mp
 
@@ -67,7 +98,7 @@ def _run(shape_args, seq):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, shape_args, seq, q)) for r in range(2)]
+    procs = [ctx.Process(target=worker or _worker, args=(r, 2, port, shape_args, seq, q)) for r in range(2)]
     for p in procs:
         p.start()
     try:
@@ -100,3 +131,20 @@ def test_two_rank_decode_matches_one_gpu(shape_args, cuda):
     top2 = np.sort(ref_logits)[-2:]
     if top2[1] - top2[0] > 2 * DECODE_TOL * np.abs(ref_logits).max():
         assert t0 == ref_tok
+
+
+def test_two_rank_batched_decode_matches_one_gpu(cuda):
+    # batch of 3 sequences, NCCL all-reduce after o / down and a max all-reduce of the argmax keys
+    shape_args = dict(n_layers=2, dim=512, n_heads=4, n_kv_heads=2, head_dim=128, ffn=1024, vocab=512)
+    prompts = [[3, 141, 59, 26], [7, 7, 400, 1], [500, 2, 33, 99]]
+    gathered, ref_tok, ref_logits, ref_err = _run(shape_args, prompts, worker=_batch_worker)
+    (t0, l0, e0), (t1, l1, e1) = gathered
+    assert e0 == 0 and e1 == 0 and ref_err == 0
+    np.testing.assert_array_equal(t0, t1)  # every rank writes the same tokens
+    logits = np.concatenate([l0, l1], axis=1)  # each rank holds its vocabulary slice
+    err = float(np.abs(logits - ref_logits).max() / np.abs(ref_logits).max())
+    assert err <= DECODE_TOL, err
+    for b in range(len(prompts)):
+        top2 = np.sort(ref_logits[b])[-2:]
+        if top2[1] - top2[0] > 2 * DECODE_TOL * np.abs(ref_logits[b]).max():
+            assert t0[b][-1] == ref_tok[b][-1]

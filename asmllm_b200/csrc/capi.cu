@@ -1597,6 +1597,7 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (strcmp(name, "tma") == 0) return g_opt_tma.exchange(value ? 1 : 0);
   if (strcmp(name, "pdl") == 0) return g_opt_pdl.exchange(value ? 1 : 0);
   if (strcmp(name, "gemm_splits") == 0) return g_opt_gemm_splits.exchange(value < 0 ? 0 : value);
+  if (strcmp(name, "image_min_k") == 0) return g_opt_image_min_k.exchange(value < 0 ? 0 : value);
   set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
   return -1;
 }

@@ -176,6 +176,7 @@ cudaError_t launch_rows_advance(const long long* keys, int rows, int32_t* tokens
 
 extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
 extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch
+extern std::atomic<int> g_opt_image_min_k;  // fp32-x matvecs with K >= this quantize x in a pre-pass (0: never)
 extern std::atomic<int> g_opt_gemm_splits;  // batched product: 0 = automatic K split, else exactly this many
 
 }  // namespace asmllm

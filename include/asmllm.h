@@ -495,6 +495,9 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * (-1 for an unknown name).  "tma": 1 = Q8_0-activation matvecs use the
  * bulk-copy pipeline kernel where the shape allows (default), 0 = the
  * register-streaming kernels.  "pdl": programmatic dependent launch on/off.
+ * "image_min_k": Q8_0-activation matvecs given fp32 x with K >= this value
+ * quantize x in a separate pre-pass kernel into stream-ordered scratch
+ * instead of in every CTA (default 8192; 0 = always in the CTAs).
  * "gemm_splits": 0 = the batched product picks its K split (default),
  * S >= 1 = exactly S ranges (clamped to [1, 8] and to the number of 128-byte
  * weight stages).  Results are identical either way up to fp32 summation

@@ -420,3 +420,24 @@ def test_q5_rejects_bad_arguments(cuda):
     assert rc == native.ASM_E_INVALID and "aligned" in native.last_error()[1]
     rc = L.asm_matmul_q5_async(ql.data_ptr(), ql.data_ptr(), x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 33, None)
     assert rc == native.ASM_E_INVALID and "K=33" in native.last_error()[1]
+
+
+@pytest.mark.parametrize("fmt", [FMT_Q4_0, FMT_Q8_0])
+def test_long_k_prepass_equals_fused_prologue(cuda, fmt):
+    # K >= "image_min_k": x is quantized once by a pre-pass kernel instead of in every CTA;
+    # the image bytes are the same, so y is bit-identical
+    torch = cuda
+    M, K = 300, 11008
+    w, s = (synth.q4_0_weights if fmt == FMT_Q4_0 else synth.q8_0_weights)(M, K, seed=17)
+    dw, ds = torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda().half()
+    x = torch.from_numpy(synth.activation(K, seed=18)).cuda()
+    prev = ops.set_option("image_min_k", 0)
+    try:
+        a = ops.matvec(fmt, dw, ds, x)
+        ops.set_option("image_min_k", 8192)
+        b = ops.matvec(fmt, dw, ds, x)
+    finally:
+        ops.set_option("image_min_k", prev)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert ops.device_error() == 0

@@ -361,7 +361,12 @@ def main():
         ms = float(t.item())
     total_bytes = step_bytes * K_steps * world
     value = total_bytes / (ms / 1e3) / 1e9
-    launches = len(SHAPES) * K_steps * (2 if args.mode == "image" else 1)
+    # kernels per matvec: the image pre-pass + the matvec in "image" mode; in "fused"
+    # mode the library itself runs the pre-pass for K >= its "image_min_k" option
+    image_min_k = ops.set_option("image_min_k", 8192)
+    ops.set_option("image_min_k", image_min_k)
+    launches = K_steps * sum(2 if args.mode == "image" or (image_min_k and K >= image_min_k) else 1
+                             for _, K in SHAPES)
     # The matvec is the dominant kernel; per-launch figures are per matvec
     # (its quantize pre-pass, when separate, is counted inside the time).
     per_launch_ms = ms / (len(SHAPES) * K_steps)
@@ -697,7 +702,8 @@ def main():
             "l2": f"rotating {COPIES} weight copies, {COPIES * step_bytes / 1e6:.0f} MB working set > 126 MB L2",
             "launch": "CUDA graph replay of %d steps (%d matvecs), PDL between kernels" % (G, G * len(SHAPES)),
             "quantize": "separate activation-image kernel per matvec" if args.mode == "image"
-                        else "inside each matvec kernel (fused)",
+                        else (f"inside each matvec kernel; the library's own pre-pass kernel for K >= {image_min_k}"
+                              if image_min_k else "inside each matvec kernel (fused)"),
         },
         "roofline": {
             "bound": "hbm",

@@ -103,23 +103,35 @@ template <int BN>
 struct Cfg {
   static constexpr int kBTile = BN * 64;
   static constexpr int kBEntry = kBTile + BN * 4;  // B tile | xd[BN]
+  // A tiles in tensor memory (written by the expanders with tcgen05.st, read
+  // by the MMA from there) where the accumulators leave room: half the
+  // shared-memory traffic per block of the shared-memory A path.
+  static constexpr bool kTA = BN <= 64;
   static constexpr int kG = BN >= 128 ? 1 : BN >= 64 ? 2 : 4;  // blocks per group
-  static constexpr int kR = BN >= 128 ? 4 : 3;                   // groups in flight
+  static constexpr int kR = BN >= 128 ? 4 : BN >= 64 ? 3 : BN >= 32 ? 2 : 4;  // groups in flight
   // warps 2 .. 13: expanders then epilogue.  Narrow tiles (decode batches) are
   // bound by the weight expansion, wide ones by the epilogue.
   static constexpr int kXW = BN >= 64 ? 4 : 8;  // expander warps (8: two threads per row)
   static constexpr int kEW = 12 - kXW;           // epilogue warps (8: two column halves)
   static constexpr int kCols = BN * 4 / kEW;     // accumulator columns per epilogue thread
   static constexpr int kAccCols = kR * kG * BN;
-  static constexpr int kTmemCols = kAccCols <= 32 ? 32 : kAccCols <= 64 ? 64 : kAccCols <= 128 ? 128
-                                   : kAccCols <= 256 ? 256 : 512;
+  static constexpr int kACols = kTA ? kR * kG * 16 : 0;  // 32 fp16 per row and block = 16 columns
+  static constexpr int kCols32 = kAccCols + kACols;
+  static constexpr int kTmemCols = kCols32 <= 32 ? 32 : kCols32 <= 64 ? 64 : kCols32 <= 128 ? 128
+                                   : kCols32 <= 256 ? 256 : 512;
+  static constexpr int kSlotBytes = kTA ? kGM * 4 : kASlot;  // per block: [A tile] | wd[128]
+  static constexpr int kWdOff = kTA ? 0 : kATile;
   static constexpr int kAOff = kStages * kStageBytes;
-  static constexpr int kBOff = kAOff + kR * kG * kASlot;
-  static constexpr int kBarOff = kBOff + kR * kG * kBEntry;
-  static constexpr int kNBars = 2 * kStages + 3 * kR;
+  // The activation tiles have their own, deeper ring (kRB groups): the tile
+  // loader runs that far ahead of the tensor core, off the critical path.
+  static constexpr int kRB = kTA ? 6 : kR;
+  static constexpr int kBOff = kAOff + kR * kG * kSlotBytes;
+  static constexpr int kBarOff = kBOff + kRB * kG * kBEntry;
+  static constexpr int kNBars = 2 * kStages + 3 * kR + 2 * kRB;
   static constexpr int kSmem = kBarOff + kNBars * 8 + 16 + 1024;  // barriers, tmem word, abort; 1024-byte alignment
   static_assert(kGM * BN * 4 <= kStages * kStageBytes, "split-K partial tile must fit the raw ring");
-  static_assert(kAccCols <= 512, "tensor memory");
+  static_assert(kCols32 <= 512, "tensor memory");
+  static_assert(4 % kG == 0, "a group never straddles a raw stage (4 or 8 blocks)");
   static_assert(kSmem <= 227 * 1024, "shared memory");
 };
 
@@ -143,6 +155,33 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(IdescF16<BN>::value), "r"(accumulate)
       : "memory");
 }
+
+// A from tensor memory (lanes = rows, two fp16 per 32-bit column along K).
+template <int BN>
+__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(IdescF16<BN>::value), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, uint4 a, uint4 b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(a.x),
+               "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, uint4 a, uint4 b, uint4 c, uint4 d) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w), "r"(c.x), "r"(c.y), "r"(c.z),
+      "r"(c.w), "r"(d.x), "r"(d.y), "r"(d.z), "r"(d.w)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void umma_commit(uint32_t mbar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
@@ -260,7 +299,7 @@ __device__ __forceinline__ void epi_chunk(uint32_t taddr, unsigned long long* ac
 // block's accumulator, scaled in block order (the NEON combine order).  The
 // tensor-memory loads of several blocks go out together (one wait::ld), at
 // most 64 staging registers at a time (32 for wide rows).
-template <int BN, int G, int CH>
+template <int BN, int G, int CH, int SLOT, int WDOFF>
 __device__ __forceinline__ void epi_group(uint32_t taddr, int nblk, unsigned long long* acc2,
                                           const unsigned char* aslots, const unsigned char* bentries, int lrow,
                                           int col0) {
@@ -282,7 +321,7 @@ __device__ __forceinline__ void epi_group(uint32_t taddr, int nblk, unsigned lon
     for (int i = 0; i < BATCH; ++i) {
       const int l = l0 + i, b = l / NC, c = l % NC;
       if (l >= NL || b >= nblk) break;
-      const float wd = reinterpret_cast<const float*>(aslots + b * kASlot + kATile)[lrow];
+      const float wd = reinterpret_cast<const float*>(aslots + b * SLOT + WDOFF)[lrow];
       const unsigned long long wd2 = pack2(wd, wd);
       const float* xd = reinterpret_cast<const float*>(bentries + b * kBEntry + BN * 64) + col0 + c * LC;
       unsigned long long* a2 = acc2 + c * (LC / 2);
@@ -313,10 +352,12 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* raw_full = bars;
   uint64_t* raw_empty = raw_full + kStages;
-  uint64_t* in_full = raw_empty + kStages;  // a group's A tiles (expanders) and B entries (tile loader)
+  uint64_t* in_full = raw_empty + kStages;  // a group's A tiles and wd (expanders)
   uint64_t* mma_done = in_full + R;         // the group's MMAs completed (tcgen05.commit)
-  uint64_t* grp_done = mma_done + R;        // the epilogue finished the group: its slots may be reused
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(grp_done + R);
+  uint64_t* grp_done = mma_done + R;        // the epilogue finished the group: A slots and accumulators free
+  uint64_t* b_full = grp_done + R;          // a group's B entries landed (tile loader), ring of RB
+  uint64_t* b_done = b_full + C::kRB;       // the epilogue finished with a group's B entries (xd)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(b_done + C::kRB);
   volatile uint32_t* s_abort = s_tmem + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -341,9 +382,13 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       mbar_init(smem_u32(&raw_empty[i]), C::kXW);  // expander warps
     }
     for (int i = 0; i < R; ++i) {
-      mbar_init(smem_u32(&in_full[i]), C::kXW + 32);  // expander warps + the tile loader's lanes
+      mbar_init(smem_u32(&in_full[i]), C::kXW);  // expander warps
       mbar_init(smem_u32(&mma_done[i]), 1);
       mbar_init(smem_u32(&grp_done[i]), C::kEW);
+    }
+    for (int i = 0; i < C::kRB; ++i) {
+      mbar_init(smem_u32(&b_full[i]), 32);  // the tile loader's lanes (cp.async arrivals)
+      mbar_init(smem_u32(&b_done[i]), 1 + C::kEW);  // MMA commit + epilogue warps
     }
     *s_abort = 0u;
     fence_mbar_init();
@@ -392,24 +437,25 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     // ---------------- tile loader: activation tiles by LSU async copies (not the TMA
     // queue, where they would wait behind the weight stages' HBM latency) ----------------
     pdl_wait();  // the activation tiles come from the previous kernel
+    constexpr int RB = C::kRB;
     for (int g = 0; g < ng; ++g) {
-      const int r = g % R;
+      const int rb = g % RB;
       bool ok = true;
-      if (g >= R) ok = mbar_wait_bounded(smem_u32(&grp_done[r]), ((g / R) - 1) & 1);
+      if (g >= RB) ok = mbar_wait_bounded(smem_u32(&b_done[rb]), ((g / RB) - 1) & 1);
       if (__any_sync(0xFFFFFFFFu, !ok || *s_abort)) {  // one decision per warp
         if (!ok) fail();
         break;
       }
       for (int b = 0; b < G && g * G + b < jb; ++b) {
-        unsigned char* be = bring + (r * G + b) * C::kBEntry;
+        unsigned char* be = bring + (rb * G + b) * C::kBEntry;
         const size_t tb = (size_t)(b0 + g * G + b) * np + n0;  // the block's first token
         const unsigned char* st = tiles + tb * 64;
         const unsigned char* sx = tiles + (size_t)nb * np * 64 + tb * 4;
         for (int c = lane; c < C::kBTile / 16; c += 32) cp_async16(be + 16 * c, st + 16 * c);
         for (int c = lane; c < BN * 4 / 16; c += 32) cp_async16(be + C::kBTile + 16 * c, sx + 16 * c);
       }
-      // this lane's arrival on in_full happens when its copies have landed
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&in_full[r])) : "memory");
+      // this lane's arrival on b_full happens when its copies have landed
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&b_full[rb])) : "memory");
     }
     cp_async_wait_all();  // nothing in flight when the CTA moves on
   } else if (warp == 1) {
@@ -419,7 +465,9 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       int issued = 0;
       for (int g = 0; g < ng; ++g) {
         const int r = g % R;
+        const int rb = g % C::kRB;
         bool ok = mbar_wait_bounded(smem_u32(&in_full[r]), (g / R) & 1);
+        if (ok) ok = mbar_wait_bounded(smem_u32(&b_full[rb]), (g / C::kRB) & 1);
         if (ok && g >= R) ok = mbar_wait_bounded(smem_u32(&grp_done[r]), ((g / R) - 1) & 1);  // accumulators free
         if (!ok) {
           fail();
@@ -429,13 +477,20 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
         fence_proxy_async();  // the B entries were written by generic-proxy async copies
         tc_fence_after();
         for (int b = 0; b < G && g * G + b < jb; ++b) {
-          const uint64_t ad = umma_desc(smem_u32(aring + (r * G + b) * kASlot));
-          const uint64_t bd = umma_desc(smem_u32(bring + (r * G + b) * C::kBEntry));
+          const uint64_t bd = umma_desc(smem_u32(bring + (rb * G + b) * C::kBEntry));
           const uint32_t td = tmem + (uint32_t)((r * G + b) * BN);
-          umma_f16<BN>(td, ad, bd, 0u);
-          umma_f16<BN>(td, ad + (256 >> 4), bd + (256 >> 4), 1u);
+          if constexpr (C::kTA) {
+            const uint32_t ta = tmem + (uint32_t)(C::kAccCols + (r * G + b) * 16);
+            umma_f16_ta<BN>(td, ta, bd, 0u);
+            umma_f16_ta<BN>(td, ta + 8, bd + (256 >> 4), 1u);
+          } else {
+            const uint64_t ad = umma_desc(smem_u32(aring + (r * G + b) * C::kSlotBytes));
+            umma_f16<BN>(td, ad, bd, 0u);
+            umma_f16<BN>(td, ad + (256 >> 4), bd + (256 >> 4), 1u);
+          }
         }
         umma_commit(smem_u32(&mma_done[r]));
+        umma_commit(smem_u32(&b_done[rb]));
         issued = g + 1;
       }
       // the tensor core has finished everything issued before tensor memory is released
@@ -449,8 +504,8 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     // ---------------- expanders: one weight row per thread (two with 8 warps) ----------------
     constexpr int kParts = C::kXW / 4;  // threads per row
     constexpr int kCh = 4 / kParts;     // 16-byte chunks of the A row each writes
-    const int tx = tid - 64;
-    const int t = tx & 127, part = tx >> 7;
+    // rows of this warp = its tensor-memory lane quarter (the A tiles may live there)
+    const int t = 32 * (warp & 3) + lane, part = (warp - 2) >> 2;
     const int row = m0 + t;
     const bool row_ok = row < M;
     const __half* srow = scales + (size_t)(row_ok ? row : 0) * nb;
@@ -462,23 +517,50 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
         if (!ok) fail();
         break;
       }
-      bool stop = false;
-      for (int b = 0; b < G && g * G + b < jb; ++b) {
-        const int j = g * G + b;
-        const int s = j / KB, bi = j % KB, rs = s % kStages;
-        if (bi == 0) {
-          const bool okr = mbar_wait_bounded(smem_u32(&raw_full[rs]), (s / kStages) & 1);
-          if (__any_sync(0xFFFFFFFFu, !okr || *s_abort)) {
-            if (!okr) fail();
-            stop = true;
-            break;
-          }
+      if (C::kTA) tc_fence_after();  // after the MMAs that read this group's A columns last time
+      // a group never straddles a raw stage (G divides KB): one wait, then the
+      // group's blocks unrolled so their loads and arithmetic interleave
+      const int j0 = g * G, nblk = min(G, jb - j0);
+      const int s = j0 / KB, bi0 = j0 % KB, rs = s % kStages;
+      if (bi0 == 0) {
+        const bool okr = mbar_wait_bounded(smem_u32(&raw_full[rs]), (s / kStages) & 1);
+        if (__any_sync(0xFFFFFFFFu, !okr || *s_abort)) {
+          if (!okr) fail();
+          break;
         }
-        unsigned char* slot = aring + (r * G + b) * kASlot;
-        const unsigned char* stage = raw + rs * kStageBytes;
-        const unsigned char* rrow = stage + t * 128;
+      }
+      const unsigned char* stage = raw + rs * kStageBytes;
+      const unsigned char* rrow = stage + t * 128;
+#pragma unroll
+      for (int b = 0; b < G; ++b) {
+        if (b >= nblk) break;
+        const int j = j0 + b, bi = bi0 + b;
+        unsigned char* slot = aring + (r * G + b) * C::kSlotBytes;
         unsigned char* adst = slot + (t >> 3) * 512 + (t & 7) * 16 + part * kCh * 128;
-        if (kParts == 1) {
+        const uint32_t ta = tmem + ((uint32_t)(32 * (warp & 3)) << 16) +
+                            (uint32_t)(C::kAccCols + (r * G + b) * 16 + part * kCh * 4);
+        if (C::kTA) {  // this thread's chunks as 32-bit tensor-memory columns of its row
+          if (kParts == 1) {
+            if (FMT == kFmtQ4_0) {
+              const uint4 q = lds128(rrow + ((bi ^ (t & 7)) << 4));
+              tmem_st16(ta, q4_chunk(q.x), q4_chunk(q.y), q4_chunk(q.z), q4_chunk(q.w));
+            } else {
+              const uint4 lo = lds128(rrow + (((2 * bi) ^ (t & 7)) << 4));
+              const uint4 hi = lds128(rrow + (((2 * bi + 1) ^ (t & 7)) << 4));
+              tmem_st16(ta, tiles_i8_chunk(lo.x, hi.x), tiles_i8_chunk(lo.y, hi.y), tiles_i8_chunk(lo.z, hi.z),
+                        tiles_i8_chunk(lo.w, hi.w));
+            }
+          } else {
+            if (FMT == kFmtQ4_0) {
+              const uint2 q = *reinterpret_cast<const uint2*>(rrow + ((bi ^ (t & 7)) << 4) + part * 8);
+              tmem_st8(ta, q4_chunk(q.x), q4_chunk(q.y));
+            } else {
+              const uint2 lo = *reinterpret_cast<const uint2*>(rrow + (((2 * bi) ^ (t & 7)) << 4) + part * 8);
+              const uint2 hi = *reinterpret_cast<const uint2*>(rrow + (((2 * bi + 1) ^ (t & 7)) << 4) + part * 8);
+              tmem_st8(ta, tiles_i8_chunk(lo.x, hi.x), tiles_i8_chunk(lo.y, hi.y));
+            }
+          }
+        } else if (kParts == 1) {
           if (FMT == kFmtQ4_0) {
             const uint4 q = lds128(rrow + ((bi ^ (t & 7)) << 4));
             *reinterpret_cast<uint4*>(adst) = q4_chunk(q.x);
@@ -512,14 +594,18 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
         } else {
           wd = row_ok ? __half2float(srow[b0 + j]) : 0.0f;
         }
-        if (part == 0) reinterpret_cast<float*>(slot + kATile)[t] = wd;
-        if (bi == KB - 1 || j == jb - 1) {  // this warp is done with the raw stage
-          __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&raw_empty[rs]));
-        }
+        if (part == 0) reinterpret_cast<float*>(slot + C::kWdOff)[t] = wd;
       }
-      if (stop) break;
-      fence_proxy_async();  // generic-proxy writes become visible to the tensor core
+      if (bi0 + nblk == KB || j0 + nblk == jb) {  // this warp is done with the raw stage
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&raw_empty[rs]));
+      }
+      if (C::kTA) {
+        tmem_wait_st();  // this thread's tensor-memory stores are done
+        tc_fence_before();
+      } else {
+        fence_proxy_async();  // generic-proxy writes become visible to the tensor core
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&in_full[r]));
     }
@@ -535,19 +621,25 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     for (int g = 0; g < ng; ++g) {
       const int r = g % R;
       bool ok = mbar_wait_bounded(smem_u32(&mma_done[r]), (g / R) & 1);
-      // (the MMA saw in_full complete; this wait gives this warp the expanders' and copies' writes)
+      // (the MMA saw these complete; the waits give this warp the expanders' and copies' writes)
+      const int rb = g % C::kRB;
       if (ok) ok = mbar_wait_bounded(smem_u32(&in_full[r]), (g / R) & 1);
+      if (ok) ok = mbar_wait_bounded(smem_u32(&b_full[rb]), (g / C::kRB) & 1);
       if (__any_sync(0xFFFFFFFFu, !ok || *s_abort)) {  // one decision per warp
         if (!ok) fail();
         break;
       }
       tc_fence_after();
       const int nblk = min(G, jb - g * G);
-      epi_group<BN, G, C::kCols>(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(r * G * BN + col0), nblk, acc2,
-                       aring + r * G * kASlot, bring + r * G * C::kBEntry, lrow, col0);
+      epi_group<BN, G, C::kCols, C::kSlotBytes, C::kWdOff>(
+          tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(r * G * BN + col0), nblk, acc2, aring + r * G * C::kSlotBytes,
+          bring + rb * G * C::kBEntry, lrow, col0);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&grp_done[r]));
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&grp_done[r]));
+        mbar_arrive(smem_u32(&b_done[rb]));
+      }
     }
     if (splits == 1) {
       if (row < M) {

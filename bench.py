@@ -13,11 +13,20 @@ streams its weights from HBM.  Synthetic seeded data, no model file.
   e2e     = the same metric through the reference-facing C ABI
             (asm_matmul_q4, host buffers: pinned x in, pinned y out, weights
             registered once), host copies inside the timed region.
-  roofline, cpu_baseline, clocks: see DESIGN.md.
+  roofline = the dominant kernel (the matvec) against the measured copy
+            bandwidth of MEASURED_PEAKS.json; traffic from the committed ncu
+            summary under profiles/.
+  cpu_baseline = the C restatement of the reference's CPU matvec (oracle/),
+            all host threads, a bounded sample of the same sweep.
+  clocks  = nvidia-smi samples taken during the timed region.
+Further sections of the line: the 7B batch-1 decode (both engines), the
+tensor-core batched product at N = 8 / 64 / 512 tokens, and the
+Llama-2-70B-shape decode at batch 1 and 32, tensor-parallel over the N GPUs.
 
 Launch: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
-(N > 1 under torch.distributed.run: one rank per GPU, weak scaling, no
-data-path collective; timing barrier and max-over-ranks use NCCL.)
+(N > 1 under torch.distributed.run: one rank per GPU; the matvec sweep and
+the 7B decode run as replicas, the 70B decode is tensor-parallel; timing
+barrier and max-over-ranks use NCCL.)
 """
 from __future__ import annotations
 

@@ -62,20 +62,26 @@ int cuda_error(cudaError_t e, const char* what) {
 enum PtrKind { kHostPageable = 0, kHostPinned = 1, kDevice = 2 };
 
 std::mutex g_kind_mu;
-std::unordered_map<const void*, std::pair<int, int>> g_kind_cache;  // ptr -> (kind, device)
+struct KindEntry {
+  int kind, dev;
+  const void* dptr;  // pinned host memory: its device-visible address (null if not mapped)
+};
+std::unordered_map<const void*, KindEntry> g_kind_cache;
 
-PtrKind classify(const void* p, int* device) {
+PtrKind classify(const void* p, int* device, const void** mapped = nullptr) {
   {
     std::lock_guard<std::mutex> lk(g_kind_mu);
     auto it = g_kind_cache.find(p);
     if (it != g_kind_cache.end()) {
-      if (device) *device = it->second.second;
-      return (PtrKind)it->second.first;
+      if (device) *device = it->second.dev;
+      if (mapped) *mapped = it->second.dptr;
+      return (PtrKind)it->second.kind;
     }
   }
   cudaPointerAttributes a;
   PtrKind k = kHostPageable;
   int dev = -1;
+  const void* dptr = nullptr;
   cudaError_t e = cudaPointerGetAttributes(&a, p);
   if (e != cudaSuccess) {
     cudaGetLastError();  // unknown pointer: plain host memory
@@ -85,14 +91,16 @@ PtrKind classify(const void* p, int* device) {
   } else if (a.type == cudaMemoryTypeHost) {
     k = kHostPinned;
     dev = a.device;
+    dptr = a.devicePointer;
   }
   // Pageable host memory is not cached: a later cudaHostRegister may pin it.
   if (k != kHostPageable) {
     std::lock_guard<std::mutex> lk(g_kind_mu);
     if (g_kind_cache.size() > 8192) g_kind_cache.clear();
-    g_kind_cache[p] = {(int)k, dev};
+    g_kind_cache[p] = {(int)k, dev, dptr};
   }
   if (device) *device = dev;
+  if (mapped) *mapped = dptr;
   return k;
 }
 
@@ -322,17 +330,31 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
   a.weights_static = K > 0 && ((a.w != (const void*)w) ||
                                (is_static(w, weight_bytes(fmt, M, K)) &&
                                 is_static(s, (size_t)M * (K / 32) * sizeof(float))));
+  // Pinned host x and y are used in place (mapped host memory) where only one
+  // kernel touches them: the activation pre-pass reads x once, the matvec
+  // writes y once -- no staging copies on those calls.
+  const bool image_path = !fp32_act && K > 0 && !sync_fused();
   if (K > 0) {
     const void* dx = nullptr;
-    if (device_in(st, dev, x, (size_t)K * sizeof(float), 2, &dx, name)) return;
+    const void* xmap = nullptr;
+    int xdev = -1;
+    if (image_path && classify(x, &xdev, &xmap) == kHostPinned && xdev == dev && xmap && (uintptr_t)xmap % 16 == 0) {
+      dx = xmap;
+    } else if (device_in(st, dev, x, (size_t)K * sizeof(float), 2, &dx, name)) {
+      return;
+    }
     a.x = static_cast<const float*>(dx);
     if (check_align(name, a.w, a.scales, a.scales_f16 ? 2 : 4, a.x)) return;
   }
 
   int ydev = -1;
-  const PtrKind yk = classify(y, &ydev);
+  const void* ymap = nullptr;
+  PtrKind yk = classify(y, &ydev, &ymap);
   const size_t ybytes = (size_t)M * sizeof(float);
-  if (yk == kDevice) {
+  if (yk == kHostPinned && ydev == dev && ymap && (uintptr_t)ymap % 4 == 0) {
+    a.y = static_cast<float*>(const_cast<void*>(ymap));
+    yk = kDevice;  // written in place: no copy back
+  } else if (yk == kDevice) {
     if (ydev != dev) {
       set_error(ASM_E_INVALID, "%s: y lives on device %d but the current device is %d", name, ydev, dev);
       return;
@@ -344,7 +366,7 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
   }
 
   cudaError_t e = cudaSuccess;
-  if (!fp32_act && K > 0 && !sync_fused()) {
+  if (image_path) {
     // Quantize x once into the device's activation image, then the matvec reads it.
     if (ensure_dev(st.image, act_image_bytes(K / 32))) return;
     e = launch_act_image(a.x, st.image.p, 1, K, st.stream, a.w, weight_bytes(fmt, M, K), a.scales,

@@ -76,6 +76,10 @@
 #include "pipeline.cuh"
 #include "tiles.cuh"
 
+#ifndef ASMLLM_GEMM_EW
+#define ASMLLM_GEMM_EW (BN >= 64 ? 8 : 4)
+#endif
+
 namespace asmllm {
 
 std::atomic<int> g_opt_gemm_splits{0};
@@ -89,7 +93,6 @@ constexpr int kScaleBytes = kGM * 16;            // the stage's fp16 scales: 128
 constexpr int kStageBytes = kRawBytes + kScaleBytes;  // a multiple of 1024 (the swizzle period)
 constexpr int kATile = kGM * 64;                 // one block of A: 128 rows x 32 fp16
 constexpr int kASlot = kATile + kGM * 4;         // A tile | wd[128]
-constexpr int kThreads = 480;                    // 15 warps
 constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 in both halves
 constexpr uint32_t kSub8 = 0x64086408u;   // 1032.0: (1024 + nibble) - 1032 = nibble - 8
 static_assert(kStageBytes % 1024 == 0, "raw stages keep the 1024-byte swizzle alignment");
@@ -112,7 +115,9 @@ struct Cfg {
   // warps 2 .. 13: expanders then epilogue.  Narrow tiles (decode batches) are
   // bound by the weight expansion, wide ones by the epilogue.
   static constexpr int kXW = BN >= 64 ? 4 : 8;  // expander warps (8: two threads per row)
-  static constexpr int kEW = 12 - kXW;           // epilogue warps (8: two column halves)
+  static constexpr int kEW = ASMLLM_GEMM_EW;      // epilogue warps (8: two column halves)
+  static constexpr int kLoader = 2 + kXW + kEW;  // the tile loader's warp (the last)
+  static constexpr int kThreads = (kLoader + 1) * 32;
   static constexpr int kCols = BN * 4 / kEW;     // accumulator columns per epilogue thread
   static constexpr int kAccCols = kR * kG * BN;
   static constexpr int kACols = kTA ? kR * kG * 16 : 0;  // 32 fp16 per row and block = 16 columns
@@ -336,7 +341,7 @@ __device__ __forceinline__ void epi_group(uint32_t taddr, int nblk, unsigned lon
 }
 
 template <int FMT, int BN, bool STMA>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<BN>::kThreads, 1)
 q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __half* __restrict__ scales, const unsigned char* __restrict__ tiles, int np,
                   float* __restrict__ y, int M, int N, int nb, int splits, int pre, unsigned* __restrict__ err) {
@@ -433,7 +438,7 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     } else {
       pdl_wait();
     }
-  } else if (warp == 14) {
+  } else if (warp == C::kLoader) {
     // ---------------- tile loader: activation tiles by LSU async copies (not the TMA
     // queue, where they would wait behind the weight stages' HBM latency) ----------------
     pdl_wait();  // the activation tiles come from the previous kernel
@@ -674,7 +679,7 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       const int E = kGM * BN;
       const int e0 = (int)((long long)z * E / splits), e1 = (int)((long long)(z + 1) * E / splits);
       const uint32_t pbase = smem_u32(raw);
-      for (int e = e0 + tid; e < e1; e += kThreads) {
+      for (int e = e0 + tid; e < e1; e += C::kThreads) {
         const int n = e / kGM, rr = e % kGM;
         float s = 0.0f;
         for (int src = 0; src < splits; ++src) s += ld_cluster_f32(pbase + 4u * (uint32_t)e, (uint32_t)src);
@@ -763,7 +768,7 @@ cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& smap, const __
   const int splits = (int)S;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((M + kGM - 1) / kGM), (unsigned)((N + BN - 1) / BN), (unsigned)splits);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];

@@ -441,3 +441,17 @@ def test_long_k_prepass_equals_fused_prologue(cuda, fmt):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("M,K", [(1000, 4096), (4096, 11008)])
+def test_sync_abi_pinned_buffers_used_in_place(cuda, M, K):
+    # pinned host x / y go to the kernels as mapped host memory (no staging
+    # copies); the result equals the staged (pageable) path bit for bit
+    torch = cuda
+    w, s = synth.q4_0_weights(M, K, seed=21)
+    x = synth.activation(K, seed=22)
+    hx = torch.from_numpy(x.copy()).pin_memory()
+    hy = torch.zeros(M, dtype=torch.float32).pin_memory()
+    native.lib().asm_matmul_q4(w.ctypes.data, s.ctypes.data, hx.data_ptr(), hy.data_ptr(), M, K)
+    native.check()
+    np.testing.assert_array_equal(hy.numpy(), ops.matmul_q4(w, s, x))

@@ -119,7 +119,7 @@ struct DeviceState {
   Buf dev[5];   // device staging: weights, scales, x, y, Q5_0 high bits
   Buf host[2];  // pinned host staging: x, y
   Buf image;    // Q8_0 activation image of the synchronous calls
-  unsigned* err_word = nullptr;  // pinned copy of the device error word
+  unsigned* err_word = nullptr;  // mapped pinned word the kernels' error reports also reach
   std::mutex mu;
 };
 
@@ -138,9 +138,11 @@ int get_state(DeviceState** out, int* dev_out) {
   if (!st.init) {
     e = cudaStreamCreateWithFlags(&st.stream, cudaStreamDefault);
     if (e != cudaSuccess) return cuda_error(e, "cudaStreamCreate");
-    e = cudaHostAlloc(&st.err_word, sizeof(unsigned), cudaHostAllocDefault);
+    e = cudaHostAlloc(&st.err_word, sizeof(unsigned), cudaHostAllocMapped);
     if (e != cudaSuccess) return cuda_error(e, "cudaHostAlloc (error word)");
     *st.err_word = 0;
+    e = set_device_error_mirror(st.err_word);
+    if (e != cudaSuccess) return cuda_error(e, "device error mirror");
     st.init = true;
   }
   *out = &st;
@@ -283,6 +285,11 @@ int device_in(DeviceState& st, int dev, const void* p, size_t bytes, int slot, c
 
 // Synchronous Q8_0-activation calls quantize x with a separate pre-pass into a
 // per-device image (default) or inside the matvec (ASMLLM_SYNC_FUSED=1).
+// Bit 0: pinned host x mapped into the device and read in place by the
+// activation pre-pass; bit 1: pinned host y written in place by the matvec.
+// A cleared bit stages that buffer with a copy instead.
+std::atomic<int> g_opt_sync_map{3};
+
 bool sync_fused() {
   static const bool v = [] {
     const char* e = getenv("ASMLLM_SYNC_FUSED");
@@ -338,7 +345,8 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
     const void* dx = nullptr;
     const void* xmap = nullptr;
     int xdev = -1;
-    if (image_path && classify(x, &xdev, &xmap) == kHostPinned && xdev == dev && xmap && (uintptr_t)xmap % 16 == 0) {
+    if (image_path && (g_opt_sync_map.load() & 1) && classify(x, &xdev, &xmap) == kHostPinned && xdev == dev &&
+        xmap && (uintptr_t)xmap % 16 == 0) {
       dx = xmap;
     } else if (device_in(st, dev, x, (size_t)K * sizeof(float), 2, &dx, name)) {
       return;
@@ -351,7 +359,7 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
   const void* ymap = nullptr;
   PtrKind yk = classify(y, &ydev, &ymap);
   const size_t ybytes = (size_t)M * sizeof(float);
-  if (yk == kHostPinned && ydev == dev && ymap && (uintptr_t)ymap % 4 == 0) {
+  if (yk == kHostPinned && (g_opt_sync_map.load() & 2) && ydev == dev && ymap && (uintptr_t)ymap % 4 == 0) {
     a.y = static_cast<float*>(const_cast<void*>(ymap));
     yk = kDevice;  // written in place: no copy back
   } else if (yk == kDevice) {
@@ -390,18 +398,26 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
     cuda_error(e, "cudaMemcpyAsync D2H");
     return;
   }
-  e = read_device_error_async(st.err_word, st.stream);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st.stream);
+  e = cudaStreamSynchronize(st.stream);
   if (e != cudaSuccess) {
     cuda_error(e, name);
     return;
   }
   if (*st.err_word) {
-    unsigned v = 0;
-    read_device_error(&v, true);
+    // A kernel reported an error; the device word holds all of its bits
+    // (zero if the caller already consumed them with asm_device_error).
     *st.err_word = 0;
-    set_error(ASM_E_CUDA, "%s: a device-side bounded wait timed out (error bits 0x%x); y is not valid", name, v);
-    return;
+    unsigned v = 0;
+    e = read_device_error(&v, true);
+    if (e != cudaSuccess) {
+      cuda_error(e, name);
+      return;
+    }
+    if (v) {
+      set_error(ASM_E_CUDA, "%s: a kernel reported device error bits 0x%x (see asm_device_error); y is not valid",
+                name, v);
+      return;
+    }
   }
   if (ybounce) memcpy(y, ybounce, ybytes);
 }
@@ -820,10 +836,12 @@ ASMLLM_API void asm_threadpool_shutdown(void) {
     st.image = Buf();
     cudaStreamDestroy(st.stream);
     st.stream = nullptr;
+    set_device_error_mirror(nullptr);
     if (st.err_word) cudaFreeHost(st.err_word);
     st.err_word = nullptr;
     st.init = false;
   }
+  scratch_trim();
   cudaSetDevice(cur);
   {
     std::lock_guard<std::mutex> lk(g_kind_mu);
@@ -1620,6 +1638,7 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (strcmp(name, "pdl") == 0) return g_opt_pdl.exchange(value ? 1 : 0);
   if (strcmp(name, "gemm_splits") == 0) return g_opt_gemm_splits.exchange(value < 0 ? 0 : value);
   if (strcmp(name, "image_min_k") == 0) return g_opt_image_min_k.exchange(value < 0 ? 0 : value);
+  if (strcmp(name, "sync_map") == 0) return g_opt_sync_map.exchange(value & 3);
   set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
   return -1;
 }

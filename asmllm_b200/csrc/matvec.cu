@@ -503,9 +503,56 @@ std::atomic<int> g_opt_pdl{[] {
   return (e && e[0] == '0') ? 0 : 1;
 }()};
 
+// Stream-ordered scratch (activation images and tiles the library makes for
+// one call).  Outside stream capture it comes from a per-device pool that
+// keeps its memory across synchronizations: the device's default pool
+// returns freed memory to the driver at every synchronize, and mapping it
+// again cost ~0.5 ms per call when the caller synchronized between calls.
+// Inside capture it is a graph allocation (cudaMallocAsync).
 namespace {
-
+std::mutex g_pool_mu;
+cudaMemPool_t g_pool[64] = {};
 }  // namespace
+
+cudaError_t scratch_alloc_async(void** p, size_t bytes, cudaStream_t stream) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    cs = cudaStreamCaptureStatusActive;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (cs != cudaStreamCaptureStatusNone || dev < 0 || dev >= 64) return cudaMallocAsync(p, bytes, stream);
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_pool_mu);
+    if (!g_pool[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.handleTypes = cudaMemHandleTypeNone;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      e = cudaMemPoolCreate(&g_pool[dev], &props);
+      if (e != cudaSuccess) {
+        g_pool[dev] = nullptr;
+        return e;
+      }
+      unsigned long long keep = ~0ull;
+      cudaMemPoolSetAttribute(g_pool[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pool = g_pool[dev];
+  }
+  return cudaMallocFromPoolAsync(p, bytes, pool, stream);
+}
+
+cudaError_t scratch_free_async(void* p, cudaStream_t stream) { return cudaFreeAsync(p, stream); }
+
+void scratch_trim() {
+  std::lock_guard<std::mutex> lk(g_pool_mu);
+  for (auto& pool : g_pool)
+    if (pool) cudaMemPoolTrimTo(pool, 0);
+}
 
 // Runtime switches (asm_set_option): bulk-copy pipeline kernel for the Q8_0
 // families (else the register-streaming kernels) and programmatic dependent
@@ -689,7 +736,7 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     const int min_k = g_opt_image_min_k.load();
     if (a.image == nullptr && a.isums == nullptr && min_k > 0 && a.K >= min_k) {
       void* img = nullptr;
-      e = cudaMallocAsync(&img, act_image_bytes(nb), stream);
+      e = scratch_alloc_async(&img, act_image_bytes(nb), stream);
       if (e != cudaSuccess) return e;
       const size_t wbytes = (size_t)a.M * nb * (a.fmt == kFmtQ4_0 ? 16 : 32);
       const size_t sbytes = (size_t)a.M * nb * (a.scales_f16 ? 2 : 4);
@@ -699,7 +746,7 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
         b.image = img;
         e = launch_tma_matvec(b, di.sms, di.smem_optin, stream, g_opt_pdl.load() != 0);
       }
-      const cudaError_t f = cudaFreeAsync(img, stream);
+      const cudaError_t f = scratch_free_async(img, stream);
       return e != cudaSuccess ? e : f;
     }
     return launch_tma_matvec(a, di.sms, di.smem_optin, stream, g_opt_pdl.load() != 0);

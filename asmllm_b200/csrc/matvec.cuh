@@ -121,7 +121,15 @@ cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cuda
 // Reads (and optionally clears) the device error word the kernels set when a
 // bounded wait gives up (bit 0: a shared-memory ring barrier timed out).
 cudaError_t read_device_error(unsigned* out, bool clear);
-cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream);
+// Points the kernels' error reports on the current device at a mapped pinned
+// host word as well (nullptr: none), so a synchronous caller sees them
+// without a copy.
+cudaError_t set_device_error_mirror(unsigned* host_mapped);
+// Stream-ordered scratch for one call (a per-device pool that keeps its
+// memory; a graph allocation under stream capture), and trimming the pools.
+cudaError_t scratch_alloc_async(void** p, size_t bytes, cudaStream_t stream);
+cudaError_t scratch_free_async(void* p, cudaStream_t stream);
+void scratch_trim();
 // Device address of the error word on the current device (for kernels in
 // other translation units); nullptr if it cannot be looked up.
 unsigned* device_error_word();

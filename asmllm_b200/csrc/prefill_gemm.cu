@@ -854,15 +854,15 @@ cudaError_t launch_act_tiles_from_image(const void* images, size_t img_stride, i
                             (int)N, nb, np, static_cast<unsigned char*>(tiles));
 }
 
-// Images -> tiles (stream-ordered scratch from the device's default pool) -> product.
+// Images -> tiles (stream-ordered scratch) -> product.
 cudaError_t launch_q8act_gemm(int fmt, const void* w, const void* scales_f16, const void* images, size_t img_stride,
                               float* y, int64_t M, int64_t N, int64_t K, bool weights_static, cudaStream_t stream) {
   void* tiles = nullptr;
-  cudaError_t e = cudaMallocAsync(&tiles, act_tiles_bytes(N, K), stream);
+  cudaError_t e = scratch_alloc_async(&tiles, act_tiles_bytes(N, K), stream);
   if (e != cudaSuccess) return e;
   e = launch_act_tiles_from_image(images, img_stride, N, K, tiles, stream);
   if (e == cudaSuccess) e = launch_q8act_gemm_tiles(fmt, w, scales_f16, tiles, y, M, N, K, weights_static, stream);
-  const cudaError_t f = cudaFreeAsync(tiles, stream);
+  const cudaError_t f = scratch_free_async(tiles, stream);
   return e != cudaSuccess ? e : f;
 }
 

@@ -43,6 +43,17 @@
 namespace asmllm {
 
 __device__ unsigned int g_device_error;
+// Optional mapped pinned host word that also receives the error bits (set by
+// the synchronous entries: they test it after their stream synchronize
+// instead of copying g_device_error back).  A plain store: concurrent
+// reporters may overwrite each other's bits there, g_device_error keeps them all.
+__device__ unsigned int* g_error_mirror;
+
+__device__ __forceinline__ void raise_device_error(unsigned bits) {
+  atomicOr(&g_device_error, bits);
+  unsigned int* m = g_error_mirror;
+  if (m) *reinterpret_cast<volatile unsigned int*>(m) = bits;
+}
 
 namespace {
 
@@ -75,7 +86,7 @@ __device__ __forceinline__ unsigned xchg_wait(const unsigned long long* p, unsig
     v = ld_volatile_u64(p);
     if (clock64() - t0 > kWaitCycles) {
       ok = false;
-      atomicOr(&g_device_error, kErrXchgTimeout);
+      raise_device_error(kErrXchgTimeout);
       return 0u;
     }
   } while ((unsigned)(v >> 32) != seq);
@@ -121,7 +132,7 @@ __device__ void argmax_arrive(const MvFuse& fz, unsigned nctas, unsigned seq) {
   if (p >= 0 && p + 1 < fz.max_tokens) {
     if (p + 1 >= fz.n_prompt) fz.tokens[p + 1] = idx;  // prompt positions keep their ids
   } else {
-    atomicOr(&g_device_error, kErrDecodeRange);
+    raise_device_error(kErrDecodeRange);
   }
   *pos = p + 1;
   atomicExch(fz.done, 0u);
@@ -134,7 +145,7 @@ __device__ __forceinline__ const float* prologue_source(const MvFuse& fz, const 
   const int p = __ldcg(fz.pos);
   int tok = (p >= 0 && p < fz.max_tokens) ? __ldcg(fz.tokens + p) : -1;
   if (tok < 0 || tok >= fz.vocab) {
-    if (threadIdx.x == 0) atomicOr(&g_device_error, kErrDecodeRange);
+    if (threadIdx.x == 0) raise_device_error(kErrDecodeRange);
     tok = 0;
   }
   return fz.embed + (size_t)tok * K;
@@ -225,7 +236,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
         const int g = s % NWG, k = s / NWG;  // k-th stage of warpgroup g
         const int slot = g * NSW + k % NSW, round = k / NSW;
         if (round > 0 && !mbar_wait_bounded(smem_u32(&bars[NS + slot]), (round - 1) & 1)) {
-          atomicOr(&g_device_error, 1u);
+          raise_device_error(kErrRingTimeout);
           *s_abort = 1;
           break;
         }
@@ -348,7 +359,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   for (int s = wg, k = 0; s < S; s += NWG, ++k) {
     const int slot = wg * NSW + k % NSW;
     const bool ok = mbar_wait_bounded(smem_u32(&bars[slot]), (k / NSW) & 1);
-    if (!ok) atomicOr(&g_device_error, 1u);
+    if (!ok) raise_device_error(kErrRingTimeout);
     const int row0 = r0 + s * R;
     const int nrows = min(R, r1 - row0);
     const unsigned char* st = stages + (size_t)slot * stage_bytes;
@@ -753,9 +764,13 @@ cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cuda
   return launch_tma_fmt<kFmtQ8_0, 2>(a, p, sms, stream, pdl);
 }
 
-cudaError_t read_device_error_async(unsigned* host_pinned, cudaStream_t stream) {
-  return cudaMemcpyFromSymbolAsync(host_pinned, g_device_error, sizeof(unsigned), 0, cudaMemcpyDeviceToHost,
-                                   stream);
+cudaError_t set_device_error_mirror(unsigned* host_mapped) {
+  unsigned* dptr = nullptr;
+  if (host_mapped) {
+    cudaError_t e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dptr), host_mapped, 0);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaMemcpyToSymbol(g_error_mirror, &dptr, sizeof(dptr));
 }
 
 unsigned* device_error_word() {

@@ -207,7 +207,9 @@ def unmark_static(*tensors) -> None:
 def set_option(name: str, value: int) -> int:
     """asm_set_option: "tma" / "pdl" kernel-path switches, "image_min_k" (matvecs with
     K >= it quantize x in a pre-pass; 0 = never), "gemm_splits" (0 = automatic K split
-    of the batched product, S = exactly S); returns the previous value."""
+    of the batched product, S = exactly S), "sync_map" (synchronous entries: bit 0 reads
+    pinned host x in place, bit 1 writes pinned host y in place; default 3); returns the
+    previous value."""
     prev = int(native.lib().asm_set_option(name.encode(), int(value)))
     if prev < 0:
         native.check()

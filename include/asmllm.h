@@ -501,7 +501,10 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * "gemm_splits": 0 = the batched product picks its K split (default),
  * S >= 1 = exactly S ranges (clamped to [1, 8] and to the number of 128-byte
  * weight stages).  Results are identical either way up to fp32 summation
- * order. */
+ * order.  "sync_map": how the synchronous entries treat pinned host x and y
+ * of the current device: bit 0 = the activation pre-pass reads x in place
+ * through its mapped address, bit 1 = the matvec writes y in place (default
+ * 3); a cleared bit stages that buffer with a copy. */
 ASMLLM_API int asm_set_option(const char* name, int value);
 
 /* Largest K each matvec family supports (shared-memory staging of x). */

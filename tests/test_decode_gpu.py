@@ -329,6 +329,34 @@ def test_position_out_of_range_sets_error_and_skips(cuda):
         dec.close()
 
 
+def test_sync_entry_reports_and_consumes_kernel_error_bits(cuda):
+    # the synchronous entries learn of a kernel's error report through a mapped
+    # host word (no copy back per call); the bits come from the device word
+    torch = cuda
+    rng = np.random.default_rng(3)
+    M, K = 64, 256
+    qw = rng.integers(0, 256, (M, K // 32, 16), dtype=np.uint8)
+    sc = np.abs(rng.normal(0, 0.02, (M, K // 32))).astype(np.float16).astype(np.float32)
+    x = rng.standard_normal(K).astype(np.float32)
+    y0 = ops.matmul_q4(qw, sc, x)  # also sets up the device state and its error word
+    dec = D.LlamaDecoder(SMALL, ctx=8, seed=14)
+    try:
+        dec.generate([1, 2], 6)
+        dec.step(2)  # position 8 is out of range: the argmax epilogue reports it
+        torch.cuda.synchronize()
+        with pytest.raises(native.AsmError, match="error bits 0x2"):
+            ops.matmul_q4(qw, sc, x)
+        assert ops.device_error() == 0  # consumed by the synchronous entry
+        np.testing.assert_array_equal(ops.matmul_q4(qw, sc, x), y0)
+        # bits already consumed through asm_device_error are not reported again
+        dec.step(1)
+        torch.cuda.synchronize()
+        assert ops.device_error() & native.DEVERR_DECODE_RANGE
+        np.testing.assert_array_equal(ops.matmul_q4(qw, sc, x), y0)
+    finally:
+        dec.close()
+
+
 # ---------------------------------------------------------------- persistent engine
 @pytest.mark.parametrize("shape", [SMALL, SMALL_GQA], ids=["mha", "gqa"])
 def test_persistent_engine_equals_per_launch_engine(cuda, shape):

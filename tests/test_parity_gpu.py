@@ -440,18 +440,40 @@ def test_long_k_prepass_equals_fused_prologue(cuda, fmt):
         ops.set_option("image_min_k", prev)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+    # the pre-pass scratch comes from the library's pool eagerly and from graph
+    # memory under stream capture: both give the same bytes
+    out = torch.empty_like(b)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ops.matvec(fmt, dw, ds, x, out=out)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, b)
+    for _ in range(3):  # eager calls with a synchronize between them reuse the pool
+        c = ops.matvec(fmt, dw, ds, x)
+        torch.cuda.synchronize()
+        assert torch.equal(c, b)
+    del g
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("mapping", [0, 1, 2, 3])
 @pytest.mark.parametrize("M,K", [(1000, 4096), (4096, 11008)])
-def test_sync_abi_pinned_buffers_used_in_place(cuda, M, K):
+def test_sync_abi_pinned_buffers_used_in_place(cuda, M, K, mapping):
     # pinned host x / y go to the kernels as mapped host memory (no staging
-    # copies); the result equals the staged (pageable) path bit for bit
+    # copies; option "sync_map" bit 0 = x, bit 1 = y); every choice equals
+    # the staged (pageable) path bit for bit
     torch = cuda
     w, s = synth.q4_0_weights(M, K, seed=21)
     x = synth.activation(K, seed=22)
     hx = torch.from_numpy(x.copy()).pin_memory()
     hy = torch.zeros(M, dtype=torch.float32).pin_memory()
-    native.lib().asm_matmul_q4(w.ctypes.data, s.ctypes.data, hx.data_ptr(), hy.data_ptr(), M, K)
-    native.check()
+    prev = ops.set_option("sync_map", mapping)
+    try:
+        native.lib().asm_matmul_q4(w.ctypes.data, s.ctypes.data, hx.data_ptr(), hy.data_ptr(), M, K)
+        native.check()
+    finally:
+        ops.set_option("sync_map", prev)
     np.testing.assert_array_equal(hy.numpy(), ops.matmul_q4(w, s, x))

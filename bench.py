@@ -566,16 +566,22 @@ def main():
                 for c in range(3):
                     ops.gemm(FMT_Q4_0, *Wp[c][i], X, out=out, tiles=tiles)
                 torch.cuda.synchronize()
+                # CUDA graphs of `reps` calls (the weight copies in turn): device time, without
+                # the host's per-call launch cost (which exceeds the small products' own)
                 reps = 30
+                g_t = capture(reps, lambda c, i=i: ops.gemm_tiles(FMT_Q4_0, *Wp[c][i], tiles, N, out=out))
+                g_q = capture(reps, lambda c, i=i: ops.gemm(FMT_Q4_0, *Wp[c][i], X, out=out, tiles=tiles))
+                g_t.replay()
+                g_q.replay()
+                torch.cuda.synchronize()
                 a0, a1, a2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 a0.record()
-                for r in range(reps):  # the product alone, from the activation tiles
-                    ops.gemm_tiles(FMT_Q4_0, *Wp[r % 3][i], tiles, N, out=out)
+                g_t.replay()  # the product alone, from the activation tiles
                 a1.record()
-                for r in range(reps):  # quantize the fp32 rows into tiles, then the product
-                    ops.gemm(FMT_Q4_0, *Wp[r % 3][i], X, out=out, tiles=tiles)
+                g_q.replay()  # quantize the fp32 rows into tiles, then the product
                 a2.record()
                 a2.synchronize()
+                del g_t, g_q
                 t = a0.elapsed_time(a1) / reps / 1e3
                 tq = a1.elapsed_time(a2) / reps / 1e3
                 row[f"{M}x{K}"] = {"us": round(t * 1e6, 2), "TOPS": round(2.0 * M * N * K / t / 1e12, 1),
@@ -751,7 +757,8 @@ def main():
                       "activation tiles by bulk copy; K split over a cluster (DSMEM reduction) when N is small",
             "ops": "2*M*N*K multiply-adds per call; 'us' = the product from activation tiles, 'us_with_quantize' "
                    "= quantizing the fp32 rows into tiles plus the product",
-            "l2": "three weight copies per shape used in turn (> 126 MB L2)", "per_shape": prefill,
+            "l2": "three weight copies per shape used in turn (> 126 MB L2)",
+            "launch": "CUDA graph of 30 calls per shape and mode, timed with CUDA events", "per_shape": prefill,
             "peak_note": f"dense int8 tensor peak = 2x the measured bf16 {bf16} TFLOP/s (MEASURED_PEAKS.json); "
                          f"the fp16 path's own dense peak is the bf16 figure",
         }

@@ -37,7 +37,7 @@
 //          latency: ~1.5k cycles each.)
 //   1      MMA issuer: two tcgen05.mma kind::f16 (K = 16 each) per block into
 //          the block's tensor-memory accumulator; one tcgen05.commit per group.
-//   2..    expanders (4 warps, or 8 with two threads per row for narrow tiles):
+//   2..    expanders (4 warps, or for narrow tiles 8 in two teams that take alternate groups):
 //          raw weights -> fp16 A tiles and each block's wd.
 //   ..13   epilogue (8 warps, or 4): warp w reads tensor-memory lanes
 //          32*(w%4).. (its rows) and its share of the BN columns, then
@@ -76,6 +76,9 @@
 #include "pipeline.cuh"
 #include "tiles.cuh"
 
+#ifndef ASMLLM_GEMM_TEAMS
+#define ASMLLM_GEMM_TEAMS 1
+#endif
 #ifndef ASMLLM_GEMM_EW
 #define ASMLLM_GEMM_EW (BN >= 64 ? 8 : 4)
 #endif
@@ -114,7 +117,11 @@ struct Cfg {
   static constexpr int kR = BN >= 128 ? 4 : BN >= 64 ? 3 : BN >= 32 ? 2 : 4;  // groups in flight
   // warps 2 .. 13: expanders then epilogue.  Narrow tiles (decode batches) are
   // bound by the weight expansion, wide ones by the epilogue.
-  static constexpr int kXW = BN >= 64 ? 4 : 8;  // expander warps (8: two threads per row)
+  static constexpr int kXW = BN >= 64 ? 4 : 8;  // expander warps
+  // With 8 expander warps: two teams of 4 (one thread per row each) that take
+  // alternate groups, so two groups are expanded at once (the expansion of one
+  // group is latency-bound: shared load -> convert -> tensor-memory store).
+  static constexpr int kTeams = (ASMLLM_GEMM_TEAMS && kXW == 8) ? 2 : 1;
   static constexpr int kEW = ASMLLM_GEMM_EW;      // epilogue warps (8: two column halves)
   static constexpr int kLoader = 2 + kXW + kEW;  // the tile loader's warp (the last)
   static constexpr int kThreads = (kLoader + 1) * 32;
@@ -348,6 +355,8 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
   using C = Cfg<BN>;
   constexpr int KB = FMT == kFmtQ4_0 ? 8 : 4;  // blocks per raw stage
   constexpr int G = C::kG, R = C::kR;
+  static_assert(C::kTeams == 1 || (KB / G <= C::kTeams && R % C::kTeams == 0),
+                "a team reads each raw stage at most once and owns every kTeams-th accumulator slot");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // the 128-byte swizzle of the raw ring repeats every 1024 bytes of shared address
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -384,10 +393,11 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
   if (tid == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(smem_u32(&raw_full[i]), 1);
-      mbar_init(smem_u32(&raw_empty[i]), C::kXW);  // expander warps
+      // expander warps: each team that reads the stage (KB / G groups of it, one per team)
+      mbar_init(smem_u32(&raw_empty[i]), (C::kXW / C::kTeams) * (KB / G < C::kTeams ? KB / G : C::kTeams));
     }
     for (int i = 0; i < R; ++i) {
-      mbar_init(smem_u32(&in_full[i]), C::kXW);  // expander warps
+      mbar_init(smem_u32(&in_full[i]), C::kXW / C::kTeams);  // the expander warps of the group's team
       mbar_init(smem_u32(&mma_done[i]), 1);
       mbar_init(smem_u32(&grp_done[i]), C::kEW);
     }
@@ -506,15 +516,17 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
     }
   } else if (warp < 2 + C::kXW) {
     pdl_wait();
-    // ---------------- expanders: one weight row per thread (two with 8 warps) ----------------
-    constexpr int kParts = C::kXW / 4;  // threads per row
-    constexpr int kCh = 4 / kParts;     // 16-byte chunks of the A row each writes
+    // ---------------- expanders: one weight row per thread (two per row with 8 warps in one team) ----------------
+    constexpr int kTeams = C::kTeams;
+    constexpr int kParts = C::kXW / 4 / kTeams;  // threads per row
+    constexpr int kCh = 4 / kParts;              // 16-byte chunks of the A row each writes
     // rows of this warp = its tensor-memory lane quarter (the A tiles may live there)
-    const int t = 32 * (warp & 3) + lane, part = (warp - 2) >> 2;
+    const int t = 32 * (warp & 3) + lane, xw = (warp - 2) >> 2;
+    const int team = kTeams > 1 ? xw : 0, part = kTeams > 1 ? 0 : xw;
     const int row = m0 + t;
     const bool row_ok = row < M;
     const __half* srow = scales + (size_t)(row_ok ? row : 0) * nb;
-    for (int g = 0; g < ng; ++g) {
+    for (int g = team; g < ng; g += kTeams) {
       const int r = g % R;
       bool ok = true;
       if (g >= R) ok = mbar_wait_bounded(smem_u32(&grp_done[r]), ((g / R) - 1) & 1);
@@ -527,7 +539,7 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
       // group's blocks unrolled so their loads and arithmetic interleave
       const int j0 = g * G, nblk = min(G, jb - j0);
       const int s = j0 / KB, bi0 = j0 % KB, rs = s % kStages;
-      if (bi0 == 0) {
+      if (bi0 == 0 || kTeams > 1) {  // (a team's group may start inside a stage)
         const bool okr = mbar_wait_bounded(smem_u32(&raw_full[rs]), (s / kStages) & 1);
         if (__any_sync(0xFFFFFFFFu, !okr || *s_abort)) {
           if (!okr) fail();
@@ -601,7 +613,7 @@ q8act_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constan
         }
         if (part == 0) reinterpret_cast<float*>(slot + C::kWdOff)[t] = wd;
       }
-      if (bi0 + nblk == KB || j0 + nblk == jb) {  // this warp is done with the raw stage
+      if (kTeams > 1 || bi0 + nblk == KB || j0 + nblk == jb) {  // this warp is done with the raw stage
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&raw_empty[rs]));
       }

@@ -771,8 +771,25 @@ cudaError_t launch_bn(const CUtensorMap& wmap, const CUtensorMap& smap, const __
   constexpr int KB = FMT == kFmtQ4_0 ? 8 : 4;
   const int nst = (nb + KB - 1) / KB;
   const long long tiles_n = (long long)((M + kGM - 1) / kGM) * ((N + BN - 1) / BN);
-  // one CTA per SM: split K while the tiles alone leave SMs idle
-  long long S = sms / tiles_n;
+  // One CTA per SM.  The K split S (1..8, at most the stage count) minimises
+  // waves(S) * (stages per CTA + fill): waves(S) = ceil(tiles * S / sms), and
+  // the fill is a CTA's start-up and drain, ~4 stages (fitted to measured
+  // times; ties keep the smaller S).  So 80 tiles of 256 K blocks take
+  // S = 3 (240 CTAs in two waves, a third of K each) rather than one wave on
+  // 80 SMs, and 448 tiles S = 2 (7 waves of half-K CTAs rather than 4 waves
+  // of full-K CTAs, the last of which runs 4).
+  long long S = 1;
+  {
+    double best = 1e300;
+    for (int s = 1; s <= 8 && s <= nst; ++s) {
+      const long long waves = (tiles_n * s + sms - 1) / sms;
+      const double t = (double)waves * ((double)((nst + s - 1) / s) + 4.0);
+      if (t < best) {
+        best = t;
+        S = s;
+      }
+    }
+  }
   if (g_opt_gemm_splits.load() > 0) S = g_opt_gemm_splits.load();
   if (S > 8) S = 8;
   if (S > nst) S = nst;

@@ -118,6 +118,27 @@ def test_gemm_7b_shapes_match_the_matvec(cuda, oracle, N, M, K):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("M,K", [(10240, 8192), (57344, 8192)])
+def test_gemm_70b_batch_shapes_match_the_matvec(cuda, M, K):
+    # 70B batch-32 projections whose tile counts (80, 448) make the launch split K
+    # over 3 and 2 cluster ranks to even out waves: rows against the GPU matvec
+    # (1e-4 bound), and two calls give the same bits
+    torch = cuda
+    w, s = weights(FMT_Q4_0, M, K, seed=92)
+    N = 32
+    X = synth.activation(K, seed=93, n=N)
+    dw, ds, dX = torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda().half(), torch.from_numpy(X).cuda()
+    img = ops.act_image_dev(dX)
+    y = ops.gemm_image(FMT_Q4_0, dw, ds, img, K)
+    y2 = ops.gemm_image(FMT_Q4_0, dw, ds, img, K)
+    assert torch.equal(y, y2)
+    y = y.cpu().numpy()
+    for n in (0, 7, 19, 31):
+        ref = ops.matvec_image(FMT_Q4_0, dw, ds, img[n], K).cpu().numpy()
+        assert np.abs(y[n] - ref).max() <= 1e-4 * np.abs(ref).max()
+    assert ops.device_error() == 0
+
+
 def test_gemm_rejects_bad_arguments(cuda):
     torch = cuda
     w = torch.zeros((128, 8, 16), dtype=torch.uint8, device="cuda")

@@ -1168,16 +1168,16 @@ ASMLLM_API int asm_device_error(unsigned* flags) {
 }
 
 // Q4_0 x Q8_0 matvec for callers that must not allocate device memory during
-// the call (a capture under a fixed memory plan, a serving loop with a fixed
-// budget, a plugin whose host owns all allocations).  It runs the same two
+// the call (a server that reserves all device memory at start-up, a serving
+// loop with a fixed budget, a plugin whose host owns all allocations).  It runs the same two
 // kernels as the synchronous path -- the activation-quantize pre-pass into an
 // image, then the matvec reading the image -- with the image in the
 // library's fixed device array instead of an allocated buffer.  It calls no
 // cudaMalloc / cudaFree / allocating routine.  The first call on a device
 // looks the array's address up (cudaGetSymbolAddress) and sets up the kernel
 // attributes; make that first call before any stream capture.  All calls
-// share the one array, so calls that overlap on the GPU (different streams or
-// parallel graph branches) race; calls on one stream are ordered.  The array
+// share the one array, so calls that overlap on the GPU (on different streams,
+// for instance) race; calls on one stream are ordered.  The array
 // keeps the previous call's contents; nothing in it needs clearing, since
 // each call rewrites every byte of it that the matvec uses.
 ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* scales,

@@ -237,15 +237,15 @@ ASMLLM_API int asm_weights_unmark_static(const void* ptr);
 ASMLLM_API int asm_device_error(unsigned* flags);
 
 /* Q4_0 x Q8_0 matvec that allocates no device memory, for callers that
- * cannot allocate during the call (a stream capture under a fixed memory
- * plan, a serving loop with a fixed budget, a plugin whose host owns all
- * allocations).  No counterpart in the reference.  Device pointers, stream
+ * cannot allocate during the call (a server that reserves all device memory
+ * at start-up, a serving loop with a fixed budget, a plugin whose host owns
+ * all allocations).  No counterpart in the reference.  Device pointers, stream
  * ordered; scales fp32 or fp16 (scales_are_f16); same result as
  * asm_matmul_q4_async.  The activation-quantize scratch is a fixed device
  * array inside the library, so K is limited to 32768 (ASM_E_UNSUPPORTED
  * beyond).  The first call on a device sets the array's address up: make it
  * before any stream capture.  Calls share the array: calls that overlap on
- * the GPU (different streams, parallel graph branches) race. */
+ * the GPU (on different streams, for instance) race. */
 ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* scales,
                                            int scales_are_f16, const float* x, float* y, int64_t M,
                                            int64_t K, void* stream);

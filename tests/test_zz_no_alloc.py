@@ -1,7 +1,7 @@
 """The allocation-free Q4_0 x Q8_0 entry point, asm_matmul_q4_noalloc_async.
 
 It exists for callers that cannot allocate device memory during a call: a
-CUDA stream capture running under a fixed memory plan, a serving loop with a
+server that reserves all device memory at start-up, a serving loop with a
 fixed memory budget, or a plugin whose host application owns every
 allocation.  Its quantize scratch is a fixed device array inside the library
 (K up to 32768).  These tests call it through the C ABI and check it against

@@ -188,15 +188,18 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r0 = G * (int)((long long)(M / G) * blockIdx.x / gridDim.x);
   const int r1 = G * (int)((long long)(M / G) * (blockIdx.x + 1) / gridDim.x);
-  // Plain stores may take their stages grid-strided (stage s of this CTA =
-  // stage s * grid + cta of the matrix: at any moment the CTAs stream one
-  // contiguous span); the fused epilogues need a contiguous row range per CTA.
-  constexpr bool kStride = ASMLLM_TMA_STRIDE && EPI == kEpiStore;
+  // Epilogues whose rows are independent (store, argmax, the one-GPU residual
+  // add) take their stages grid-strided: stage s of this CTA = stage
+  // s * grid + cta of the matrix, so at any moment the CTAs stream one
+  // contiguous span.  SwiGLU (pairs and per-CTA block counters) and the
+  // tensor-parallel residual exchange need a contiguous row range per CTA.
+  const bool stride = ASMLLM_TMA_STRIDE && (EPI == kEpiStore || EPI == kEpiArgmax ||
+                                            (EPI == kEpiResidual && fz.tp <= 1));
   const int n_st = (M + R - 1) / R;
-  const int S = kStride ? ((int)blockIdx.x < n_st ? (n_st - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
-                        : (r1 - r0 + R - 1) / R;  // stages; stage s owned by warpgroup s % NWG
-  auto stage_row0 = [&](int t) { return kStride ? (t * (int)gridDim.x + (int)blockIdx.x) * R : r0 + t * R; };
-  const int r_end = kStride ? M : r1;
+  const int S = stride ? ((int)blockIdx.x < n_st ? (n_st - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0)
+                       : (r1 - r0 + R - 1) / R;  // stages; stage s owned by warpgroup s % NWG
+  auto stage_row0 = [&](int t) { return stride ? (t * (int)gridDim.x + (int)blockIdx.x) * R : r0 + t * R; };
+  const int r_end = stride ? M : r1;
 
   pdl_trigger();
   if (S == 0) {

@@ -9,10 +9,12 @@
 //
 // Structure of one CTA (persistent: two per SM by default, ~100 KB of shared
 // memory each):
-//   * The CTA owns a contiguous range of rows, cut into stages of R whole rows
-//     (R in {8,4,2,1}, ~16 KB of weights).  Rows are contiguous in memory, so
-//     a stage is exactly two cp.async.bulk copies: the R rows' weights and
-//     their scales.
+//   * The matrix is cut into stages of R whole rows (R in {8,4,2,1}, ~16 KB
+//     of weights); rows are contiguous in memory, so a stage is exactly two
+//     cp.async.bulk copies: the R rows' weights and their scales.  CTA c
+//     takes stages c, c + grid, ... (all CTAs stream one contiguous span at
+//     a time), or a contiguous range of rows for the epilogues that need one
+//     (SwiGLU pairs, the tensor-parallel exchange).
 //   * 1 producer warp: one lane issues the stages into per-warpgroup rings of
 //     shared-memory slots (full/empty mbarriers, expect_tx).  Weights do not
 //     depend on the previous kernel, so when the caller declares them static

@@ -63,7 +63,7 @@ __device__ __forceinline__ void raise_device_error(unsigned bits) {
 
 namespace {
 
-constexpr int kBarBytes = 256;                   // room for 2 x 8 mbarriers + abort flag
+constexpr int kBarBytes = 256;                   // room for 2 x 15 mbarriers + abort flag
 constexpr int kPartBytes = 2 * 2 * 8 * 2 * 4;    // row partials [2 parities][2 warpgroups][8 warps][2 rows]
 
 }  // namespace
@@ -597,6 +597,8 @@ constexpr int g_tma_nwg = 2;  // consumer warpgroups
 constexpr int kTmaRowsPerWarp = ASMLLM_TMA_RW;  // rows each consumer warp takes in a stage
 const int g_tma_carveout = env_int2("ASMLLM_TMA_CARVEOUT", 100);  // percent of the unified L1/shared
 const int g_tma_pf_kb = env_int2("ASMLLM_TMA_PF_KB", 0);          // L2 prefetch window per CTA (off)
+const int g_tma_stage_kb = env_int2("ASMLLM_TMA_STAGE_KB", 16);    // weight bytes per stage (target)
+const int g_tma_max_slots = env_int2("ASMLLM_TMA_MAX_SLOTS", 8);   // ring slots per CTA (cap)
 
 struct TmaPlan {
   int R = 0, NS = 0;
@@ -613,7 +615,7 @@ bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
   const size_t row_w = (size_t)nb * ub, row_s = (size_t)nb * ss;
   if (row_w > 24 * 1024) return false;
   int R = 8;
-  while (R > 1 && (size_t)R * row_w > 16 * 1024) R /= 2;
+  while (R > 1 && (size_t)R * row_w > (size_t)g_tma_stage_kb * 1024) R /= 2;
   const size_t stage = (size_t)R * (row_w + row_s);
   const size_t img = (act_image_bytes(nb) + 127) & ~(size_t)127;
   size_t budget = (size_t)g_tma_smem_kb * 1024;
@@ -623,7 +625,9 @@ bool tma_plan(int fmt, bool f16s, int64_t nb, int smem_optin, TmaPlan* p) {
   auto slots = [&](size_t b) -> size_t {
     if (b < fixed) return 0;
     size_t n = (b - fixed) / stage;
-    if (n > 8) n = 8;
+    // the barrier area holds 2 x 15 mbarriers beside the abort flag
+    const size_t cap = g_tma_max_slots < 2 ? 2 : g_tma_max_slots > 14 ? 14 : (size_t)g_tma_max_slots;
+    if (n > cap) n = cap;
     return n - n % nwg;  // equal rings per warpgroup
   };
   size_t ns = slots(budget);

@@ -595,6 +595,9 @@ constexpr int g_tma_nwg = 2;  // consumer warpgroups
 #define ASMLLM_TMA_RW 2
 #endif
 constexpr int kTmaRowsPerWarp = ASMLLM_TMA_RW;  // rows each consumer warp takes in a stage
+// One row per warp with 8-row stages (each warp alone on its rows) failed the
+// graph-replay determinism test when tried; only two rows per warp is validated.
+static_assert(kTmaRowsPerWarp == 2, "only ASMLLM_TMA_RW=2 is validated");
 const int g_tma_carveout = env_int2("ASMLLM_TMA_CARVEOUT", 100);  // percent of the unified L1/shared
 const int g_tma_pf_kb = env_int2("ASMLLM_TMA_PF_KB", 0);          // L2 prefetch window per CTA (off)
 const int g_tma_stage_kb = env_int2("ASMLLM_TMA_STAGE_KB", 16);    // weight bytes per stage (target)

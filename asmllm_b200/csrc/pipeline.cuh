@@ -92,6 +92,18 @@ static __device__ __forceinline__ bool wg_bar_or(int wg, bool v) {
   return r != 0;
 }
 
+// Barrier over the nthreads threads (whole warps) that use named barrier id,
+// ORing a flag across them: every warp gets the same answer.
+static __device__ __forceinline__ bool group_bar_or(int id, int nthreads, bool v) {
+  unsigned r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(r)
+      : "r"((unsigned)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 
 // Orderable 64-bit key of (value, row): larger value first, then lower row
 // (numpy.argmax returns the first maximum).  Zero is below every key.

@@ -42,6 +42,9 @@
 #include "matvec.cuh"
 #include "pipeline.cuh"
 
+#ifndef ASMLLM_TMA_GROUPBAR
+#define ASMLLM_TMA_GROUPBAR 1  // per-row-group barrier per stage (sweep and decode +1 % measured)
+#endif
 #ifndef ASMLLM_TMA_STRIDE
 #define ASMLLM_TMA_STRIDE 1  // grid-strided stages for plain stores (sweep +1.3 % measured)
 #endif
@@ -479,9 +482,14 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     } else if (holder) {
       pb[wi * 2 + my_row] = v;
     }
-    // One decision per warpgroup: stop together if any warp timed out or the
-    // producer gave up (no warp can be left waiting at this barrier).
-    const bool stop = wg_bar_or(wg, !ok || *s_abort);
+    // One decision per group of warps that share rows (their partials meet
+    // here; named barriers 4..11), or per warpgroup: stop together if any
+    // warp timed out or the producer gave up (no warp can be left waiting at
+    // this barrier; a group that stops leaves the ring's empty barriers
+    // short, so the producer's bounded wait raises the abort for the rest).
+    const bool stop = (ASMLLM_TMA_GROUPBAR && WPG < 8)
+                          ? group_bar_or(4 + wg * NRG + rg, 32 * WPG, !ok || *s_abort)
+                          : wg_bar_or(wg, !ok || *s_abort);
     if (stop) {
       *s_abort = 1;
       break;

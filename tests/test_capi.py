@@ -130,3 +130,21 @@ def test_package_has_no_cpu_fallback():
     for f in pkg.rglob("*.py"):
         text = f.read_text()
         assert "oracle" not in re.sub(r"#.*", "", text).replace('"""', ""), f
+
+
+def test_every_runtime_option_is_documented_and_unknown_names_are_refused(L):
+    # asm_set_option's names (capi.cu) all appear in the header's description,
+    # and an unknown name returns -1 with an error (no GPU needed)
+    src = (ROOT / "asmllm_b200" / "csrc" / "capi.cu").read_text()
+    body = src[src.index("ASMLLM_API int asm_set_option("):]
+    body = body[: body.index("\n}\n")]
+    names = re.findall(r'strcmp\(name, "([a-z_0-9]+)"\)', body)
+    assert names, "no option names found"
+    header = (ROOT / "include" / "asmllm.h").read_text()
+    for n in names:
+        assert f'"{n}"' in header, f"option {n} is not described in include/asmllm.h"
+    L.asm_set_option.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    L.asm_set_option.restype = ctypes.c_int
+    assert L.asm_set_option(b"no_such_option", 1) == -1
+    buf = ctypes.create_string_buffer(256)
+    assert L.asm_get_last_error(buf, 256) != 0 and b"no_such_option" in buf.value

@@ -186,7 +186,7 @@ def run_reference(args, rank, world):
     from asmllm_b200 import synth
     from oracle import oracle as O
 
-    REF_BUDGET_S = 100.0
+    REF_BUDGET_S = float(os.environ.get("ASMLLM_REF_BUDGET_S", "100"))  # seconds of timed CPU work
     threads = O.host_threads()
     data = []
     for i, (M, K) in enumerate(SHAPES):

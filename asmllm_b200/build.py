@@ -22,7 +22,7 @@ LIB_DIR = ROOT / "build"
 LIB_PATH = LIB_DIR / "libasmllm.so"
 
 SOURCES = ["matvec.cu", "tma_matvec.cu", "decode.cu", "decode_persistent.cu", "q5_matvec.cu", "prefill_gemm.cu",
-           "batch_decode.cu", "capi.cu"]
+           "batch_decode.cu", "glue.cu", "capi.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

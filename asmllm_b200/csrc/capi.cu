@@ -57,27 +57,20 @@ int cuda_error(cudaError_t e, const char* what) {
 }
 
 // --------------------------------------------------------------------------
-// Pointer classification (cached per exact address)
+// Pointer classification
+//
+// Asked of the driver on every call, never cached: an address says nothing
+// about the allocation behind it over time.  A pinned buffer can be
+// unregistered (cudaHostUnregister / cudaFreeHost) and its address handed out
+// again as pageable memory, and a device allocation can be freed and its
+// address reused; a cached kind or mapped device address would then send a
+// kernel through a dead mapping.  The query costs well under a microsecond
+// against the tens of microseconds of a synchronous call.
 // --------------------------------------------------------------------------
 enum PtrKind { kHostPageable = 0, kHostPinned = 1, kDevice = 2 };
 
-std::mutex g_kind_mu;
-struct KindEntry {
-  int kind, dev;
-  const void* dptr;  // pinned host memory: its device-visible address (null if not mapped)
-};
-std::unordered_map<const void*, KindEntry> g_kind_cache;
-
+// *mapped: for pinned host memory, its device-visible address (null if not mapped).
 PtrKind classify(const void* p, int* device, const void** mapped = nullptr) {
-  {
-    std::lock_guard<std::mutex> lk(g_kind_mu);
-    auto it = g_kind_cache.find(p);
-    if (it != g_kind_cache.end()) {
-      if (device) *device = it->second.dev;
-      if (mapped) *mapped = it->second.dptr;
-      return (PtrKind)it->second.kind;
-    }
-  }
   cudaPointerAttributes a;
   PtrKind k = kHostPageable;
   int dev = -1;
@@ -92,12 +85,6 @@ PtrKind classify(const void* p, int* device, const void** mapped = nullptr) {
     k = kHostPinned;
     dev = a.device;
     dptr = a.devicePointer;
-  }
-  // Pageable host memory is not cached: a later cudaHostRegister may pin it.
-  if (k != kHostPageable) {
-    std::lock_guard<std::mutex> lk(g_kind_mu);
-    if (g_kind_cache.size() > 8192) g_kind_cache.clear();
-    g_kind_cache[p] = {(int)k, dev, dptr};
   }
   if (device) *device = dev;
   if (mapped) *mapped = dptr;
@@ -117,6 +104,7 @@ struct DeviceState {
   bool init = false;
   cudaStream_t stream = nullptr;
   Buf dev[5];   // device staging: weights, scales, x, y, Q5_0 high bits
+  Buf glue[4];  // device staging of the decode-glue entries' buffers
   Buf host[2];  // pinned host staging: x, y
   Buf image;    // Q8_0 activation image of the synchronous calls
   unsigned* err_word = nullptr;  // mapped pinned word the kernels' error reports also reach
@@ -423,6 +411,62 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
 }
 
 // --------------------------------------------------------------------------
+// Synchronous decode-glue entries (asm_rmsnorm, asm_rope, asm_softmax,
+// asm_attention, asm_silu_hadamard): each buffer is used in place when it is
+// device memory of the current device, else staged through a device buffer
+// of this device's state -- copied in when the kernel reads it, copied back
+// when the kernel writes it -- and the call returns after the copies back.
+// --------------------------------------------------------------------------
+struct GlueBuf {
+  const void* host;
+  size_t bytes;
+  bool in, out;
+  void* dev;
+};
+
+template <class Launch>
+void glue_call(const char* name, GlueBuf* b, int nb, Launch launch) {
+  DeviceState* stp = nullptr;
+  int dev = 0;
+  if (get_state(&stp, &dev)) return;
+  DeviceState& st = *stp;
+  std::lock_guard<std::mutex> lk(st.mu);
+  bool staged[4] = {};
+  for (int i = 0; i < nb; ++i) {
+    int pdev = -1;
+    if (classify(b[i].host, &pdev) == kDevice) {
+      if (pdev != dev) {
+        set_error(ASM_E_INVALID, "%s: a buffer lives on device %d but the current device is %d", name, pdev, dev);
+        return;
+      }
+      b[i].dev = const_cast<void*>(b[i].host);
+      continue;
+    }
+    if (ensure_dev(st.glue[i], b[i].bytes)) return;
+    b[i].dev = st.glue[i].p;
+    staged[i] = true;
+    if (b[i].in) {
+      const cudaError_t e = cudaMemcpyAsync(b[i].dev, b[i].host, b[i].bytes, cudaMemcpyHostToDevice, st.stream);
+      if (e != cudaSuccess) {
+        cuda_error(e, name);
+        return;
+      }
+    }
+  }
+  cudaError_t e = launch(st.stream);
+  if (e == cudaErrorInvalidValue || e == cudaErrorNotSupported) {
+    set_error(ASM_E_UNSUPPORTED, "%s: size not supported (%s)", name, cudaGetErrorName(e));
+    cudaGetLastError();
+    return;
+  }
+  for (int i = 0; i < nb && e == cudaSuccess; ++i)
+    if (staged[i] && b[i].out)
+      e = cudaMemcpyAsync(const_cast<void*>(b[i].host), b[i].dev, b[i].bytes, cudaMemcpyDeviceToHost, st.stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st.stream);
+  if (e != cudaSuccess) cuda_error(e, name);
+}
+
+// --------------------------------------------------------------------------
 // Async entries: device pointers only
 // --------------------------------------------------------------------------
 int require_device(const char* name, const void* p, const char* what) {
@@ -437,7 +481,8 @@ int require_device(const char* name, const void* p, const char* what) {
 }
 
 int async_matvec(const char* name, int fmt, bool fp32_act, bool f16s, const void* w, const void* s,
-                 const float* x, float* y, int32_t* isums, int64_t M, int64_t K, void* stream) {
+                 const float* x, float* y, int32_t* isums, int64_t M, int64_t K, void* stream,
+                 bool independent = false) {
   int rc = validate(name, w, s, x, y, M, K);
   if (rc) return rc;
   if (M == 0) return ASM_OK;
@@ -467,6 +512,7 @@ int async_matvec(const char* name, int fmt, bool fp32_act, bool f16s, const void
   a.K = K;
   a.weights_static = K > 0 && is_static(w, weight_bytes(fmt, M, K)) &&
                      is_static(s, (size_t)M * (K / 32) * (f16s ? 2 : 4));
+  a.act_independent = independent;
   e = launch_matvec(a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_error(e, name);
   return ASM_OK;
@@ -799,6 +845,106 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
   return ASM_OK;
 }
 
+ASMLLM_API void asm_threadpool_dispatch_q5(const uint8_t* ql, const uint8_t* qh, const float* scales,
+                                           const float* x, float* y, int64_t M, int64_t K) {
+  sync_q5("asm_threadpool_dispatch_q5", ql, qh, scales, x, y, M, K);
+}
+
+ASMLLM_API void asm_rmsnorm(const float* x, const float* weight, float* y, int64_t dim, float eps) {
+  const char* name = "asm_rmsnorm";
+  if (dim <= 0 || dim > glue_max_len()) {
+    set_error(dim < 0 ? ASM_E_INVALID : ASM_E_UNSUPPORTED, "%s: dim=%lld out of range (1..%lld)", name,
+              (long long)dim, (long long)glue_max_len());
+    return;
+  }
+  if (!x || !weight || !y) {
+    set_error(ASM_E_INVALID, "%s: NULL pointer", name);
+    return;
+  }
+  const size_t nb = (size_t)dim * 4;
+  GlueBuf b[3] = {{x, nb, true, false, nullptr}, {weight, nb, true, false, nullptr}, {y, nb, false, true, nullptr}};
+  glue_call(name, b, 3, [&](cudaStream_t s) {
+    return launch_rmsnorm(static_cast<const float*>(b[0].dev), static_cast<const float*>(b[1].dev),
+                          static_cast<float*>(b[2].dev), dim, eps, s);
+  });
+}
+
+ASMLLM_API void asm_rope(float* q, float* k, int64_t head_dim, int64_t pos, float theta) {
+  const char* name = "asm_rope";
+  if (head_dim <= 0 || head_dim % 2 || head_dim > glue_max_len() || pos < 0) {
+    set_error(ASM_E_INVALID, "%s: head_dim=%lld must be positive and even, pos=%lld non-negative", name,
+              (long long)head_dim, (long long)pos);
+    return;
+  }
+  if (!q || !k) {
+    set_error(ASM_E_INVALID, "%s: NULL pointer", name);
+    return;
+  }
+  const size_t nb = (size_t)head_dim * 4;
+  GlueBuf b[2] = {{q, nb, true, true, nullptr}, {k, nb, true, true, nullptr}};
+  glue_call(name, b, 2, [&](cudaStream_t s) {
+    return launch_rope(static_cast<float*>(b[0].dev), static_cast<float*>(b[1].dev), head_dim, pos, theta, s);
+  });
+}
+
+ASMLLM_API void asm_softmax(const float* x, float* y, int64_t n) {
+  const char* name = "asm_softmax";
+  if (n <= 0 || n > glue_max_len()) {
+    set_error(n < 0 ? ASM_E_INVALID : ASM_E_UNSUPPORTED, "%s: n=%lld out of range (1..%lld)", name, (long long)n,
+              (long long)glue_max_len());
+    return;
+  }
+  if (!x || !y) {
+    set_error(ASM_E_INVALID, "%s: NULL pointer", name);
+    return;
+  }
+  const size_t nb = (size_t)n * 4;
+  GlueBuf b[2] = {{x, nb, true, false, nullptr}, {y, nb, false, true, nullptr}};
+  glue_call(name, b, 2, [&](cudaStream_t s) {
+    return launch_softmax(static_cast<const float*>(b[0].dev), static_cast<float*>(b[1].dev), n, s);
+  });
+}
+
+ASMLLM_API void asm_attention(const float* q, const float* k, const float* v, float* y, int64_t seq_len,
+                              int64_t head_dim, float scale) {
+  const char* name = "asm_attention";
+  if (seq_len <= 0 || head_dim <= 0 || seq_len > glue_max_len() || head_dim > glue_max_len()) {
+    set_error(ASM_E_INVALID, "%s: seq_len=%lld and head_dim=%lld must be positive", name, (long long)seq_len,
+              (long long)head_dim);
+    return;
+  }
+  if (!q || !k || !v || !y) {
+    set_error(ASM_E_INVALID, "%s: NULL pointer", name);
+    return;
+  }
+  const size_t nb = (size_t)seq_len * (size_t)head_dim * 4;
+  GlueBuf b[4] = {{q, nb, true, false, nullptr}, {k, nb, true, false, nullptr}, {v, nb, true, false, nullptr},
+                  {y, nb, false, true, nullptr}};
+  glue_call(name, b, 4, [&](cudaStream_t s) {
+    return launch_attention(static_cast<const float*>(b[0].dev), static_cast<const float*>(b[1].dev),
+                            static_cast<const float*>(b[2].dev), static_cast<float*>(b[3].dev), seq_len, head_dim,
+                            scale, s);
+  });
+}
+
+ASMLLM_API void asm_silu_hadamard(float* gate, const float* up, int64_t n) {
+  const char* name = "asm_silu_hadamard";
+  if (n < 0) {
+    set_error(ASM_E_INVALID, "%s: n=%lld is negative", name, (long long)n);
+    return;
+  }
+  if (n == 0) return;
+  if (!gate || !up) {
+    set_error(ASM_E_INVALID, "%s: NULL pointer", name);
+    return;
+  }
+  const size_t nb = (size_t)n * 4;
+  GlueBuf b[2] = {{gate, nb, true, true, nullptr}, {up, nb, true, false, nullptr}};
+  glue_call(name, b, 2, [&](cudaStream_t s) {
+    return launch_silu_hadamard(static_cast<float*>(b[0].dev), static_cast<const float*>(b[1].dev), n, s);
+  });
+}
+
 ASMLLM_API void asm_threadpool_dispatch_q8(const int8_t* qweights, const float* scales,
                                            const float* x, float* y, int64_t M, int64_t K) {
   sync_matvec("asm_threadpool_dispatch_q8", kFmtQ8_0, true, qweights, scales, x, y, M, K);
@@ -834,6 +980,10 @@ ASMLLM_API void asm_threadpool_shutdown(void) {
     }
     if (st.image.p) cudaFree(st.image.p);
     st.image = Buf();
+    for (auto& b : st.glue) {
+      if (b.p) cudaFree(b.p);
+      b = Buf();
+    }
     cudaStreamDestroy(st.stream);
     st.stream = nullptr;
     set_device_error_mirror(nullptr);
@@ -843,14 +993,17 @@ ASMLLM_API void asm_threadpool_shutdown(void) {
   }
   scratch_trim();
   cudaSetDevice(cur);
-  {
-    std::lock_guard<std::mutex> lk(g_kind_mu);
-    g_kind_cache.clear();
-  }
   g_num_threads = 0;
 }
 
 ASMLLM_API int asm_threadpool_get_num_threads(void) { return g_num_threads; }
+
+ASMLLM_API int asm_pointer_kind(const void* p, int* device) {
+  int dev = -1;
+  const PtrKind k = classify(p, &dev);
+  if (device) *device = dev;
+  return (int)k;
+}
 
 ASMLLM_API void asm_quantize_q8_0(const float* x, int8_t* xq, float* xd, int64_t K) {
   const char* name = "asm_quantize_q8_0";
@@ -994,6 +1147,15 @@ ASMLLM_API int asm_matmul_q4_f16s_async(const uint8_t* qweights, const uint16_t*
                                         void* stream) {
   return async_matvec("asm_matmul_q4_f16s_async", kFmtQ4_0, false, true, qweights, scales_f16, x,
                       y, nullptr, M, K, stream);
+}
+
+ASMLLM_API int asm_matvec_ex_async(int fmt, const void* qweights, const void* scales, int scales_are_f16,
+                                   const float* x, float* y, int64_t M, int64_t K, unsigned flags, void* stream) {
+  const char* name = "asm_matvec_ex_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (flags & ~(unsigned)ASM_MV_INDEPENDENT) return set_error(ASM_E_INVALID, "%s: unknown flags 0x%x", name, flags);
+  return async_matvec(name, fmt, false, scales_are_f16 != 0, qweights, scales, x, y, nullptr, M, K, stream,
+                      (flags & ASM_MV_INDEPENDENT) != 0);
 }
 
 ASMLLM_API int asm_matmul_q8q8_async(const int8_t* qweights, const float* scales, const float* x,
@@ -1639,6 +1801,10 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (strcmp(name, "gemm_splits") == 0) return g_opt_gemm_splits.exchange(value < 0 ? 0 : value);
   if (strcmp(name, "image_min_k") == 0) return g_opt_image_min_k.exchange(value < 0 ? 0 : value);
   if (strcmp(name, "sync_map") == 0) return g_opt_sync_map.exchange(value & 3);
+  if (strcmp(name, "mv_rows") == 0) return g_opt_mv_rows.exchange(value == 1 || value == 2 || value == 4 ? value : 0);
+  if (strcmp(name, "mv_slots") == 0) return g_opt_mv_slots.exchange(value < 0 ? 0 : value);
+  if (strcmp(name, "mv_smem_kb") == 0) return g_opt_mv_smem_kb.exchange(value < 16 ? 16 : value);
+  if (strcmp(name, "mv_ctas") == 0) return g_opt_mv_ctas.exchange(value < 1 ? 1 : value > 4 ? 4 : value);
   set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
   return -1;
 }

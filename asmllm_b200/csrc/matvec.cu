@@ -734,7 +734,9 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     // (measured at K = 11008: 8.1 vs 10.7 us; at K = 4096 the fused prologue
     // is as fast).  The image lives in stream-ordered scratch.
     const int min_k = g_opt_image_min_k.load();
-    if (a.image == nullptr && a.isums == nullptr && min_k > 0 && a.K >= min_k) {
+    // (An independent launch quantizes in its own prologue: a pre-pass would
+    // have to wait for the previous kernel.)
+    if (a.image == nullptr && a.isums == nullptr && !a.act_independent && min_k > 0 && a.K >= min_k) {
       void* img = nullptr;
       e = scratch_alloc_async(&img, act_image_bytes(nb), stream);
       if (e != cudaSuccess) return e;

@@ -80,6 +80,10 @@ struct MatvecArgs {
   bool weights_static = false;
   // Use the register-streaming (LDG) kernel even where the bulk-copy one applies.
   bool isums_force_ldg = false;
+  // x is not written, and y neither read nor written, by the kernel that
+  // precedes this launch in the stream: the bulk-copy kernel then starts on
+  // x without waiting for that kernel (it still waits before it completes).
+  bool act_independent = false;
   int64_t M = 0, K = 0;
   // Decode fusions (bulk-copy kernel, fp16 scales only): the prologue is
   // kProImage when image is set, else kProNorm when fuse->norm_w is set, else
@@ -182,9 +186,28 @@ cudaError_t launch_rows_argmax(const float* logits, int rows, int n, size_t stri
 cudaError_t launch_rows_advance(const long long* keys, int rows, int32_t* tokens, int max_tokens, int32_t* pos,
                                 int n_prompt, cudaStream_t stream);
 
+// The reference's decode-glue kernels (glue.cu): RMSNorm, softmax, RoPE on
+// one head's q and k in place, SiLU(gate) * up into gate, and single-head
+// attention over seq query rows.  Lengths up to glue_max_len().
+int64_t glue_max_len();
+cudaError_t launch_rmsnorm(const float* x, const float* w, float* y, int64_t n, float eps, cudaStream_t stream);
+cudaError_t launch_softmax(const float* x, float* y, int64_t n, cudaStream_t stream);
+cudaError_t launch_rope(float* q, float* k, int64_t hd, int64_t pos, float theta, cudaStream_t stream);
+cudaError_t launch_silu_hadamard(float* gate, const float* up, int64_t n, cudaStream_t stream);
+size_t attention_smem(int64_t seq);
+cudaError_t launch_attention(const float* q, const float* k, const float* v, float* y, int64_t seq, int64_t hd,
+                             float scale, cudaStream_t stream);
+
 extern std::atomic<int> g_opt_tma;  // 1: bulk-copy kernel where it applies
 extern std::atomic<int> g_opt_pdl;  // 1: programmatic dependent launch
 extern std::atomic<int> g_opt_image_min_k;  // fp32-x matvecs with K >= this quantize x in a pre-pass (0: never)
 extern std::atomic<int> g_opt_gemm_splits;  // batched product: 0 = automatic K split, else exactly this many
+// Bulk-copy matvec plan (tma_matvec.cu): rows per stage (0 = automatic), ring
+// slots per warp cap (0 = automatic), shared-memory budget per CTA in KB,
+// CTAs per SM.
+extern std::atomic<int> g_opt_mv_rows;
+extern std::atomic<int> g_opt_mv_slots;
+extern std::atomic<int> g_opt_mv_smem_kb;
+extern std::atomic<int> g_opt_mv_ctas;
 
 }  // namespace asmllm

@@ -425,10 +425,13 @@ class LlamaDecoder:
             self._handle = h
         return self._handle
 
-    def run(self, n: int, chunk: int = 16, engine: str = "persistent") -> None:
-        """n decode steps.  engine "persistent": one cooperative launch for all
-        n steps; "graph": CUDA graphs of `chunk` steps (and of one step) of the
-        per-operation launches."""
+    def run(self, n: int, chunk: int = 16, engine: str = "graph") -> None:
+        """n decode steps.  engine "graph" (default): CUDA graphs of `chunk`
+        steps (and of one step) of the per-operation launches, the same kernels
+        as the eager `step`; "persistent": one cooperative launch for all n
+        steps.  Each engine is deterministic; the two add a row's block
+        products in different fp32 orders, so their logits agree to fp32
+        rounding, not bit for bit."""
         if n <= 0:
             return
         if engine == "persistent":
@@ -444,7 +447,7 @@ class LlamaDecoder:
         for _ in range(n):
             self._graph(1).replay()
 
-    def generate(self, prompt, n_new: int, chunk: int = 16, engine: str = "persistent") -> list[int]:
+    def generate(self, prompt, n_new: int, chunk: int = 16, engine: str = "graph") -> list[int]:
         """Greedy decode: the prompt's positions, then n_new generated tokens."""
         if len(prompt) + n_new > self.max_tokens:
             raise ValueError("prompt + n_new exceeds max_tokens")

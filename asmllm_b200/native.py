@@ -78,6 +78,12 @@ SIGNATURES = {
     "asm_threadpool_shutdown": ([], None),
     "asm_threadpool_get_num_threads": ([], c_int),
     "asm_threadpool_dispatch_q8": ([vp, vp, vp, vp, i64, i64], None),
+    "asm_threadpool_dispatch_q5": ([vp, vp, vp, vp, vp, i64, i64], None),
+    "asm_rmsnorm": ([vp, vp, vp, i64, f32], None),
+    "asm_rope": ([vp, vp, i64, i64, f32], None),
+    "asm_softmax": ([vp, vp, i64], None),
+    "asm_attention": ([vp, vp, vp, vp, i64, i64, f32], None),
+    "asm_silu_hadamard": ([vp, vp, i64], None),
     "asm_matmul_q5": ([vp, vp, vp, vp, vp, i64, i64], None),
     "asm_matmul_q5_mt": ([vp, vp, vp, vp, vp, i64, i64, c_int], None),
     "asm_matmul_q5_async": ([vp, vp, vp, vp, vp, i64, i64, vp], c_int),
@@ -98,9 +104,11 @@ SIGNATURES = {
     "asm_weights_unregister": ([vp], c_int),
     "asm_weights_resident_bytes": ([ctypes.POINTER(c_int)], i64),
     "asm_get_last_error": ([ctypes.c_char_p, ctypes.c_size_t], c_int),
+    "asm_pointer_kind": ([vp, ctypes.POINTER(c_int)], c_int),
     "asm_matmul_q4_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q4_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q8q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matvec_ex_async": ([c_int, vp, vp, c_int, vp, vp, i64, i64, ctypes.c_uint, vp], c_int),
     "asm_matmul_q8q8_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q4_f32_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),

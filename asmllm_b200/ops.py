@@ -22,6 +22,8 @@ import numpy as np
 from . import native
 from .native import FMT_Q4_0, FMT_Q8_0, AsmError
 
+MV_INDEPENDENT = 1  # ASM_MV_INDEPENDENT (include/asmllm.h)
+
 # --------------------------------------------------------------------------
 # Host (numpy) layer: the reference-facing synchronous ABI
 # --------------------------------------------------------------------------
@@ -155,12 +157,15 @@ def _check_dev(t, dtypes, name):
         raise ValueError(f"{name}: tensor must be contiguous")
 
 
-def matvec(fmt: int, qweights, scales, x, out=None, *, fp32_activations=False, stream=None):
+def matvec(fmt: int, qweights, scales, x, out=None, *, fp32_activations=False, stream=None, independent=False):
     """y = W x on device tensors.
 
     fmt: FMT_Q4_0 (qweights uint8 [M, K/32, 16]) or FMT_Q8_0 (int8 [M, K/32, 32]).
     scales: fp32 or fp16 [M, K/32].  fp32_activations selects the x86 (fp32-x)
     semantics instead of Q8_0-quantized activations (fp32 scales only).
+    independent: the kernel enqueued just before this call neither writes x
+    nor touches `out` (asm_matvec_ex_async with ASM_MV_INDEPENDENT), so the
+    matvec may overlap it.
     """
     torch = _torch()
     wdt = torch.uint8 if fmt == FMT_Q4_0 else torch.int8
@@ -183,6 +188,9 @@ def matvec(fmt: int, qweights, scales, x, out=None, *, fp32_activations=False, s
         if f16:
             raise ValueError("fp32-activation kernels take fp32 scales")
         rc = (L.asm_matmul_q4_f32_async if fmt == FMT_Q4_0 else L.asm_matmul_q8_async)(*args)
+    elif independent:
+        rc = L.asm_matvec_ex_async(fmt, _ptr(qweights), _ptr(scales), 1 if f16 else 0, _ptr(x), _ptr(out), M, K,
+                                   MV_INDEPENDENT, st)
     elif fmt == FMT_Q4_0:
         rc = (L.asm_matmul_q4_f16s_async if f16 else L.asm_matmul_q4_async)(*args)
     else:

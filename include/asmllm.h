@@ -115,6 +115,46 @@ ASMLLM_API int asm_threadpool_get_num_threads(void);
 ASMLLM_API void asm_threadpool_dispatch_q8(const int8_t* qweights, const float* scales,
                                            const float* x, float* y, int64_t M, int64_t K);
 
+/* Q5_0 x fp32 dispatch with the current pool; same as asm_matmul_q5.
+ * Replaces asm_threadpool_dispatch_q5: threadpool.h:89-97, threadpool.c:667-747
+ * (exported at build_kernel.py:100). */
+ASMLLM_API void asm_threadpool_dispatch_q5(const uint8_t* ql, const uint8_t* qh, const float* scales,
+                                           const float* x, float* y, int64_t M, int64_t K);
+
+/* ---- Decode-step glue of the reference's generation driver -----------
+ * The kernels AsmEngineForward binds next to asm_matmul_q4
+ * (src/runtime/generate.py:221-250) and the correctness harness checks
+ * (tests/correctness/test_runner.py:376-467), run on the GPU.  Same names,
+ * signatures and in-place conventions; host or device pointers in any mix,
+ * synchronous like the matvec entries; errors through asm_get_last_error.
+ * Arithmetic is fp32 operation by operation as the reference's numpy
+ * definitions (tests/reference/ops.py:103-170); vector sums use numpy's
+ * pairwise order, so asm_rmsnorm is bit-exact against numpy; exp, sin, cos
+ * and pow are evaluated in double precision and rounded once to fp32, as the
+ * reference's x86 kernels do on the x87 unit (numpy's own fp32 versions
+ * differ from that by about one ulp).  Lengths up to 2^20. */
+
+/* y = (x / sqrt(mean(x^2) + eps)) * weight.  Replaces asm_rmsnorm
+ * (src/kernels/x86_64/rmsnorm_avx2.asm, arm64/rmsnorm_neon.S; build_kernel.py:89). */
+ASMLLM_API void asm_rmsnorm(const float* x, const float* weight, float* y, int64_t dim, float eps);
+/* RoPE of one head's q and k in place, interleaved pairs (x[2i], x[2i+1]):
+ * angle = pos / theta^(2i / head_dim).  Replaces asm_rope
+ * (x86_64/rope_avx2.asm, arm64/rope_neon.S; build_kernel.py:90). */
+ASMLLM_API void asm_rope(float* q, float* k, int64_t head_dim, int64_t pos, float theta);
+/* y = exp(x - max x) / sum(exp(x - max x)).  Replaces asm_softmax
+ * (x86_64/softmax_avx2.asm, arm64/softmax_neon.S; build_kernel.py:91). */
+ASMLLM_API void asm_softmax(const float* x, float* y, int64_t n);
+/* Single-head attention over seq_len query rows: y[i] = softmax_j(q[i].k[j] *
+ * scale) . v, every key (no mask); q, k, v, y [seq_len][head_dim].  Replaces
+ * asm_attention (x86_64/attention_avx2.asm:7-27, arm64/attention_neon.S;
+ * build_kernel.py:92). */
+ASMLLM_API void asm_attention(const float* q, const float* k, const float* v, float* y, int64_t seq_len,
+                              int64_t head_dim, float scale);
+/* gate[i] = (gate[i] / (1 + exp(-gate[i]))) * up[i], in place.  Replaces
+ * asm_silu_hadamard (x86_64/swiglu_avx2.asm:7-17, arm64/swiglu_neon.S;
+ * build_kernel.py:93). */
+ASMLLM_API void asm_silu_hadamard(float* gate, const float* up, int64_t n);
+
 /* ===================================================================== */
 /* 2. Additions for the B200 path                                         */
 /* ===================================================================== */
@@ -140,8 +180,13 @@ ASMLLM_API void asm_matmul_q4_f32(const uint8_t* qweights, const float* scales,
  * K) use the resident copy instead of copying the weights again.  fmt: 2 =
  * Q4_0, 8 = Q8_0 (GGUF type ids).  Scales are stored as fp16 when every
  * scale converts to fp16 exactly, else as fp32.  The host buffers must not
- * change while registered; register again after changing them.  This is the
- * one-time "upload to HBM" of the reference's loader path
+ * change while registered; register again after changing them.  The
+ * registration is keyed by the host address: unregister BEFORE freeing the
+ * host buffer.  A buffer freed while registered, and an unrelated array that
+ * later gets the same address (with the same scales pointer, M and K), is
+ * undefined: such calls compute with the resident copy of the old weights
+ * (device memory the library still owns, so nothing faults, but y is wrong).
+ * This is the one-time "upload to HBM" of the reference's loader path
  * (src/runtime/generate.py:169-180).  Returns ASM_OK or an ASM_E_* code. */
 ASMLLM_API int asm_weights_register(const void* qweights, const float* scales,
                                     int64_t M, int64_t K, int fmt);
@@ -152,6 +197,15 @@ ASMLLM_API int64_t asm_weights_resident_bytes(int* count);
 /* Last error text of the calling thread (empty when none); returns its code
  * and clears it.  The reference ABI returns void, so this is its error channel. */
 ASMLLM_API int asm_get_last_error(char* buf, size_t n);
+
+/* How the synchronous entries see pointer p right now: 0 = pageable host
+ * memory (staged by copies), 1 = pinned host memory (used in place through its
+ * mapped device address), 2 = device memory; *device (may be NULL) gets the
+ * owning device or -1.  Asked of the CUDA driver on every call and never
+ * cached, so a buffer unregistered or freed since an earlier call is seen as
+ * it is now.  Host-side query only: launches nothing.  No counterpart in the
+ * reference (its entries take host pointers only). */
+ASMLLM_API int asm_pointer_kind(const void* p, int* device);
 
 /* ---- Stream-ordered entries on device pointers ---------------------- */
 
@@ -175,6 +229,20 @@ ASMLLM_API int asm_matmul_q4_f32_async(const uint8_t* qweights, const float* sca
                                        void* stream);
 ASMLLM_API int asm_matmul_q8_async(const int8_t* qweights, const float* scales,
                                    const float* x, float* y, int64_t M, int64_t K,
+                                   void* stream);
+/* Q4_0 (fmt 2) or Q8_0 (fmt 8) x Q8_0 matvec with launch flags; scales fp32
+ * or fp16 (scales_are_f16).  Same result as asm_matmul_q4_async /
+ * asm_matmul_q8q8_async.  ASM_MV_INDEPENDENT: the caller guarantees that the
+ * kernel enqueued just before this one on `stream` neither writes x nor reads
+ * or writes y -- for instance consecutive matvecs of different inputs and
+ * outputs.  The matvec then quantizes x and computes without waiting for
+ * that kernel to finish (it still waits before it completes, so whatever
+ * follows in the stream sees both finished), and consecutive independent
+ * matvecs overlap.  No counterpart in the reference (its calls are
+ * synchronous). */
+#define ASM_MV_INDEPENDENT 1u
+ASMLLM_API int asm_matvec_ex_async(int fmt, const void* qweights, const void* scales, int scales_are_f16,
+                                   const float* x, float* y, int64_t M, int64_t K, unsigned flags,
                                    void* stream);
 /* Batched quantize: N rows of x fp32[N][K] -> xq int8[N][K], xd fp32[N][K/32]. */
 ASMLLM_API int asm_quantize_q8_0_async(const float* x, int8_t* xq, float* xd,
@@ -504,7 +572,13 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * order.  "sync_map": how the synchronous entries treat pinned host x and y
  * of the current device: bit 0 = the activation pre-pass reads x in place
  * through its mapped address, bit 1 = the matvec writes y in place (default
- * 3); a cleared bit stages that buffer with a copy. */
+ * 3); a cleared bit stages that buffer with a copy.
+ * Plan of the bulk-copy matvec (results do not depend on them): "mv_rows"
+ * rows per stage, 1, 2 or 4 (0 = automatic, default); "mv_slots" cap on the
+ * ring slots of each warp (0 = automatic up to 6, default); "mv_smem_kb"
+ * shared-memory budget of a CTA in KB (default 110, which leaves room on
+ * every SM for a CTA of the next launch; a plan that does not fit takes the
+ * whole opt-in shared memory); "mv_ctas" CTAs per SM (default 1). */
 ASMLLM_API int asm_set_option(const char* name, int value);
 
 /* Largest K each matvec family supports (shared-memory staging of x). */

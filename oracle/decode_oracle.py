@@ -13,9 +13,9 @@ src/runtime/generate.py:255-326) with the model shape as a parameter:
     (x / sqrt(mean(x^2) + eps)) * w in float32;
   * RoPE as ``ref_rope`` (ops.py:119-141) on interleaved pairs, with the
     (cos, sin) table the decoder uses (same numpy expressions);
-  * the KV cache is fp16 (the config the path is measured on); the reference
-    keeps fp32 (generate.py:252-253) -- k and v are rounded to fp16 when
-    stored and read back as float32;
+  * the KV cache is fp16 by default (the config the path is measured on); the
+    reference keeps fp32 (generate.py:252-253), kv_dtype=np.float32 -- k and v
+    are rounded to the cache dtype when stored and read back as float32;
   * attention per head: scores = q.K^T / float32(sqrt(hd)) (generate.py:292),
     softmax = exp(s - max) / sum (ops.py:144-153), out = p.V;
   * silu(gate) * up = (gate / (1 + exp(-gate))) * up (generate.py:370);
@@ -56,15 +56,16 @@ def softmax(s: np.ndarray) -> np.ndarray:
 class DecodeOracle:
     """One model's decode state on the CPU; weights from LlamaDecoder.host_weights()."""
 
-    def __init__(self, shape, weights: dict, ctx: int, fmt: int = 2, nthreads: int | None = None):
+    def __init__(self, shape, weights: dict, ctx: int, fmt: int = 2, nthreads: int | None = None,
+                 kv_dtype=np.float16):
         self.s = shape
         self.w = weights
         self.fmt = fmt
         self.ctx = ctx
         self.nthreads = nthreads or _o.host_threads()
         L, nkv, hd = shape.n_layers, shape.n_kv_heads, shape.head_dim
-        self.kc = np.zeros((L, ctx, nkv, hd), dtype=np.float16)
-        self.vc = np.zeros((L, ctx, nkv, hd), dtype=np.float16)
+        self.kc = np.zeros((L, ctx, nkv, hd), dtype=kv_dtype)  # fp16: the measured config; fp32: the reference's
+        self.vc = np.zeros((L, ctx, nkv, hd), dtype=kv_dtype)
         self.sqrt_hd = np.sqrt(np.float32(hd), dtype=np.float32)
 
     def matvec(self, w, x: np.ndarray) -> np.ndarray:
@@ -89,8 +90,8 @@ class DecodeOracle:
             v = self.matvec(L["wv"], xn).reshape(nkv, hd)
             q = rope(q, cs)
             k = rope(k, cs)
-            self.kc[li, pos] = k.astype(np.float16)
-            self.vc[li, pos] = v.astype(np.float16)
+            self.kc[li, pos] = k.astype(self.kc.dtype)
+            self.vc[li, pos] = v.astype(self.vc.dtype)
             att = np.zeros((nh, hd), dtype=np.float32)
             for h in range(nh):
                 j = h // group

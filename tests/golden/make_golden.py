@@ -6,7 +6,8 @@ checked out; pass its root as the first argument or via ASMLLM_REFERENCE_ROOT.
 It imports the reference's own Python (no copy of it lives in this repo):
 
   * tools/reference_gen.py:31-112  generate_reference_data(seed=42) -- the
-    fixture tests/correctness/test_runner.py feeds every kernel;
+    fixture tests/correctness/test_runner.py feeds every kernel (the matvecs
+    and the glue kernels rmsnorm / rope / softmax / attention);
   * tests/reference/ops.py:33-64   ref_q4_matmul / ref_q8_matmul -- the numpy
     fp32 expectations the reference harness compares against;
   * the input recipes of bench/harness/bench_matmul_q4.py:76-80,
@@ -86,7 +87,8 @@ def main() -> None:
     from tests.reference.ops import ref_q4_matmul, ref_q8_matmul  # noqa: E402
 
     data = generate_reference_data(seed=42)
-    keep = {k: v for k, v in data.items() if k.startswith(("q4_matmul", "q8_matmul", "q5_matmul"))}
+    keep = {k: v for k, v in data.items()
+            if k.startswith(("q4_matmul", "q8_matmul", "q5_matmul", "rmsnorm", "rope", "softmax", "attention"))}
     np.savez_compressed(HERE / "reference_seed42.npz", **keep)
 
     out = {}

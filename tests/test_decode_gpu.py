@@ -359,25 +359,39 @@ def test_sync_entry_reports_and_consumes_kernel_error_bits(cuda):
 
 # ---------------------------------------------------------------- persistent engine
 @pytest.mark.parametrize("shape", [SMALL, SMALL_GQA], ids=["mha", "gqa"])
-def test_persistent_engine_equals_per_launch_engine(cuda, shape):
+def test_persistent_engine_agrees_with_per_launch_engine(cuda, shape):
+    # The two engines add a row's block products in different fp32 orders
+    # (the persistent kernel splits a row over two warps), so they agree to
+    # fp32 rounding: compared teacher-forced on the same token sequence, each
+    # engine bit-deterministic on its own.
     torch = cuda
     dec = D.LlamaDecoder(shape, ctx=64, seed=15)
     try:
         prompt = [5, 600, 7, 8]
         g = dec.generate(prompt, 14, engine="graph")
-        lg = dec.logits.clone()
-        kc = dec.k_cache.clone()
+        seq = prompt + g  # every position teacher-forced (all of seq is "prompt")
+        out = {}
+        for eng in ("graph", "persistent", "persistent"):
+            dec.reset(seq)
+            dec.run(len(seq) - 1, engine=eng)
+            torch.cuda.synchronize()
+            lg, kc = dec.logits.clone(), dec.k_cache[:, :len(seq) - 1].float().clone()
+            if eng in out:  # the same engine again: bit for bit
+                assert torch.equal(lg, out[eng][0]) and torch.equal(kc, out[eng][1])
+            out[eng] = (lg, kc)
+        (lg_g, kc_g), (lg_p, kc_p) = out["graph"], out["persistent"]
+        assert rel_err(lg_p.cpu().numpy(), lg_g.cpu().numpy()) <= DECODE_TOL
+        assert rel_err(kc_p.cpu().numpy(), kc_g.cpu().numpy()) <= DECODE_TOL
+        assert dec.position() == len(seq) - 1 and ops.device_error() == 0
+        # persistent: the same steps split over several launches, bit for bit
+        dec.reset(prompt)
         p = dec.generate(prompt, 14, engine="persistent")
-        assert p == g
-        assert torch.equal(dec.logits, lg)
-        assert torch.equal(dec.k_cache[:, :17], kc[:, :17])
-        assert dec.position() == 17 and ops.device_error() == 0
-        # the same steps split over several launches
+        lp = dec.logits.clone()
         dec.reset(prompt)
         for n in (1, 4, 12):
-            dec.run(n)
+            dec.run(n, engine="persistent")
         torch.cuda.synchronize()
-        assert dec.tokens[4:18].cpu().tolist() == p and torch.equal(dec.logits, lg)
+        assert dec.tokens[4:18].cpu().tolist() == p and torch.equal(dec.logits, lp)
         assert not dec.best.any() and not dec.counters.any()
     finally:
         dec.close()
@@ -391,11 +405,14 @@ def test_persistent_engine_7b_shapes_matches_oracle(cuda, DO):
         prompt = [31999, 0, 12345]
         toks = dec.generate(prompt, 3, engine="persistent")
         lg = dec.logits.cpu().numpy().copy()
-        assert dec.generate(prompt, 3, engine="graph") == toks
-        np.testing.assert_array_equal(dec.logits.cpu().numpy(), lg)
         orc = DO.DecodeOracle(shape, dec.host_weights(), ctx=16)
         _, ol = orc.generate(prompt, 3, forced=toks)
         assert rel_err(lg, ol[-1]) <= WIDE_DECODE_TOL
+        # the per-launch engine on the same (teacher-forced) sequence
+        dec.reset(prompt + toks[:-1])
+        dec.run(len(prompt) + 2, engine="graph")
+        torch.cuda.synchronize()
+        assert rel_err(dec.logits.cpu().numpy(), ol[-1]) <= WIDE_DECODE_TOL
         assert ops.device_error() == 0
     finally:
         dec.close()
@@ -405,13 +422,13 @@ def test_persistent_engine_refuses_runs_past_the_cache(cuda):
     torch = cuda
     dec = D.LlamaDecoder(SMALL, ctx=8, seed=16)
     try:
-        dec.generate([1, 2], 3)  # position 4 afterwards
+        dec.generate([1, 2], 3, engine="persistent")  # position 4 afterwards
         assert ops.device_error() == 0
-        dec.run(5)  # would need positions 4..8: refused on the device, nothing done
+        dec.run(5, engine="persistent")  # would need positions 4..8: refused on the device, nothing done
         torch.cuda.synchronize()
         assert ops.device_error() & native.DEVERR_DECODE_RANGE
         assert dec.position() == 4
-        dec.run(3)  # positions 4..6 fit (the last id lands in tokens[7])
+        dec.run(3, engine="persistent")  # positions 4..6 fit (the last id lands in tokens[7])
         torch.cuda.synchronize()
         assert dec.position() == 7 and ops.device_error() == 0
     finally:
@@ -427,6 +444,8 @@ def test_gguf_round_trip_decodes_identically(cuda, tmp_path):
         prompt = [4, 8, 15]
         toks = dec.generate(prompt, 6, engine="graph")
         lg = dec.logits.clone()
+        toks_p = dec.generate(prompt, 6, engine="persistent")
+        lg_p = dec.logits.clone()
         dec.to_gguf(tmp_path / "m.gguf")
     finally:
         dec.close()
@@ -435,6 +454,7 @@ def test_gguf_round_trip_decodes_identically(cuda, tmp_path):
         assert back.shape == SMALL_GQA and back.fmt == FMT_Q4_0
         assert back.generate(prompt, 6, engine="graph") == toks
         assert torch.equal(back.logits, lg)
-        assert back.generate(prompt, 6, engine="persistent") == toks
+        assert back.generate(prompt, 6, engine="persistent") == toks_p
+        assert torch.equal(back.logits, lg_p)
     finally:
         back.close()

@@ -191,6 +191,7 @@ struct RegEntry {
   void* d_w = nullptr;
   void* d_s = nullptr;
   bool f16 = false;
+  bool packed = false;  // d_w holds packed rows (quants then fp16 scales per row); d_s unused
   size_t bytes = 0;
 };
 
@@ -308,11 +309,14 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
   if (K > 0) {
     std::lock_guard<std::mutex> rl(g_reg_mu);
     auto it = g_reg.find(w);
+    // A packed registration serves the Q8_0-activation kernels; the fp32-x
+    // kernels read two planes, so they stage the host weights instead.
     if (it != g_reg.end() && it->second.host_s == s && it->second.M == M && it->second.K == K &&
-        it->second.fmt == fmt && it->second.dev == dev) {
+        it->second.fmt == fmt && it->second.dev == dev && !(it->second.packed && fp32_act)) {
       a.w = it->second.d_w;
       a.scales = it->second.d_s;
       a.scales_f16 = it->second.f16;
+      a.packed = it->second.packed;
       have_w = true;
     }
   }
@@ -365,8 +369,9 @@ void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const 
   if (image_path) {
     // Quantize x once into the device's activation image, then the matvec reads it.
     if (ensure_dev(st.image, act_image_bytes(K / 32))) return;
-    e = launch_act_image(a.x, st.image.p, 1, K, st.stream, a.w, weight_bytes(fmt, M, K), a.scales,
-                         (size_t)M * (K / 32) * (a.scales_f16 ? 2 : 4));
+    const size_t sb = (size_t)M * (K / 32) * (a.scales_f16 ? 2 : 4);
+    e = launch_act_image(a.x, st.image.p, 1, K, st.stream, a.w, weight_bytes(fmt, M, K) + (a.packed ? sb : 0),
+                         a.packed ? nullptr : a.scales, a.packed ? 0 : sb);
     a.image = st.image.p;
   }
   if (e == cudaSuccess) e = launch_matvec(a, st.stream);
@@ -1086,6 +1091,29 @@ ASMLLM_API int asm_weights_register(const void* qweights, const float* scales, i
   r.dev = dev;
   r.f16 = f16;
   const size_t sb = n * (f16 ? 2 : 4);
+  // fp16 scales and K/32 a multiple of 8: one packed plane (each row's quants,
+  // then its scales), streamed one copy per stage.
+  const int64_t nb = K / 32;
+  r.packed = f16 && nb % 8 == 0;
+  if (r.packed) {
+    const size_t qrow = (size_t)nb * (fmt == kFmtQ4_0 ? 16 : 32), srow = (size_t)nb * 2;
+    std::vector<unsigned char> rows((size_t)M * (qrow + srow));
+    for (int64_t i = 0; i < M; ++i) {
+      memcpy(rows.data() + (size_t)i * (qrow + srow), static_cast<const unsigned char*>(qweights) + (size_t)i * qrow,
+             qrow);
+      memcpy(rows.data() + (size_t)i * (qrow + srow) + qrow, hs.data() + (size_t)i * nb, srow);
+    }
+    if ((e = cudaMalloc(&r.d_w, rows.size())) != cudaSuccess) return cuda_error(e, "cudaMalloc (weights)");
+    e = cudaMemcpy(r.d_w, rows.data(), rows.size(), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      free_entry(r);
+      return cuda_error(e, "cudaMemcpy (register)");
+    }
+    r.bytes = rows.size();
+    std::lock_guard<std::mutex> rl(g_reg_mu);
+    g_reg[qweights] = r;
+    return ASM_OK;
+  }
   if ((e = cudaMalloc(&r.d_w, wb)) != cudaSuccess) return cuda_error(e, "cudaMalloc (weights)");
   if ((e = cudaMalloc(&r.d_s, sb)) != cudaSuccess) {
     cudaFree(r.d_w);
@@ -1156,6 +1184,68 @@ ASMLLM_API int asm_matvec_ex_async(int fmt, const void* qweights, const void* sc
   if (flags & ~(unsigned)ASM_MV_INDEPENDENT) return set_error(ASM_E_INVALID, "%s: unknown flags 0x%x", name, flags);
   return async_matvec(name, fmt, false, scales_are_f16 != 0, qweights, scales, x, y, nullptr, M, K, stream,
                       (flags & ASM_MV_INDEPENDENT) != 0);
+}
+
+ASMLLM_API int asm_launch_floor_async(int32_t n, int32_t pdl, int32_t wait, void* stream) {
+  if (n < 0) return set_error(ASM_E_INVALID, "asm_launch_floor_async: n=%d is negative", n);
+  const cudaError_t e = launch_floor_chain(n, pdl != 0, wait != 0, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, "asm_launch_floor_async");
+  return ASM_OK;
+}
+
+ASMLLM_API int64_t asm_packed_row_bytes(int fmt, int64_t K) {
+  if ((fmt != kFmtQ4_0 && fmt != kFmtQ8_0) || K <= 0 || K % 256 != 0) return -1;
+  return (K / 32) * ((fmt == kFmtQ4_0 ? 16 : 32) + 2);
+}
+
+ASMLLM_API int asm_pack_rows_async(int fmt, const void* qweights, const uint16_t* scales_f16, void* packed, int64_t M,
+                                   int64_t K, void* stream) {
+  const char* name = "asm_pack_rows_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (M <= 0 || K <= 0 || K % 256 != 0 || M > INT32_MAX)
+    return set_error(ASM_E_INVALID, "%s: need M > 0 and K > 0 a multiple of 256", name);
+  int rc;
+  if ((rc = require_device(name, qweights, "qweights")) || (rc = require_device(name, scales_f16, "scales")) ||
+      (rc = require_device(name, packed, "packed")))
+    return rc;
+  if ((uintptr_t)qweights % 16 || (uintptr_t)scales_f16 % 16 || (uintptr_t)packed % 16)
+    return set_error(ASM_E_INVALID, "%s: buffers must be 16-byte aligned", name);
+  const cudaError_t e = launch_pack_rows(fmt, qweights, scales_f16, packed, M, K, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_matvec_packed_async(int fmt, const void* packed, const float* x, float* y, int64_t M, int64_t K,
+                                       unsigned flags, void* stream) {
+  const char* name = "asm_matvec_packed_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (flags & ~(unsigned)ASM_MV_INDEPENDENT) return set_error(ASM_E_INVALID, "%s: unknown flags 0x%x", name, flags);
+  int rc = validate(name, packed, packed, x, y, M, K);
+  if (rc) return rc;
+  if (M == 0) return ASM_OK;
+  if (K % 256 != 0) return set_error(ASM_E_INVALID, "%s: K=%lld is not a multiple of 256", name, (long long)K);
+  if ((rc = require_device(name, packed, "packed")) || (rc = require_device(name, x, "x")) ||
+      (rc = require_device(name, y, "y")))
+    return rc;
+  if ((uintptr_t)packed % 16 || (uintptr_t)x % 16)
+    return set_error(ASM_E_INVALID, "%s: packed and x must be 16-byte aligned", name);
+  MatvecArgs a;
+  a.fmt = fmt;
+  a.packed = true;
+  a.scales_f16 = true;
+  a.w = packed;
+  a.x = x;
+  a.y = y;
+  a.M = M;
+  a.K = K;
+  a.weights_static = K > 0 && is_static(packed, (size_t)M * (size_t)asm_packed_row_bytes(fmt, K));
+  a.act_independent = (flags & ASM_MV_INDEPENDENT) != 0;
+  const cudaError_t e = launch_matvec(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported)
+    return set_error(ASM_E_UNSUPPORTED, "%s: no bulk-copy plan for K=%lld (or the tma option is off)", name,
+                     (long long)K);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
 }
 
 ASMLLM_API int asm_matmul_q8q8_async(const int8_t* qweights, const float* scales, const float* x,
@@ -1803,8 +1893,9 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (strcmp(name, "sync_map") == 0) return g_opt_sync_map.exchange(value & 3);
   if (strcmp(name, "mv_rows") == 0) return g_opt_mv_rows.exchange(value == 1 || value == 2 || value == 4 ? value : 0);
   if (strcmp(name, "mv_slots") == 0) return g_opt_mv_slots.exchange(value < 0 ? 0 : value);
-  if (strcmp(name, "mv_smem_kb") == 0) return g_opt_mv_smem_kb.exchange(value < 16 ? 16 : value);
+  if (strcmp(name, "mv_smem_kb") == 0) return g_opt_mv_smem_kb.exchange(value <= 0 ? 0 : value < 16 ? 16 : value);
   if (strcmp(name, "mv_ctas") == 0) return g_opt_mv_ctas.exchange(value < 1 ? 1 : value > 4 ? 4 : value);
+  if (strcmp(name, "mv_kernel") == 0) return g_opt_mv_kernel.exchange(value == 1 || value == 2 ? value : 0);
   set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
   return -1;
 }

@@ -105,6 +105,37 @@ __device__ __forceinline__ unsigned quantize_quad(float4 v, float& d, int& qsum)
                      __byte_perm((unsigned)q[2], (unsigned)q[3], 0x0040u), 0x5410u);
 }
 
+// Quantizes one 32-element block spread over 4 consecutive lanes (lane group
+// of 4 aligned in the warp; this lane holds elements 8j..8j+7, j = lane & 3,
+// in v0 = 8j..8j+3 and v1 = 8j+4..8j+7).  All 32 lanes of the warp must call
+// it.  Same formulas as quantize_quad; returns this lane's 8 int8 values
+// packed little-endian in q0 (first four) and q1, and d and the block q-sum to
+// all 4 lanes.
+__device__ __forceinline__ void quantize_oct(float4 v0, float4 v1, float& d, int& qsum, unsigned& q0, unsigned& q1) {
+  float a = arm_fmax(arm_fmax(arm_fmax(fabsf(v0.x), fabsf(v0.y)), arm_fmax(fabsf(v0.z), fabsf(v0.w))),
+                     arm_fmax(arm_fmax(fabsf(v1.x), fabsf(v1.y)), arm_fmax(fabsf(v1.z), fabsf(v1.w))));
+  a = arm_fmax(a, __shfl_xor_sync(kFull, a, 1));
+  a = arm_fmax(a, __shfl_xor_sync(kFull, a, 2));
+  d = __fdiv_rn(a, 127.0f);
+  const float inv = (a == 0.0f) ? 0.0f : __fdiv_rn(127.0f, a);
+  const float e[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+  int q[8];
+  int s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float t = __fmul_rn(e[j], inv);
+    q[j] = (t != t) ? 0 : __float2int_rn(fminf(fmaxf(t, -128.0f), 127.0f));
+    s += q[j];
+  }
+  s += __shfl_xor_sync(kFull, s, 1);
+  s += __shfl_xor_sync(kFull, s, 2);
+  qsum = s;
+  q0 = __byte_perm(__byte_perm((unsigned)q[0], (unsigned)q[1], 0x0040u),
+                   __byte_perm((unsigned)q[2], (unsigned)q[3], 0x0040u), 0x5410u);
+  q1 = __byte_perm(__byte_perm((unsigned)q[4], (unsigned)q[5], 0x0040u),
+                   __byte_perm((unsigned)q[6], (unsigned)q[7], 0x0040u), 0x5410u);
+}
+
 // Bulk prefetch of [p, p + bytes) into L2 (sm_90+ bulk-copy unit).  Fire and
 // forget: nothing waits on it; p 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, unsigned bytes) {

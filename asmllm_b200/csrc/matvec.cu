@@ -564,7 +564,7 @@ std::atomic<int> g_opt_tma{[] {
 
 // Matvecs with K at or above this quantize x in a pre-pass kernel instead of
 // in every CTA's prologue (0: never).
-std::atomic<int> g_opt_image_min_k{8192};
+std::atomic<int> g_opt_image_min_k{0};
 
 namespace {
 
@@ -728,6 +728,9 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
     if (a.fp32_act || !tma_matvec_supported(a, di.smem_optin)) return cudaErrorNotSupported;
     return launch_tma_matvec(a, di.sms, di.smem_optin, stream, g_opt_pdl.load() != 0);
   }
+  // Packed rows are read by the bulk-copy kernel only.
+  if (a.packed && (a.fp32_act || !g_opt_tma.load() || !tma_matvec_supported(a, di.smem_optin)))
+    return cudaErrorNotSupported;
   if (!a.fp32_act && g_opt_tma.load() && !a.isums_force_ldg && tma_matvec_supported(a, di.smem_optin)) {
     // Long rows: quantizing x once in a pre-pass (which also starts pulling the
     // weights into L2) beats every CTA quantizing all of x in its prologue
@@ -740,9 +743,9 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
       void* img = nullptr;
       e = scratch_alloc_async(&img, act_image_bytes(nb), stream);
       if (e != cudaSuccess) return e;
-      const size_t wbytes = (size_t)a.M * nb * (a.fmt == kFmtQ4_0 ? 16 : 32);
-      const size_t sbytes = (size_t)a.M * nb * (a.scales_f16 ? 2 : 4);
-      e = launch_act_image(a.x, img, 1, a.K, stream, a.w, wbytes, a.scales, sbytes);
+      const size_t wbytes = (size_t)a.M * nb * ((a.fmt == kFmtQ4_0 ? 16 : 32) + (a.packed ? 2 : 0));
+      const size_t sbytes = a.packed ? 0 : (size_t)a.M * nb * (a.scales_f16 ? 2 : 4);
+      e = launch_act_image(a.x, img, 1, a.K, stream, a.w, wbytes, a.packed ? nullptr : a.scales, sbytes);
       if (e == cudaSuccess) {
         MatvecArgs b = a;
         b.image = img;
@@ -816,6 +819,62 @@ cudaError_t launch_quantize(const float* x, int8_t* xq, float* xd, long long nbl
   if (grid > cap) grid = cap;
   void* args[] = {(void*)&x, (void*)&xq, (void*)&xd, (void*)&nblocks};
   return launch_pdl((const void*)quantize_q8_0_kernel, dim3((unsigned)grid), dim3(kThreads), 0, stream, args);
+}
+
+// Launch-dependency floor: a chain of kernels that do nothing but the
+// programmatic-dependent-launch protocol the matvecs use (trigger at entry,
+// then wait for the previous grid when `wait` is set), one CTA per SM.
+__global__ void floor_kernel(int wait) {
+  pdl_trigger();
+  if (wait) pdl_wait();
+}
+
+cudaError_t launch_floor_chain(int n, bool pdl, bool wait, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const DevInfo& di = dev_info(dev);
+  const int wt = wait ? 1 : 0;
+  for (int i = 0; i < n; ++i) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)di.sms);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, floor_kernel, wt);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Packed rows: row r = its qs bytes (wq16 16-byte units), then its fp16
+// scales (ws16 units).  One thread per 16-byte unit of the output.
+__global__ void pack_rows_kernel(const uint4* __restrict__ qs, const uint4* __restrict__ sc, uint4* __restrict__ out,
+                                 long long M, int wq16, int ws16) {
+  const long long per = wq16 + ws16, total = M * per;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / per;
+    const int j = (int)(i - r * per);
+    out[i] = j < wq16 ? qs[r * wq16 + j] : sc[r * ws16 + (j - wq16)];
+  }
+}
+
+cudaError_t launch_pack_rows(int fmt, const void* qs, const void* scales_f16, void* out, int64_t M, int64_t K,
+                             cudaStream_t stream) {
+  const int64_t nb = K / QK;
+  if (M <= 0 || nb <= 0 || nb % 8 != 0) return cudaErrorInvalidValue;
+  const int wq16 = (int)(nb * (fmt == kFmtQ4_0 ? 16 : 32) / 16), ws16 = (int)(nb * 2 / 16);
+  long long blocks = (M * (wq16 + ws16) + 255) / 256;
+  if (blocks > 148LL * 32) blocks = 148LL * 32;
+  pack_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const uint4*>(qs),
+                                                         static_cast<const uint4*>(scales_f16),
+                                                         static_cast<uint4*>(out), (long long)M, wq16, ws16);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gguf_split(int fmt, const uint8_t* raw, uint8_t* qs, void* scales, int f16,

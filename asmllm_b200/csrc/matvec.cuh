@@ -84,6 +84,9 @@ struct MatvecArgs {
   // precedes this launch in the stream: the bulk-copy kernel then starts on
   // x without waiting for that kernel (it still waits before it completes).
   bool act_independent = false;
+  // w holds packed rows [M][K/32 * (16 or 32) quant bytes, then K/32 fp16
+  // scales] (pack_rows); `scales` is unused.  Bulk-copy kernel only.
+  bool packed = false;
   int64_t M = 0, K = 0;
   // Decode fusions (bulk-copy kernel, fp16 scales only): the prologue is
   // kProImage when image is set, else kProNorm when fuse->norm_w is set, else
@@ -114,6 +117,12 @@ cudaError_t launch_quantize(const float* x, int8_t* xq, float* xd, long long nbl
                             cudaStream_t stream);
 cudaError_t launch_gguf_split(int fmt, const uint8_t* raw, uint8_t* qs, void* scales, int f16,
                               long long nblocks, cudaStream_t stream);
+// n empty kernels chained as the matvecs chain (PDL attribute, trigger at
+// entry, griddepcontrol.wait when `wait`): the launch-dependency floor.
+cudaError_t launch_floor_chain(int n, bool pdl, bool wait, cudaStream_t stream);
+// qs plane + fp16 scale plane -> packed rows (MatvecArgs::packed); K/32 a multiple of 8.
+cudaError_t launch_pack_rows(int fmt, const void* qs, const void* scales_f16, void* out, int64_t M, int64_t K,
+                             cudaStream_t stream);
 int64_t max_k(int fmt, bool fp32_act, int dev);
 
 // Bulk-copy (TMA) pipeline kernel for the Q8_0-activation families
@@ -208,6 +217,7 @@ extern std::atomic<int> g_opt_gemm_splits;  // batched product: 0 = automatic K 
 extern std::atomic<int> g_opt_mv_rows;
 extern std::atomic<int> g_opt_mv_slots;
 extern std::atomic<int> g_opt_mv_smem_kb;
+extern std::atomic<int> g_opt_mv_kernel;
 extern std::atomic<int> g_opt_mv_ctas;
 
 }  // namespace asmllm

@@ -31,6 +31,11 @@
 //   * Every mbarrier wait is bounded (about a second of clock cycles); on
 //     timeout the kernel sets bit 0 of g_device_error, lets the copies it
 //     issued land, and returns.
+//
+// Rows of more than 128 blocks in launches that wait for the previous kernel
+// (decode chains, the plain entries) are streamed by the row-stage kernel of
+// tma_rows.cuh instead (use_rows below): in such chains its CTA-wide ~16 KB
+// stages measured 20-40 % faster than per-warp rings of long rows.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -73,8 +78,9 @@ static_assert(kNcw * kMaxNsw * 8 <= kBarBytes, "barrier area");
 // "mv_smem_kb", "mv_ctas"): 0 = automatic.
 std::atomic<int> g_opt_mv_rows{0};
 std::atomic<int> g_opt_mv_slots{0};
-std::atomic<int> g_opt_mv_smem_kb{110};
+std::atomic<int> g_opt_mv_smem_kb{0};
 std::atomic<int> g_opt_mv_ctas{1};
+std::atomic<int> g_opt_mv_kernel{0};
 
 
 // ---- tensor-parallel exchange words: (sequence << 32) | payload bits ------
@@ -195,6 +201,26 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Shared-memory loads at 32-bit shared addresses (volatile: they stay after
+// the mbarrier wait that makes the bulk-copied bytes visible).
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
+template <bool F16S>
+__device__ __forceinline__ float lds_scale(uint32_t a) {
+  if (F16S) {
+    unsigned short h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h) : "r"(a));
+    return half_bits_to_float(h);
+  }
+  float f;
+  asm volatile("ld.shared.f32 %0, [%1];" : "=f"(f) : "r"(a));
+  return f;
+}
+
 // Q4_0 block dot of 16 nibble bytes q with the block's 32 int8 activations
 // (xa = elements 0..15, xb = 16..31): sum (n - 8) * x, exact.  Byte j holds
 // element j in its low nibble and element 16 + j in its high nibble;
@@ -246,9 +272,13 @@ constexpr int kMvIndep = 2;  // x and y independent of the previous kernel: no w
 
 // Bytes of the activation image as the kernel keeps it in shared memory:
 // x32 [nb][32] int8 values, then dq [nb] (d fp32, q-sum int32), rounded to 128.
+// Within block b's 32 bytes the two 16-byte halves (elements 0-15 and
+// 16-31) swap places when bit 2 of b is set: lanes reading blocks b .. b + 7
+// (a quarter warp's 16-byte reads) then hit eight distinct bank quads.
+__device__ __forceinline__ int xhalf(int b, int h) { return b * 32 + ((h ^ ((b >> 2) & 1)) << 4); }
 __host__ __device__ inline size_t smem_image_bytes(int64_t nb) { return ((size_t)nb * 40 + 127) & ~(size_t)127; }
 
-template <int FMT, bool F16S, bool DBG, int PRO, int EPI, int RS, int XR, int P>
+template <int FMT, bool F16S, bool DBG, int PRO, int EPI, int RS, int XR, int NBQ, bool PK>
 __global__ void __launch_bounds__(kNcw * 32, 2)
 tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales, const void* __restrict__ act,
                   float* __restrict__ y, int32_t* __restrict__ isums, const MvShape sh, const MvFuse fz) {
@@ -265,6 +295,19 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   const float2* sdq = reinterpret_cast<const float2*>(x32 + (size_t)nb * 32);
   unsigned char* ring = x32 + smem_image_bytes(nb);
   const size_t row_w = (size_t)nb * UB, row_s = (size_t)nb * SS;
+  // Weight layouts.  Planes (PK false): w = [M][row_w] quants, scales =
+  // [M][row_s].  Packed rows (PK true): w = [M][row_w + row_s], each row its
+  // quants then its fp16 scales (the GGUF byte count), so R consecutive whole
+  // rows are one contiguous copy.  A slot of whole packed rows keeps that
+  // layout; any other slot holds [RS][cb] quant blocks then [RS][cb] scales.
+  static_assert(!PK || F16S, "packed rows carry fp16 scales");
+  const size_t g_wstride = PK ? row_w + row_s : row_w;  // global row stride of the quants
+  const size_t g_sstride = PK ? row_w + row_s : row_s;  // and of the scales
+  const unsigned char* gsc = PK ? w + row_w : static_cast<const unsigned char*>(scales);
+  const bool pk_slot = PK && C == 1;
+  const size_t sl_wstride = pk_slot ? row_w + row_s : (size_t)cb * UB;  // in a slot: row stride of the quants,
+  const size_t sl_sbase = pk_slot ? row_w : (size_t)RS * cb * UB;        // where the scales start,
+  const size_t sl_sstride = pk_slot ? row_w + row_s : (size_t)cb * SS;   // and their row stride
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Row groups of RS rows.  Epilogues whose rows are independent (store,
@@ -310,26 +353,37 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   // reuses the slot for stage k + NSW.  No warp waits for another.
   const int nqw = warp < nq ? (nq - 1 - warp) / kNcw + 1 : 0;
   const int nk = nqw * C;
-  auto issue = [&](int k) {
-    const int m = k / C, c = k - m * C;
-    const int row0 = group_of(warp + m * kNcw) * RS, nrows = min(RS, M - row0);
-    const int cbn = min(cb, nb - c * cb);
-    const int slot = warp * NSW + k % NSW;
-    const uint32_t full = smem_u32(&bars[slot]);
-    const uint32_t sw = smem_u32(ring + (size_t)slot * sh.slot_bytes);
-    const uint32_t ss = sw + (uint32_t)(RS * cb * UB);
-    const unsigned char* gs = static_cast<const unsigned char*>(scales);
+  // Stages are issued in order by lane 0; its cursor (stage index, slot,
+  // chunk, row group) advances by one per copy set, without divisions.
+  const uint32_t ring_u32 = smem_u32(ring), bars_u32 = smem_u32(bars);
+  const int grp_step = stride ? kNcw * G : kNcw;  // row groups between a warp's consecutive groups
+  int i_k = 0, i_slot = 0, i_c = 0, i_grp = group_of(warp);
+  auto issue_next = [&]() {  // lane 0 only
+    if (i_k >= nk) return;
+    const int row0 = i_grp * RS, nrows = min(RS, M - row0);
+    const int cbn = min(cb, nb - i_c * cb);
+    const uint32_t full = bars_u32 + 8u * (uint32_t)(warp * NSW + i_slot);
+    const uint32_t sw = ring_u32 + (uint32_t)(warp * NSW + i_slot) * (uint32_t)sh.slot_bytes;
+    const uint32_t ss = sw + (uint32_t)sl_sbase;
     mbar_arrive_expect_tx(full, (uint32_t)(nrows * cbn * (UB + SS)));
-    if (C == 1) {
+    if (pk_slot) {  // whole packed rows: one copy
+      bulk_g2s(sw, w + (size_t)row0 * g_wstride, (uint32_t)(nrows * g_wstride), full);
+    } else if (C == 1) {
       bulk_g2s(sw, w + (size_t)row0 * row_w, (uint32_t)(nrows * row_w), full);
-      bulk_g2s(ss, gs + (size_t)row0 * row_s, (uint32_t)(nrows * row_s), full);
+      bulk_g2s(ss, gsc + (size_t)row0 * row_s, (uint32_t)(nrows * row_s), full);
     } else {
       for (int r = 0; r < nrows; ++r) {
-        bulk_g2s(sw + (uint32_t)(r * cb * UB), w + (size_t)(row0 + r) * row_w + (size_t)c * cb * UB,
+        bulk_g2s(sw + (uint32_t)(r * cb * UB), w + (size_t)(row0 + r) * g_wstride + (size_t)i_c * cb * UB,
                  (uint32_t)(cbn * UB), full);
-        bulk_g2s(ss + (uint32_t)(r * cb * SS), gs + (size_t)(row0 + r) * row_s + (size_t)c * cb * SS,
+        bulk_g2s(ss + (uint32_t)(r * cb * SS), gsc + (size_t)(row0 + r) * g_sstride + (size_t)i_c * cb * SS,
                  (uint32_t)(cbn * SS), full);
       }
+    }
+    ++i_k;
+    if (++i_slot == NSW) i_slot = 0;
+    if (++i_c == C) {
+      i_c = 0;
+      i_grp += grp_step;
     }
   };
   const int n_first = min(NSW, nk);
@@ -337,64 +391,94 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   // them static: under programmatic dependent launch the rings fill while the
   // previous kernel still runs.
   if (pre && lane == 0)
-    for (int k = 0; k < n_first; ++k) issue(k);
+    for (int t = 0; t < n_first; ++t) issue_next();
   if (!indep) pdl_wait();  // x / the image may come from the previous kernel; y may still be in use
   if (!pre && lane == 0)
-    for (int k = 0; k < n_first; ++k) issue(k);
+    for (int t = 0; t < n_first; ++t) issue_next();
 
   // Tensor-parallel call number (the previous exchange's last CTA stored it).
   const unsigned seq = (fz.tp > 1 && (EPI == kEpiResidual || EPI == kEpiArgmax)) ? __ldcg(fz.ar_seq) + 1u : 0u;
 
   // ---------------------------------------------------------- activation image
   if (PRO != kProImage) {
+    // 4 lanes per block (8 elements each), 64 blocks per pass; the loads of up
+    // to PB passes are issued before any use, so x costs one L2 round trip
+    // per PB passes (one in all for K <= 12288).
     const float* x = prologue_source(fz, act, nb * QK);
     const bool copy = fz.x_copy != nullptr && blockIdx.x == 0;
-    const int lane8 = threadIdx.x & 7;
-    constexpr int BPP = NCT / 8;  // blocks per pass
-    float rms = 1.0f;
-    if (PRO == kProNorm) {
-      // rms = sqrt(mean(x^2) + eps), one fixed-order sum shared by every thread.
-      float ssum = 0.0f;
-      for (int i = threadIdx.x; i < nb * 8; i += NCT) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(x) + i);
-        ssum = __fadd_rn(ssum, __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
-                                         __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w))));
-        if (copy) reinterpret_cast<float4*>(fz.x_copy)[i] = v;
-      }
-      ssum = warp_sum(ssum);
-      if (lane == 0) part[warp] = ssum;
-      __syncthreads();
-      float tot = 0.0f;
+    const int lane4 = threadIdx.x & 3;
+    constexpr int BPP = NCT / 4;  // blocks per pass
+    constexpr int PB = 6;         // passes per batch of loads
+    float4 v0[PB], v1[PB];
+    auto load_batch = [&](int base) {
 #pragma unroll
-      for (int i = 0; i < kNcw; ++i) tot = __fadd_rn(tot, part[i]);
-      rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * QK)), fz.eps));
-    } else if (copy) {
-      for (int i = threadIdx.x; i < nb * 8; i += NCT)
-        reinterpret_cast<float4*>(fz.x_copy)[i] = __ldcg(reinterpret_cast<const float4*>(x) + i);
-    }
-    for (int base = 0; base < nb; base += 4 * BPP) {
-      float4 v[4];
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {  // the loads of 4 passes before any use
-        const int b = base + p * BPP + (threadIdx.x >> 3);
-        v[p] = b < nb ? __ldcg(reinterpret_cast<const float4*>(x + (size_t)b * QK) + lane8)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (PRO == kProNorm && b < nb) {  // (x / rms) * w, as the reference RMSNorm
-          const float4 nw = reinterpret_cast<const float4*>(fz.norm_w + (size_t)b * QK)[lane8];
-          v[p] = make_float4(__fmul_rn(__fdiv_rn(v[p].x, rms), nw.x), __fmul_rn(__fdiv_rn(v[p].y, rms), nw.y),
-                             __fmul_rn(__fdiv_rn(v[p].z, rms), nw.z), __fmul_rn(__fdiv_rn(v[p].w, rms), nw.w));
+      for (int p = 0; p < PB; ++p) {
+        const int b = base + p * BPP + (threadIdx.x >> 2);
+        if (b < nb) {
+          const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * QK) + 2 * lane4;
+          v0[p] = __ldcg(src);
+          v1[p] = __ldcg(src + 1);
+        } else {
+          v0[p] = v1[p] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
+    };
+    auto sq4 = [](float4 v) {
+      return __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
+                       __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
+    };
+    const bool held = nb <= PB * BPP;  // all of x in one batch: the norm pass's loads serve the quantize
+    float rms = 1.0f;
+    if (PRO == kProNorm || copy) {
+      // rms = sqrt(mean(x^2) + eps), one fixed-order sum shared by every thread.
+      float ssum = 0.0f;
+      for (int base = 0; base < nb; base += PB * BPP) {
+        load_batch(base);
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const int b = base + p * BPP + (threadIdx.x >> 3);
+        for (int p = 0; p < PB; ++p) {
+          const int b = base + p * BPP + (threadIdx.x >> 2);
+          if (b < nb) {
+            if (PRO == kProNorm) ssum = __fadd_rn(ssum, __fadd_rn(sq4(v0[p]), sq4(v1[p])));
+            if (copy) {
+              float4* dst = reinterpret_cast<float4*>(fz.x_copy + (size_t)b * QK) + 2 * lane4;
+              dst[0] = v0[p];
+              dst[1] = v1[p];
+            }
+          }
+        }
+      }
+      if (PRO == kProNorm) {
+        ssum = warp_sum(ssum);
+        if (lane == 0) part[warp] = ssum;
+        __syncthreads();
+        float tot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < kNcw; ++i) tot = __fadd_rn(tot, part[i]);
+        rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)(nb * QK)), fz.eps));
+      }
+    }
+    for (int base = 0; base < nb; base += PB * BPP) {
+      if (!((PRO == kProNorm || copy) && held)) load_batch(base);
+#pragma unroll
+      for (int p = 0; p < PB; ++p) {
         if (base + p * BPP >= nb) break;  // uniform across the CTA
+        const int b = base + p * BPP + (threadIdx.x >> 2);
+        float4 a = v0[p], c4 = v1[p];
+        if (PRO == kProNorm && b < nb) {  // (x / rms) * w, as the reference RMSNorm
+          const float4* nwp = reinterpret_cast<const float4*>(fz.norm_w + (size_t)b * QK) + 2 * lane4;
+          const float4 w0 = nwp[0], w1 = nwp[1];
+          a = make_float4(__fmul_rn(__fdiv_rn(a.x, rms), w0.x), __fmul_rn(__fdiv_rn(a.y, rms), w0.y),
+                          __fmul_rn(__fdiv_rn(a.z, rms), w0.z), __fmul_rn(__fdiv_rn(a.w, rms), w0.w));
+          c4 = make_float4(__fmul_rn(__fdiv_rn(c4.x, rms), w1.x), __fmul_rn(__fdiv_rn(c4.y, rms), w1.y),
+                           __fmul_rn(__fdiv_rn(c4.z, rms), w1.z), __fmul_rn(__fdiv_rn(c4.w, rms), w1.w));
+        }
         float d;
         int qsum;
-        const unsigned q = quantize_quad(v[p], d, qsum);
+        unsigned q0, q1;
+        quantize_oct(a, c4, d, qsum, q0, q1);
         if (b < nb) {
-          reinterpret_cast<unsigned*>(x32 + (size_t)b * 32)[lane8] = q;
-          if (lane8 == 0) const_cast<float2*>(sdq)[b] = make_float2(d, __int_as_float(qsum));
+          *reinterpret_cast<uint2*>(x32 + xhalf(b, lane4 >> 1) + 8 * (lane4 & 1)) = make_uint2(q0, q1);
+          if (lane4 == 0) const_cast<float2*>(sdq)[b] = make_float2(d, __int_as_float(qsum));
         }
       }
     }
@@ -402,7 +486,8 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     // A prepared image (48-byte slots, then the (d, q-sum) pairs): the two
     // 16-byte halves of each slot, then the pairs.
     const unsigned char* src = static_cast<const unsigned char*>(act);
-    for (int i = threadIdx.x; i < 2 * nb; i += NCT) cp_async16(x32 + 16 * i, src + (size_t)(i >> 1) * 48 + (i & 1) * 16);
+    for (int i = threadIdx.x; i < 2 * nb; i += NCT)
+      cp_async16(x32 + xhalf(i >> 1, i & 1), src + (size_t)(i >> 1) * 48 + (i & 1) * 16);
     const int npair = (nb * 8 + 15) / 16;
     for (int i = threadIdx.x; i < npair; i += NCT)
       cp_async16(x32 + (size_t)nb * 32 + 16 * i, src + (size_t)nb * 48 + 16 * i);
@@ -418,8 +503,8 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   for (int j = 0; j < XR; ++j) {
     const int b = lane + 32 * j;
     if (b < nb) {
-      rxa[j] = *reinterpret_cast<const uint4*>(x32 + (size_t)b * 32);
-      rxb[j] = *reinterpret_cast<const uint4*>(x32 + (size_t)b * 32 + 16);
+      rxa[j] = *reinterpret_cast<const uint4*>(x32 + xhalf(b, 0));
+      rxb[j] = *reinterpret_cast<const uint4*>(x32 + xhalf(b, 1));
       const float2 dq = sdq[b];
       rxd[j] = dq.x;
       rqs8[j] = __float_as_int(dq.y) * 8;
@@ -431,100 +516,96 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   }
 
   // ---------------------------------------------------------- stages
-  // An iteration consumes P consecutive stages of this warp (P > 1 only for
-  // whole-row plans): their RS rows each are reduced together, so the warp
-  // has P times the independent work between waits.
-  constexpr int PR = P * RS;  // rows reduced per iteration
+  // Each stage is read out of its slot into registers first (a lane's blocks
+  // lane + 32 j of every row, at most NBL of them), the slot goes straight
+  // back to the copy engine for stage k + NSW, and only then does the warp
+  // compute: a slot is held for the shared-memory reads alone, so nearly the
+  // whole ring stays in flight.
+  constexpr int PR = RS;                       // rows reduced per iteration
+  constexpr int QW = FMT == kFmtQ4_0 ? 1 : 2;  // uint4 of quants per block
+  // Blocks a lane holds per row of a stage: the activation registers' count,
+  // or the register class NBQ (Q4_0 blocks of one row) divided among the rows
+  // and quant words.  The plan keeps every chunk within 32 * NBL blocks.
+  constexpr int NBL = XR > 0 ? XR : (NBQ / (QW * RS) > 0 ? NBQ / (QW * RS) : 1);
   unsigned long long best_local = 0;  // kEpiArgmax: this lane's best (value, row)
   float acc[PR];
 #pragma unroll
   for (int r = 0; r < PR; ++r) acc[r] = 0.0f;
   bool ok = true;
-  int k = 0;
-  for (; k < nk; k += P) {
-    const int np = min(P, nk - k);  // stages in this iteration (warp-uniform)
-    bool got = true;
-#pragma unroll
-    for (int p = 0; p < P; ++p)
-      if (p < np) got = mbar_wait_bounded(smem_u32(&bars[warp * NSW + (k + p) % NSW]), (unsigned)((k + p) / NSW) & 1u) && got;
+  int k = 0, slot = 0, c = 0, grp = group_of(warp);
+  unsigned phase = 0;
+  for (; k < nk; ++k) {
+    const int np = 1;
+    const uint32_t sbar = bars_u32 + 8u * (uint32_t)(warp * NSW + slot);
+    const bool got = mbar_wait_bounded(sbar, phase);
     if (__any_sync(kFull, !got)) {  // every lane stops together
       ok = false;
       if (lane == 0) raise_device_error(kErrRingTimeout);
       break;
     }
-    const int c = k % C;  // chunk of these stages (P == 1 whenever C > 1)
+    const int row0 = grp * RS, nr = min(RS, M - row0);
+    const int cbn = min(cb, nb - c * cb);
+    const uint32_t sw = ring_u32 + (uint32_t)(warp * NSW + slot) * (uint32_t)sh.slot_bytes;
+    const uint32_t ssc = sw + (uint32_t)sl_sbase;
+    const uint32_t lw = sw + (uint32_t)lane * UB, ls = ssc + (uint32_t)lane * SS;  // this lane's first block
+    uint4 q[RS][NBL][QW];
+    float sc[RS][NBL];
+    // Loads are predicated per lane: a block beyond the stage (a short last
+    // chunk, a missing last row) reads as zero weights, zero scale and zero
+    // activation, whose product adds exactly nothing -- so the block dots run
+    // unconditionally, as independent instructions the scheduler can interleave.
 #pragma unroll
-    for (int p = 0; p < P; ++p) {
-      if (p >= np) break;
-      const int row0 = group_of(warp + ((k + p) / C) * kNcw) * RS, nr = min(RS, M - row0);
-      const unsigned char* sw = ring + (size_t)(warp * NSW + (k + p) % NSW) * sh.slot_bytes;
-      const unsigned char* ss = sw + (size_t)RS * cb * UB;
-      if (XR > 0) {  // whole rows (C == 1), activation in registers
+    for (int r = 0; r < RS; ++r)
 #pragma unroll
-        for (int r = 0; r < RS; ++r) {
-          if (r < nr) {  // uniform across the warp
+      for (int j = 0; j < NBL; ++j) {
+        const bool in = r < nr && lane + 32 * j < cbn;
+        const uint32_t o = (uint32_t)r * (uint32_t)sl_wstride + (uint32_t)(32 * j * UB);
 #pragma unroll
-            for (int j = 0; j < XR; ++j) {
-              const int b = lane + 32 * j;
-              if (b < nb) {
-                const float sc = smem_scale<F16S>(ss + ((size_t)r * cb + b) * SS);
-                int isum;
-                if (FMT == kFmtQ4_0) {
-                  const uint4 q = *reinterpret_cast<const uint4*>(sw + (size_t)r * cb * UB + (size_t)b * 16);
-                  isum = q4_block_dot(q, rxa[j], rxb[j], rqs8[j]);
-                } else {
-                  const unsigned char* qp = sw + (size_t)r * cb * UB + (size_t)b * 32;
-                  isum = q8_block_dot(*reinterpret_cast<const uint4*>(qp), *reinterpret_cast<const uint4*>(qp + 16),
-                                      rxa[j], rxb[j]);
-                }
-                if (DBG) isums[(size_t)(row0 + r) * nb + b] = isum;
-                acc[p * RS + r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, rxd[j]), acc[p * RS + r]);
-              }
-            }
-          }
-        }
-      } else {
-        const int cbn = min(cb, nb - c * cb);
-#pragma unroll 2
-        for (int bl = lane; bl < cbn; bl += 32) {
-          const int b = c * cb + bl;
-          const uint4 xa = *reinterpret_cast<const uint4*>(x32 + (size_t)b * 32);
-          const uint4 xb = *reinterpret_cast<const uint4*>(x32 + (size_t)b * 32 + 16);
-          const float2 dq = sdq[b];
-#pragma unroll
-          for (int r = 0; r < RS; ++r) {
-            if (r < nr) {  // uniform across the warp
-              const float sc = smem_scale<F16S>(ss + ((size_t)r * cb + bl) * SS);
-              int isum;
-              if (FMT == kFmtQ4_0) {
-                const uint4 q = *reinterpret_cast<const uint4*>(sw + (size_t)r * cb * UB + (size_t)bl * 16);
-                isum = q4_block_dot(q, xa, xb, __float_as_int(dq.y) * 8);
-              } else {
-                const unsigned char* qp = sw + (size_t)r * cb * UB + (size_t)bl * 32;
-                isum = q8_block_dot(*reinterpret_cast<const uint4*>(qp), *reinterpret_cast<const uint4*>(qp + 16), xa,
-                                    xb);
-              }
-              if (DBG) isums[(size_t)(row0 + r) * nb + b] = isum;
-              acc[p * RS + r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc, dq.x), acc[p * RS + r]);
-            }
-          }
-        }
+        for (int h = 0; h < QW; ++h) q[r][j][h] = in ? lds_v4(lw + o + 16u * h) : make_uint4(0u, 0u, 0u, 0u);
+        sc[r][j] = in ? lds_scale<F16S>(ls + (uint32_t)r * (uint32_t)sl_sstride + (uint32_t)(32 * j * SS)) : 0.0f;
       }
-    }
     __syncwarp();
-    if (lane == 0) {  // the slots are free again: stage t + NSW goes into the slot of stage t
+    if (lane == 0 && i_k < nk) {  // the slot is free again: the next stage in order goes into it
       fence_proxy_async_smem();
-      for (int p = 0; p < np; ++p)
-        if (k + p + NSW < nk) issue(k + p + NSW);
+      issue_next();
+    }
+#pragma unroll
+    for (int j = 0; j < NBL; ++j) {
+      const int bl = lane + 32 * j;
+      const bool in = bl < cbn;
+      const int b = c * cb + bl;
+      uint4 xa, xb;
+      float xd;
+      int qs8;
+      if (XR > 0) {
+        xa = rxa[j < XR ? j : 0];
+        xb = rxb[j < XR ? j : 0];
+        xd = rxd[j < XR ? j : 0];
+        qs8 = rqs8[j < XR ? j : 0];
+      } else {
+        const uint32_t xs = smem_u32(x32);
+        const int bb = in ? b : 0;
+        xa = lds_v4(xs + (uint32_t)xhalf(bb, 0));
+        xb = lds_v4(xs + (uint32_t)xhalf(bb, 1));
+        const float2 dq = sdq[in ? b : 0];
+        xd = in ? dq.x : 0.0f;
+        qs8 = in ? __float_as_int(dq.y) * 8 : 0;
+        if (!in) xa = xb = make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int r = 0; r < RS; ++r) {
+        const int isum = FMT == kFmtQ4_0 ? q4_block_dot(q[r][j][0], xa, xb, qs8)
+                                         : q8_block_dot(q[r][j][0], q[r][j][QW - 1], xa, xb);
+        if (DBG && in && r < nr) isums[(size_t)(row0 + r) * nb + b] = isum;
+        acc[r] = __fmaf_rn(__int2float_rn(isum), __fmul_rn(sc[r][j], xd), acc[r]);
+      }
     }
     if (c == C - 1) {
       const float v = rows_reduce<PR>(acc, lane);
       constexpr int HOP = 32 / PR;  // lanes between the holders of consecutive rows
       const int rr = lane / HOP;    // row (of the PR) this lane's v totals, holders only
       const int p = rr / RS, r = rr - p * RS;
-      const int row0 = group_of(warp + ((k + p) / C) * kNcw) * RS;
-      const int nr = p < np ? min(RS, M - row0) : 0;
-      const bool holder = (lane % HOP) == 0 && r < nr;
+      const bool holder = (lane % HOP) == 0 && p < np && r < nr;
       if (EPI == kEpiSwiglu) {
         // Rows (2i, 2i + 1) = (gate_i, up_i), in one stage (RS is even): h_i =
         // silu(gate) * up, as the reference's (gate / (1 + exp(-gate))) * up.
@@ -552,6 +633,14 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       }
 #pragma unroll
       for (int r2 = 0; r2 < PR; ++r2) acc[r2] = 0.0f;
+    }
+    if (++slot == NSW) {  // the consumer's cursor: next slot, phase, chunk, row group
+      slot = 0;
+      phase ^= 1u;
+    }
+    if (++c == C) {
+      c = 0;
+      grp += grp_step;
     }
   }
   if (!ok && lane == 0) {
@@ -654,7 +743,7 @@ std::map<std::tuple<const void*, int>, bool> g_tma_attr;  // (kernel, device) ->
 
 // Work split of one launch.
 struct TmaPlan {
-  int RS = 0, XR = 0, C = 1, cb = 0, NSW = 0, slot_bytes = 0;
+  int RS = 0, XR = 0, NBQ = 4, C = 1, cb = 0, NSW = 0, slot_bytes = 0;
   size_t smem = 0;
   int per_sm = 1;
 };
@@ -672,55 +761,88 @@ struct TmaPlan {
 // and every plan adds a row's products in the same order.  When even the smallest plan does not fit the
 // budget (a very long activation image), the CTA takes the whole opt-in
 // shared memory and runs alone on its SM.
-bool tma_plan(int fmt, bool f16s, int64_t nb, int epi, int smem_optin, TmaPlan* p) {
+bool tma_plan(int fmt, bool f16s, bool packed, int64_t nb, int epi, int smem_optin, int smem_sm, int reserved,
+              TmaPlan* p) {
   const int ub = fmt == kFmtQ4_0 ? 16 : 32, ss = f16s ? 2 : 4;
   const int align = f16s ? 8 : 4;
   if (nb <= 0 || nb % align != 0) return false;  // 16-byte aligned scale rows
+  if (packed && !f16s) return false;
   const size_t fixed = (size_t)kBarBytes + kPartBytes + smem_image_bytes(nb);
   const bool swiglu = epi == kEpiSwiglu;
   const int xr = nb <= 128 ? 4 : 0;
   const int forced_rs = g_opt_mv_rows.load();
-  int rs_pref = swiglu ? 2 : (xr ? 1 : 4);
-  if (forced_rs == 1 || forced_rs == 2 || forced_rs == 4) rs_pref = (swiglu && forced_rs == 1) ? 2 : forced_rs;
-  if (xr && rs_pref > 2) rs_pref = 2;  // register-activation kernels take 1 or 2 rows per stage
   const int nsw_cap = std::max(2, std::min(kMaxNsw, g_opt_mv_slots.load() > 0 ? g_opt_mv_slots.load() : kMaxNsw));
+  // The bulk-copy engine's cost is per copy (each issuing warp gets through
+  // about one copy per ~0.6 us whatever its size; measured), so the plan
+  // wants the most bytes per copy: whole rows (one copy per plane, a single
+  // copy for packed rows) before chunks (one copy per row and plane), then
+  // the deepest ring.  Rows with the activation in registers take 1 or 2 rows
+  // per stage; SwiGLU stages hold whole (gate, up) pairs.
   auto try_budget = [&](size_t budget, TmaPlan* out) -> bool {
     if (budget <= fixed) return false;
     const size_t ring = budget - fixed;
-    for (int rs = rs_pref; rs >= (swiglu ? 2 : 1); rs /= 2) {
-      for (int C = 1; C <= 64; ++C) {
+    double best = -1.0;
+    const int qw = fmt == kFmtQ4_0 ? 1 : 2;
+    for (int rs : {2, 1})
+    for (int nbq : {4, 8, 12}) {
+      if (swiglu && rs < 2) continue;
+      if (forced_rs > 0 && rs != forced_rs && !(swiglu && forced_rs == 1 && rs == 2)) continue;
+      if (xr && fmt == kFmtQ8_0 && rs == 2 && !swiglu && forced_rs != 2) continue;  // Q8_0 registers: one row
+      if (xr && nbq != 4) continue;  // the activation-register kernels hold 4 blocks per lane
+      if (!xr && rs == 2 && nbq > 8) continue;  // two rows of staged blocks: at most 8 Q4_0 blocks' registers
+      // blocks a lane holds per row of a stage (the kernel's NBL)
+      const int nbl = xr ? xr : std::max(1, nbq / (qw * rs));
+      for (int C = 1; C <= 256; ++C) {
         if (xr && C > 1) break;  // activation registers cover whole rows only
         // Chunks of a multiple of 32 blocks: lane l then always takes the
         // blocks b = l (mod 32) in ascending order, whatever the plan, so y
         // does not depend on it (bit for bit).
         const int64_t cb = C == 1 ? nb : ((nb + C - 1) / C + 31) / 32 * 32;
         if (C > 1 && (int64_t)(C - 1) * cb >= nb) continue;  // no empty last chunk
-        const size_t slot = ((size_t)rs * cb * (ub + ss) + 127) & ~(size_t)127;
+        if (cb > 32LL * nbl) continue;                       // more blocks than a lane holds
+        const size_t bytes = (size_t)rs * cb * (ub + ss);
+        const size_t slot = (bytes + 127) & ~(size_t)127;
         int nsw = (int)(ring / ((size_t)kNcw * slot));
         if (nsw < 2) continue;
         if (nsw > nsw_cap) nsw = nsw_cap;
-        out->RS = rs;
-        out->XR = xr;
-        out->C = C;
-        out->cb = (int)cb;
-        out->NSW = nsw;
-        out->slot_bytes = (int)slot;
-        out->smem = fixed + (size_t)kNcw * nsw * slot;
-        return true;
+        const int copies = C == 1 ? (packed ? 1 : 2) : 2 * rs;
+        // Lanes compute every block slot they hold (missing blocks are zeros),
+        // so util = blocks present / block slots computed.  Copies cost per
+        // copy up to a few KB (measured), then bytes dominate: score the
+        // bytes per copy up to 4 KB, times util; a deeper ring, more rows per
+        // stage and a smaller register class break ties.
+        const double util = (double)nb / ((double)C * 32.0 * nbl);
+        const double per_copy = std::min(4096.0, (double)bytes / copies);
+        const double score = per_copy * util + 1e-3 * nsw + 1e-6 * rs - 1e-8 * nbq;
+        if (score > best) {
+          best = score;
+          out->NBQ = xr ? 4 : nbq;
+          out->RS = rs;
+          out->XR = xr;
+          out->C = C;
+          out->cb = (int)cb;
+          out->NSW = nsw;
+          out->slot_bytes = (int)slot;
+          out->smem = fixed + (size_t)kNcw * nsw * slot;
+        }
+        break;  // the first chunk count that fits is the one with the largest copies
       }
-      if (rs == 1) break;
     }
-    return false;
+    return best >= 0.0;
   };
-  size_t budget = (size_t)g_opt_mv_smem_kb.load() * 1024;
+  // Default budget: the most that still lets two CTAs (this launch's and the
+  // next one's) share an SM: half the SM's shared memory less the per-block
+  // reservation and the kernel's static shared memory (256 bytes).
+  size_t budget = g_opt_mv_smem_kb.load() > 0 ? (size_t)g_opt_mv_smem_kb.load() * 1024
+                                               : (size_t)(smem_sm / 2 - reserved - 256);
   if (budget > (size_t)smem_optin) budget = smem_optin;
   if (try_budget(budget, p)) return true;
   return try_budget((size_t)smem_optin - 1024, p);  // room for the static shared memory
 }
 
-template <int FMT, bool F16S, bool DBG, int PRO, int EPI, int RS, int XR, int P>
+template <int FMT, bool F16S, bool DBG, int PRO, int EPI, int RS, int XR, int NBQ, bool PK = false>
 cudaError_t launch_tma_t(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
-  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, PRO, EPI, RS, XR, P>;
+  auto kernel = tma_matvec_kernel<FMT, F16S, DBG, PRO, EPI, RS, XR, NBQ, PK>;
   int dev = 0;
   cudaGetDevice(&dev);
   {
@@ -786,24 +908,24 @@ bool is_fused(const MatvecArgs& a) {
 
 // Decode fusions: fp16 scales, no per-block sums; the combinations a decode
 // step uses (RMSNorm -> q/k/v, gate/up or lm_head; image or x -> residual).
-template <int FMT, int RS, int XR, int P>
+template <int FMT, int RS, int XR, int NBQ>
 cudaError_t launch_tma_fused(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
   const int pro = prologue_of(a);
   switch (a.epi) {
     case kEpiStore:
-      if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl);
+      if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl);
       break;
     case kEpiResidual:
-      if (pro == kProImage) return launch_tma_t<FMT, true, false, kProImage, kEpiResidual, RS, XR, P>(a, p, sms, stream, pdl);
-      if (pro == kProQuant) return launch_tma_t<FMT, true, false, kProQuant, kEpiResidual, RS, XR, P>(a, p, sms, stream, pdl);
+      if (pro == kProImage) return launch_tma_t<FMT, true, false, kProImage, kEpiResidual, RS, XR, NBQ>(a, p, sms, stream, pdl);
+      if (pro == kProQuant) return launch_tma_t<FMT, true, false, kProQuant, kEpiResidual, RS, XR, NBQ>(a, p, sms, stream, pdl);
       break;
     case kEpiSwiglu:
       if constexpr (RS % 2 == 0) {
-        if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiSwiglu, RS, XR, P>(a, p, sms, stream, pdl);
+        if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiSwiglu, RS, XR, NBQ>(a, p, sms, stream, pdl);
       }
       break;
     case kEpiArgmax:
-      if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiArgmax, RS, XR, P>(a, p, sms, stream, pdl);
+      if (pro == kProNorm) return launch_tma_t<FMT, true, false, kProNorm, kEpiArgmax, RS, XR, NBQ>(a, p, sms, stream, pdl);
       break;
     default:
       break;
@@ -811,33 +933,84 @@ cudaError_t launch_tma_fused(const MatvecArgs& a, const TmaPlan& p, int sms, cud
   return cudaErrorNotSupported;
 }
 
-template <int FMT, int RS, int XR, int P>
+template <int FMT, int RS, int XR, int NBQ>
 cudaError_t launch_tma_r(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
-  if (is_fused(a)) return launch_tma_fused<FMT, RS, XR, P>(a, p, sms, stream, pdl);
+  if (is_fused(a)) return launch_tma_fused<FMT, RS, XR, NBQ>(a, p, sms, stream, pdl);
   const bool fused = a.image == nullptr;
+  if (a.packed) {
+    return fused ? launch_tma_t<FMT, true, false, kProQuant, kEpiStore, RS, XR, NBQ, true>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, true, false, kProImage, kEpiStore, RS, XR, NBQ, true>(a, p, sms, stream, pdl);
+  }
   if (a.isums) {
-    return fused ? launch_tma_t<FMT, false, true, kProQuant, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl)
-                 : launch_tma_t<FMT, false, true, kProImage, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl);
+    return fused ? launch_tma_t<FMT, false, true, kProQuant, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, false, true, kProImage, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl);
   }
   if (a.scales_f16) {
-    return fused ? launch_tma_t<FMT, true, false, kProQuant, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl)
-                 : launch_tma_t<FMT, true, false, kProImage, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl);
+    return fused ? launch_tma_t<FMT, true, false, kProQuant, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl)
+                 : launch_tma_t<FMT, true, false, kProImage, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl);
   }
-  return fused ? launch_tma_t<FMT, false, false, kProQuant, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl)
-               : launch_tma_t<FMT, false, false, kProImage, kEpiStore, RS, XR, P>(a, p, sms, stream, pdl);
+  return fused ? launch_tma_t<FMT, false, false, kProQuant, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl)
+               : launch_tma_t<FMT, false, false, kProImage, kEpiStore, RS, XR, NBQ>(a, p, sms, stream, pdl);
 }
 
 template <int FMT>
 cudaError_t launch_tma_fmt(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
   if (p.XR) {
-    if (p.RS == 2) return launch_tma_r<FMT, 2, 4, 1>(a, p, sms, stream, pdl);
-    return launch_tma_r<FMT, 1, 4, 2>(a, p, sms, stream, pdl);
+    if (p.RS == 2) return launch_tma_r<FMT, 2, 4, 4>(a, p, sms, stream, pdl);
+    return launch_tma_r<FMT, 1, 4, 4>(a, p, sms, stream, pdl);
   }
-  switch (p.RS) {
-    case 4: return launch_tma_r<FMT, 4, 0, 1>(a, p, sms, stream, pdl);
-    case 2: return launch_tma_r<FMT, 2, 0, 1>(a, p, sms, stream, pdl);
-    default: return launch_tma_r<FMT, 1, 0, 1>(a, p, sms, stream, pdl);
+  if (p.RS == 2) return p.NBQ == 4 ? launch_tma_r<FMT, 2, 0, 4>(a, p, sms, stream, pdl)
+                                   : launch_tma_r<FMT, 2, 0, 8>(a, p, sms, stream, pdl);
+  switch (p.NBQ) {
+    case 4: return launch_tma_r<FMT, 1, 0, 4>(a, p, sms, stream, pdl);
+    case 8: return launch_tma_r<FMT, 1, 0, 8>(a, p, sms, stream, pdl);
+    default: return launch_tma_r<FMT, 1, 0, 12>(a, p, sms, stream, pdl);
   }
+}
+
+// Shared-memory figures of a device, read once.
+struct SmemInfo {
+  int sm = 0, reserved = 0;
+};
+SmemInfo smem_info(int smem_optin) {
+  static std::mutex mu;
+  static std::map<int, SmemInfo> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  SmemInfo s;
+  if (cudaDeviceGetAttribute(&s.sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess) s.sm = smem_optin;
+  if (cudaDeviceGetAttribute(&s.reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess) s.reserved = 1024;
+  cache[dev] = s;
+  return s;
+}
+
+bool plan_of(const MatvecArgs& a, int smem_optin, TmaPlan* p) {
+  const SmemInfo si = smem_info(smem_optin);
+  return tma_plan(a.fmt, a.packed || (a.isums ? false : a.scales_f16), a.packed, a.K / QK, a.epi, smem_optin, si.sm,
+                  si.reserved, p);
+}
+
+}  // namespace
+
+#include "tma_rows.cuh"
+
+namespace {
+
+// Which kernel streams a launch: rows longer than 128 blocks whose launch
+// waits for the previous kernel (a decode chain, the plain entries) go to the
+// row-stage kernel, everything else (short rows, packed rows, independent
+// launches) to the warp-ring kernel.  Option "mv_kernel": 0 = that choice,
+// 1 = warp rings always, 2 = row stages wherever they apply.
+bool use_rows(const MatvecArgs& a, int smem_optin, RowsPlan* rp) {
+  const int mode = g_opt_mv_kernel.load();
+  if (mode == 1 || a.packed || a.act_independent) return false;
+  if (mode == 0 && a.K / QK <= 128) return false;
+  if (!rows_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, rp)) return false;
+  if (a.epi == kEpiSwiglu && rp->R < 2) return false;
+  return true;
 }
 
 }  // namespace
@@ -846,10 +1019,16 @@ bool tma_matvec_supported(const MatvecArgs& a, int smem_optin) {
   if (a.fp32_act || a.M <= 0 || a.K <= 0 || a.M > 0x7fffffffLL) return false;
   // Bulk copies read from 16-byte aligned global addresses only (row starts
   // are multiples of 16 by the plan; the planes' bases must be too).
-  if ((uintptr_t)a.w % 16 != 0 || (uintptr_t)a.scales % 16 != 0) return false;
+  if ((uintptr_t)a.w % 16 != 0 || (!a.packed && (uintptr_t)a.scales % 16 != 0)) return false;
   if (a.image && (uintptr_t)a.image % 16 != 0) return false;
+  if (a.packed && (a.isums || is_fused(a))) return false;
+  RowsPlan rp;
+  if (use_rows(a, smem_optin, &rp)) {
+    if (is_fused(a) && (!a.scales_f16 || a.isums || (a.epi == kEpiSwiglu && a.M % 64 != 0))) return false;
+    return true;
+  }
   TmaPlan p;
-  if (!tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, a.epi, smem_optin, &p)) return false;
+  if (!plan_of(a, smem_optin, &p)) return false;
   if (is_fused(a)) {
     if (!a.scales_f16 || a.isums || a.act_independent) return false;
     if (a.epi == kEpiSwiglu && a.M % 64 != 0) return false;
@@ -860,8 +1039,13 @@ bool tma_matvec_supported(const MatvecArgs& a, int smem_optin) {
 bool matvec_is_fused(const MatvecArgs& a) { return is_fused(a); }
 
 cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl) {
+  RowsPlan rp;
+  if (use_rows(a, smem_optin, &rp)) {
+    if (a.fmt == kFmtQ4_0) return launch_rows_fmt<kFmtQ4_0>(a, rp, sms, stream, pdl);
+    return launch_rows_fmt<kFmtQ8_0>(a, rp, sms, stream, pdl);
+  }
   TmaPlan p;
-  if (!tma_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, a.epi, smem_optin, &p)) return cudaErrorInvalidValue;
+  if (!plan_of(a, smem_optin, &p)) return cudaErrorInvalidValue;
   if (a.fmt == kFmtQ4_0) return launch_tma_fmt<kFmtQ4_0>(a, p, sms, stream, pdl);
   return launch_tma_fmt<kFmtQ8_0>(a, p, sms, stream, pdl);
 }

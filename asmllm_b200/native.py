@@ -109,6 +109,10 @@ SIGNATURES = {
     "asm_matmul_q4_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q8q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matvec_ex_async": ([c_int, vp, vp, c_int, vp, vp, i64, i64, ctypes.c_uint, vp], c_int),
+    "asm_packed_row_bytes": ([c_int, i64], i64),
+    "asm_launch_floor_async": ([i32, i32, i32, vp], c_int),
+    "asm_pack_rows_async": ([c_int, vp, vp, vp, i64, i64, vp], c_int),
+    "asm_matvec_packed_async": ([c_int, vp, vp, vp, i64, i64, ctypes.c_uint, vp], c_int),
     "asm_matmul_q8q8_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q4_f32_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),

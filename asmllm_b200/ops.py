@@ -199,6 +199,43 @@ def matvec(fmt: int, qweights, scales, x, out=None, *, fp32_activations=False, s
     return out
 
 
+def packed_row_bytes(fmt: int, K: int) -> int:
+    """Bytes of one packed row (asm_packed_row_bytes); K a multiple of 256."""
+    n = int(native.lib().asm_packed_row_bytes(fmt, int(K)))
+    if n < 0:
+        raise ValueError(f"no packed layout for fmt={fmt}, K={K} (K must be a multiple of 256)")
+    return n
+
+
+def pack_rows(fmt: int, qweights, scales_f16, out=None, stream=None):
+    """Device qweights + fp16 scales -> packed rows uint8 [M, packed_row_bytes] (asm_pack_rows_async)."""
+    torch = _torch()
+    _check_dev(scales_f16, (torch.float16,), "scales")
+    M, K = scales_f16.shape[0], scales_f16.shape[1] * 32
+    if out is None:
+        out = torch.empty((M, packed_row_bytes(fmt, K)), dtype=torch.uint8, device=qweights.device)
+    native.check(native.lib().asm_pack_rows_async(fmt, _ptr(qweights), _ptr(scales_f16), _ptr(out), M, K,
+                                                  _stream_handle(stream)))
+    return out
+
+
+def matvec_packed(fmt: int, packed, x, out=None, *, stream=None, independent=False):
+    """y = W x on packed rows (asm_matvec_packed_async): Q4_0 / Q8_0 x Q8_0."""
+    torch = _torch()
+    _check_dev(packed, (torch.uint8,), "packed")
+    _check_dev(x, (torch.float32,), "x")
+    M, K = packed.shape[0], x.shape[-1]
+    if packed.numel() != M * packed_row_bytes(fmt, K):
+        raise ValueError(f"packed {tuple(packed.shape)} does not hold {M} rows of K={K}")
+    if out is None:
+        out = torch.empty(M, dtype=torch.float32, device=x.device)
+    else:
+        _check_dev(out, (torch.float32,), "out")
+    native.check(native.lib().asm_matvec_packed_async(fmt, _ptr(packed), _ptr(x), _ptr(out), M, K,
+                                                      MV_INDEPENDENT if independent else 0, _stream_handle(stream)))
+    return out
+
+
 def mark_static(*tensors) -> None:
     """Declares device tensors (model weights) static: see asm_weights_mark_static."""
     L = native.lib()

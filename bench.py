@@ -251,9 +251,13 @@ def main():
                     help="rows of the batched Llama-2-70B-shape decode timed after the batch-1 one (0: skip)")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the batched (prefill) tensor-core product at N = 8, 64, 512 tokens")
-    ap.add_argument("--mode", choices=["image", "fused"], default="fused",
-                    help="image: activation-quantize pre-pass kernel + matvec (2 launches per matvec); "
-                         "fused: quantize inside the matvec (1 launch)")
+    ap.add_argument("--layout", choices=["packed", "planes"], default="packed",
+                    help="weights as packed rows (quants then fp16 scales per row: one bulk copy per stage) "
+                         "or as the two planes of the reference ABI")
+    ap.add_argument("--chain", choices=["independent", "dependent"], default="independent",
+                    help="independent: the matvecs of a step (and of consecutive steps) use different x and y, "
+                         "declared with ASM_MV_INDEPENDENT so they overlap; dependent: each launch waits for "
+                         "the previous one, as in a decode chain")
     args = ap.parse_args()
     rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
 
@@ -295,25 +299,38 @@ def main():
     for row in W4:  # model weights: uploaded once, never rewritten (see asm_weights_mark_static)
         for qs, d in row:
             ops.mark_static(qs, d)
-    xs = {}
-    for K in sorted({K for _, K in SHAPES}):
-        gen.manual_seed(base + 500 + K)
-        xs[K] = torch.randn(K, device=dev, generator=gen)
-    ys = {M: torch.empty(M, device=dev) for M in sorted({M for M, _ in SHAPES})}
-    imgs = {K: torch.empty(ops.act_image_bytes(K), dtype=torch.uint8, device=dev) for K in xs}
+    # The resident layout the headline streams: packed rows (each row's quant
+    # blocks, then its fp16 scales; 18 bytes per block as in GGUF).
+    P4 = [[ops.pack_rows(FMT_Q4_0, qs, d) for qs, d in row] for row in W4]
+    for row in P4:
+        ops.mark_static(*row)
+    # one activation and one output per shape: no matvec of a step reads another's output
+    xs, ys = [], []
+    for i, (M, K) in enumerate(SHAPES):
+        gen.manual_seed(base + 500 + i)
+        xs.append(torch.randn(K, device=dev, generator=gen))
+        ys.append(torch.empty(M, device=dev))
+    imgs = [torch.empty(ops.act_image_bytes(K), dtype=torch.uint8, device=dev) for _, K in SHAPES]
     step_bytes = sum(q4_bytes(M, K) for M, K in SHAPES)
 
-    def one_matvec(fmt, qs, d, M, K, mode=args.mode):
-        # Each matvec quantizes its own x (the activation quantize is part of the path).
-        if mode == "fused":
-            ops.matvec(fmt, qs, d, xs[K], out=ys[M])
-        else:
-            ops.act_image_dev(xs[K], out=imgs[K], prefetch=(qs, d))
-            ops.matvec_image(fmt, qs, d, imgs[K], K, out=ys[M])
+    def one_matvec(fmt, w, i, chain=args.chain, mode="fused"):
+        """Matvec of shape i: w = packed rows (uint8 [M, row bytes]) or (qs, scales) planes."""
+        indep = chain == "independent"
+        M, K = SHAPES[i]
+        if not isinstance(w, tuple):
+            ops.matvec_packed(fmt, w, xs[i], out=ys[i], independent=indep)
+        elif mode == "fused":
+            ops.matvec(fmt, *w, xs[i], out=ys[i], independent=indep)
+        else:  # the activation-image pre-pass, then the matvec on the image
+            ops.act_image_dev(xs[i], out=imgs[i], prefetch=w)
+            ops.matvec_image(fmt, *w, imgs[i], K, out=ys[i])
 
-    def step(c, W=W4, fmt=FMT_Q4_0, shapes=SHAPES):
-        for (qs, d), (M, K) in zip(W[c], shapes):
-            one_matvec(fmt, qs, d, M, K)
+    def weights(c, layout=args.layout):
+        return P4[c] if layout == "packed" else W4[c]
+
+    def step(c, fmt=FMT_Q4_0, W=None, chain=args.chain, mode="fused"):
+        for i, w in enumerate(W[c] if W is not None else weights(c)):
+            one_matvec(fmt, w, i, chain=chain, mode=mode)
 
     # warm-up: eager steps (also primes the library's launch caches)
     for i in range(max(3, args.warmup)):
@@ -370,12 +387,13 @@ def main():
         ms = float(t.item())
     total_bytes = step_bytes * K_steps * world
     value = total_bytes / (ms / 1e3) / 1e9
-    # kernels per matvec: the image pre-pass + the matvec in "image" mode; in "fused"
-    # mode the library itself runs the pre-pass for K >= its "image_min_k" option
+    # kernels per matvec: packed rows and independent launches quantize x inside the matvec
+    # (one launch); dependent plane launches with K >= the library's "image_min_k" run its
+    # activation pre-pass first
     image_min_k = ops.set_option("image_min_k", 8192)
     ops.set_option("image_min_k", image_min_k)
-    launches = K_steps * sum(2 if args.mode == "image" or (image_min_k and K >= image_min_k) else 1
-                             for _, K in SHAPES)
+    prepass = args.layout == "planes" and args.chain == "dependent"
+    launches = K_steps * sum(2 if prepass and image_min_k and K >= image_min_k else 1 for _, K in SHAPES)
     # The matvec is the dominant kernel; per-launch figures are per matvec
     # (its quantize pre-pass, when separate, is counted inside the time).
     per_launch_ms = ms / (len(SHAPES) * K_steps)
@@ -383,63 +401,85 @@ def main():
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     del gA, gB
 
-    # ---- per-shape and Q8_0 x Q8_0 breakdown (not part of the timed value) ----
+    # ---- breakdowns (not part of the timed value) ----
     extras = {}
-    if not args.no_extras:
-        def time_graph(fn, n):
-            g = capture(n, fn)
-            g.replay()
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            for _ in range(5):
-                g.replay()
-            b.record()
-            b.synchronize()
-            return a.elapsed_time(b) / (5 * n)
+    pk = ROOT / "MEASURED_PEAKS.json"
+    peak_gbs = float(json.loads(pk.read_text())["hbm_gbs"]) if pk.exists() else FALLBACK_HBM_GBS
 
-        for mode in ("fused", "image"):
-            per_shape = {}
-            for i, (M, K) in enumerate(SHAPES):
-                def one(c, i=i, M=M, K=K, mode=mode):
-                    qs, d = W4[c][i]
-                    one_matvec(FMT_Q4_0, qs, d, M, K, mode=mode)
-                t = time_graph(one, 300)
-                per_shape[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q4_bytes(M, K) / (t / 1e3) / 1e9, 1)}
-            extras[f"q4q8_per_shape_{mode}"] = per_shape
-        t_sw = time_graph(lambda c: step(c), 60)
-        extras["q4q8_sweep_other_mode"] = {"mode": "fused" if args.mode == "image" else "image"}
-        def step_other(c):
-            for (qs, d), (M, K) in zip(W4[c], SHAPES):
-                one_matvec(FMT_Q4_0, qs, d, M, K, mode="fused" if args.mode == "image" else "image")
-        t_o = time_graph(step_other, 60)
-        extras["q4q8_sweep_other_mode"]["GB/s"] = round(step_bytes / (t_o / 1e3) / 1e9, 1)
-        extras["q4q8_sweep_this_mode_recheck_GB/s"] = round(step_bytes / (t_sw / 1e3) / 1e9, 1)
-        # Q8_0 x Q8_0 sweep on the same shapes
-        del W4
-        W8 = [[make_q8(M, K, base + 70 + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+    def time_graph(fn, n, reps=5):
+        g = capture(n, fn)
+        g.replay()
         torch.cuda.synchronize()
-        for row in W8:
-            for qs, d in row:
-                ops.mark_static(qs, d)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            g.replay()
+        b.record()
+        b.synchronize()
+        del g
+        return a.elapsed_time(b) / (reps * n)  # ms per fn call
+
+    # config 0 on its own: the M = K = 4096 matvec, chained independent and dependent
+    cfg0 = {"shape": "4096x4096", "bytes": q4_bytes(4096, 4096), "layout": args.layout}
+    for chain in ("independent", "dependent"):
+        t = time_graph(lambda c, chain=chain: one_matvec(FMT_Q4_0, weights(c)[0], 0, chain=chain), 300)
+        gbs = q4_bytes(4096, 4096) / (t / 1e3) / 1e9
+        cfg0[chain] = {"us": round(t * 1e3, 3), "GB/s": round(gbs, 1), "frac": round(gbs / peak_gbs, 4)}
+    # the launch-dependency floor: empty kernels chained as the matvecs chain
+    L0 = native.lib()
+    floor = {}
+    for wait in (1, 0):
+        def chain_fn(c, wait=wait):
+            native.check(L0.asm_launch_floor_async(1, 1, wait, ops._stream_handle(None)))
+        floor["wait" if wait else "no_wait"] = round(time_graph(chain_fn, 300) * 1e3, 3)
+    cfg0["floor_us_per_launch"] = floor
+    cfg0["note"] = ("us per matvec from CUDA graphs of 300 launches over 3 weight copies; 'dependent': every "
+                    "launch waits for the previous one (griddepcontrol.wait); floor: empty one-CTA-per-SM "
+                    "kernels chained the same way")
+    extras["config0"] = cfg0
+
+    if not args.no_extras:
+        for layout in ("packed", "planes"):
+            for chain in ("independent", "dependent"):
+                per_shape = {}
+                for i, (M, K) in enumerate(SHAPES):
+                    t = time_graph(lambda c, i=i, layout=layout, chain=chain:
+                                   one_matvec(FMT_Q4_0, weights(c, layout)[i], i, chain=chain), 300)
+                    per_shape[f"{M}x{K}"] = {"us": round(t * 1e3, 3),
+                                             "GB/s": round(q4_bytes(M, K) / (t / 1e3) / 1e9, 1)}
+                t_sw = time_graph(lambda c, layout=layout, chain=chain: step(c, W=P4 if layout == "packed" else W4,
+                                                                               chain=chain), 60)
+                extras[f"q4q8_{layout}_{chain}"] = {"sweep_GB/s": round(step_bytes / (t_sw / 1e3) / 1e9, 1),
+                                                    "per_shape": per_shape}
+        t_im = time_graph(lambda c: step(c, W=W4, chain="dependent", mode="image"), 60)
+        extras["q4q8_planes_dependent_image_prepass_sweep_GB/s"] = round(step_bytes / (t_im / 1e3) / 1e9, 1)
+        # Q8_0 x Q8_0 sweep on the same shapes (packed rows, independent launches)
+        del W4, P4
+        torch.cuda.empty_cache()
+        W8 = [[make_q8(M, K, base + 70 + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
+        P8 = [[ops.pack_rows(FMT_Q8_0, qs, d) for qs, d in row] for row in W8]
+        del W8
+        torch.cuda.synchronize()
+        for row in P8:
+            ops.mark_static(*row)
         for i in range(COPIES):
-            step(i, W=W8, fmt=FMT_Q8_0)
-        t8 = time_graph(lambda c: step(c, W=W8, fmt=FMT_Q8_0), 60)
+            step(i, fmt=FMT_Q8_0, W=P8)
+        t8 = time_graph(lambda c: step(c, fmt=FMT_Q8_0, W=P8), 60)
         b8 = sum(q8_bytes(M, K) for M, K in SHAPES)
-        extras["q8q8_sweep"] = {"us_per_step": round(t8 * 1e3, 3), "GB/s": round(b8 / (t8 / 1e3) / 1e9, 1)}
         per8 = {}
         for i, (M, K) in enumerate(SHAPES):
-            def one8(c, i=i, M=M, K=K):
-                qs, d = W8[c][i]
-                one_matvec(FMT_Q8_0, qs, d, M, K)
-            t = time_graph(one8, 300)
+            t = time_graph(lambda c, i=i: one_matvec(FMT_Q8_0, P8[c][i], i), 300)
             per8[f"{M}x{K}"] = {"us": round(t * 1e3, 3), "GB/s": round(q8_bytes(M, K) / (t / 1e3) / 1e9, 1)}
-        extras["q8q8_per_shape"] = per8
-        del W8
+        extras["q8q8_packed_" + args.chain] = {"us_per_step": round(t8 * 1e3, 3),
+                                               "GB/s": round(b8 / (t8 / 1e3) / 1e9, 1), "per_shape": per8}
+        for row in P8:
+            ops.unmark_static(*row)
+        del P8
         torch.cuda.synchronize()
         W4 = [[make_q4(M, K, base + 10 * c + i) for i, (M, K) in enumerate(SHAPES)] for c in range(COPIES)]
 
     # ---- end to end through the reference-facing C ABI (host buffers) ----
+    P4 = None  # the packed device copies are not needed any more
     L = native.lib()
     host_w = []
     for c in range(COPIES):
@@ -452,12 +492,12 @@ def main():
         host_w.append(row)
     del W4
     torch.cuda.empty_cache()
-    hx = {K: torch.from_numpy(xs[K].cpu().numpy()).pin_memory() for K in xs}
-    hy = {M: torch.empty(M, dtype=torch.float32).pin_memory() for M in ys}
+    hx = [torch.from_numpy(x.cpu().numpy()).pin_memory() for x in xs]
+    hy = [torch.empty(y.numel(), dtype=torch.float32).pin_memory() for y in ys]
 
     def e2e_step(c):
-        for hq, hs, M, K in host_w[c]:
-            L.asm_matmul_q4(hq.ctypes.data, hs.ctypes.data, hx[K].data_ptr(), hy[M].data_ptr(), M, K)
+        for i, (hq, hs, M, K) in enumerate(host_w[c]):
+            L.asm_matmul_q4(hq.ctypes.data, hs.ctypes.data, hx[i].data_ptr(), hy[i].data_ptr(), M, K)
 
     for i in range(6):
         e2e_step(i % COPIES)
@@ -713,12 +753,15 @@ def main():
         "config": {
             "workload": "Q4_0xQ8_0 matvec sweep: 4096x4096, 11008x4096, 4096x11008, 32000x4096, batch 1",
             "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-            "weights_layout": "resident qs[M][K/32][16] + fp16 scales (18 B/block)",
+            "weights_layout": ("resident packed rows: each row's nibbles then its fp16 scales (18 B/block)"
+                               if args.layout == "packed" else "resident qs[M][K/32][16] + fp16 scale plane (18 B/block)"),
             "l2": f"rotating {COPIES} weight copies, {COPIES * step_bytes / 1e6:.0f} MB working set > 126 MB L2",
-            "launch": "CUDA graph replay of %d steps (%d matvecs), PDL between kernels" % (G, G * len(SHAPES)),
-            "quantize": "separate activation-image kernel per matvec" if args.mode == "image"
-                        else (f"inside each matvec kernel; the library's own pre-pass kernel for K >= {image_min_k}"
-                              if image_min_k else "inside each matvec kernel (fused)"),
+            "launch": ("CUDA graph replay of %d steps (%d matvecs), PDL between kernels; " % (G, G * len(SHAPES))
+                       + ("independent launches (ASM_MV_INDEPENDENT: every matvec has its own x and y, so "
+                          "consecutive ones overlap)" if args.chain == "independent"
+                          else "dependent launches (each waits for the previous kernel)")),
+            "quantize": ("inside each matvec kernel" if not prepass else
+                         f"inside each matvec kernel; the library's own pre-pass kernel for K >= {image_min_k}"),
         },
         "roofline": {
             "bound": "hbm",
@@ -775,6 +818,22 @@ def main():
                                                    + bt["kv_bytes_per_step_avg"]), 1)
         line["decode_70b"] = decode70
     line.update(extras)
+    # compact summary last, so a reader of the line's tail sees the headline figures
+    summ = {"sweep_GB/s": line["value"], "sweep_frac": line["roofline"]["frac"], "e2e_GB/s": line["e2e"]["value"]}
+    if "config0" in line:
+        c0 = line["config0"]
+        summ["config0"] = {k: c0[k]["frac"] for k in ("independent", "dependent") if k in c0}
+        summ["config0_us"] = {k: c0[k]["us"] for k in ("independent", "dependent") if k in c0}
+        summ["floor_us"] = c0.get("floor_us_per_launch")
+    if decode is not None:
+        summ["decode_7b"] = {"tokens_per_s": decode["tokens_per_s"], "frac": decode["frac_of_measured_hbm"],
+                             "engine": decode["engine"]}
+    if decode70 is not None:
+        summ["decode_70b"] = {"tp": decode70["tensor_parallel"], "tokens_per_s": decode70["tokens_per_s"],
+                              "batch32_tokens_per_s": decode70.get("batch", {}).get("tokens_per_s")}
+        if "tp_parity" in decode70:
+            summ["tp_parity"] = decode70["tp_parity"]
+    line["summary"] = summ
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -244,6 +244,33 @@ ASMLLM_API int asm_matmul_q8_async(const int8_t* qweights, const float* scales,
 ASMLLM_API int asm_matvec_ex_async(int fmt, const void* qweights, const void* scales, int scales_are_f16,
                                    const float* x, float* y, int64_t M, int64_t K, unsigned flags,
                                    void* stream);
+/* ---- Packed rows: the resident layout the bulk-copy matvec streams best ----
+ * Row r of a packed matrix is its K/32 quant blocks (16 bytes per Q4_0
+ * block, 32 per Q8_0) followed by its K/32 fp16 scales: the same 18 (34)
+ * bytes per block as GGUF, but R consecutive rows form one contiguous range,
+ * fetched by a single bulk copy.  K must be a multiple of 256.
+ * asm_packed_row_bytes: bytes of one packed row (-1 if fmt or K is invalid).
+ * asm_pack_rows_async: device qweights + fp16 scales -> device packed rows
+ * (all 16-byte aligned).  asm_matvec_packed_async: Q4_0 / Q8_0 x Q8_0 on
+ * packed rows, same result as asm_matmul_q4_f16s_async /
+ * asm_matmul_q8q8_f16s_async on the planes; flags as asm_matvec_ex_async.
+ * Host weights registered with asm_weights_register are kept packed when
+ * their scales are fp16-exact and K is a multiple of 256; the fp32-activation
+ * entries (asm_matmul_q4_avx512, asm_matmul_q4_f32, asm_matmul_q8) then stage
+ * those host weights per call instead of using the resident copy.  No
+ * counterpart in the reference (its kernels read the two planes). */
+ASMLLM_API int64_t asm_packed_row_bytes(int fmt, int64_t K);
+/* Measurement aid: enqueues n empty kernels (one CTA per SM) chained the way
+ * the matvecs chain -- programmatic dependent launch when pdl != 0, each
+ * kernel triggering its dependents at entry and, when wait != 0, waiting for
+ * the previous kernel (griddepcontrol.wait).  Timing such a chain gives the
+ * per-launch dependency floor a chain of dependent matvecs cannot go below.
+ * No counterpart in the reference. */
+ASMLLM_API int asm_launch_floor_async(int32_t n, int32_t pdl, int32_t wait, void* stream);
+ASMLLM_API int asm_pack_rows_async(int fmt, const void* qweights, const uint16_t* scales_f16, void* packed,
+                                   int64_t M, int64_t K, void* stream);
+ASMLLM_API int asm_matvec_packed_async(int fmt, const void* packed, const float* x, float* y, int64_t M,
+                                       int64_t K, unsigned flags, void* stream);
 /* Batched quantize: N rows of x fp32[N][K] -> xq int8[N][K], xd fp32[N][K/32]. */
 ASMLLM_API int asm_quantize_q8_0_async(const float* x, int8_t* xq, float* xd,
                                        int64_t N, int64_t K, void* stream);
@@ -565,7 +592,8 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * register-streaming kernels.  "pdl": programmatic dependent launch on/off.
  * "image_min_k": Q8_0-activation matvecs given fp32 x with K >= this value
  * quantize x in a separate pre-pass kernel into stream-ordered scratch
- * instead of in every CTA (default 8192; 0 = always in the CTAs).
+ * instead of in every CTA (default 0 = always in the CTAs: with the per-warp
+ * ring kernel the pre-pass measured slower at K = 11008 and 28672).
  * "gemm_splits": 0 = the batched product picks its K split (default),
  * S >= 1 = exactly S ranges (clamped to [1, 8] and to the number of 128-byte
  * weight stages).  Results are identical either way up to fp32 summation
@@ -578,7 +606,14 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * ring slots of each warp (0 = automatic up to 6, default); "mv_smem_kb"
  * shared-memory budget of a CTA in KB (default 110, which leaves room on
  * every SM for a CTA of the next launch; a plan that does not fit takes the
- * whole opt-in shared memory); "mv_ctas" CTAs per SM (default 1). */
+ * whole opt-in shared memory); "mv_ctas" CTAs per SM (default 1).
+ * "mv_kernel": which bulk-copy kernel streams a matvec: 0 (default) = rows of
+ * more than 128 blocks in launches that wait for the previous kernel go to the
+ * row-stage kernel (one producer warp, ~16 KB stages of whole rows shared by
+ * 16 warps), everything else to the warp-ring kernel; 1 = warp rings always;
+ * 2 = row stages wherever they apply (not packed rows, not independent
+ * launches).  The two kernels add a row's products in different fixed orders,
+ * so y may differ in the last bits between settings (each is deterministic). */
 ASMLLM_API int asm_set_option(const char* name, int value);
 
 /* Largest K each matvec family supports (shared-memory staging of x). */

@@ -278,6 +278,7 @@ int device_in(DeviceState& st, int dev, const void* p, size_t bytes, int slot, c
 // activation pre-pass; bit 1: pinned host y written in place by the matvec.
 // A cleared bit stages that buffer with a copy instead.
 std::atomic<int> g_opt_sync_map{3};
+std::atomic<int> g_opt_xchg_wait_us{0};  // 0 = the default exchange wait limit (about a second)
 
 bool sync_fused() {
   static const bool v = [] {
@@ -1248,6 +1249,90 @@ ASMLLM_API int asm_matvec_packed_async(int fmt, const void* packed, const float*
   return ASM_OK;
 }
 
+ASMLLM_API int asm_matvec_rowsplit_async(int fmt, const void* qweights, const uint16_t* scales_f16, const float* x,
+                                         float* y_full, int64_t M, int64_t K, int32_t tp, int32_t rank,
+                                         void* const* xchg, uint32_t* seq, unsigned flags, void* stream) {
+  const char* name = "asm_matvec_rowsplit_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (flags & ~(unsigned)(ASM_MV_INDEPENDENT | ASM_MV_PACKED))
+    return set_error(ASM_E_INVALID, "%s: unknown flags 0x%x", name, flags);
+  if (tp < 1 || tp > kMaxTp || rank < 0 || rank >= tp)
+    return set_error(ASM_E_INVALID, "%s: tp=%d rank=%d (need 1 <= tp <= %d, 0 <= rank < tp)", name, tp, rank, kMaxTp);
+  const bool packed = (flags & ASM_MV_PACKED) != 0;
+  int rc = validate(name, qweights, packed ? qweights : (const void*)scales_f16, x, y_full, M, K);
+  if (rc) return rc;
+  if (M == 0) return ASM_OK;
+  if (packed && K % 256 != 0) return set_error(ASM_E_INVALID, "%s: K=%lld is not a multiple of 256", name, (long long)K);
+  if ((rc = require_device(name, qweights, "qweights")) || (!packed && (rc = require_device(name, scales_f16, "scales"))) ||
+      (rc = require_device(name, x, "x")) || (rc = require_device(name, y_full, "y_full")))
+    return rc;
+  if (!seq) return set_error(ASM_E_INVALID, "%s: seq is null", name);
+  if ((rc = require_device(name, seq, "seq"))) return rc;
+  MvFuse fz;
+  fz.tp = tp;
+  fz.tp_rank = rank;
+  fz.xchg_rows = (int)M;
+  fz.ar_seq = seq;
+  for (int r = 0; r < tp; ++r) {
+    if (r == rank) continue;
+    if (!xchg || !xchg[r]) return set_error(ASM_E_INVALID, "%s: gather buffer of rank %d is null", name, r);
+    fz.xchg[r] = static_cast<unsigned long long*>(xchg[r]);
+  }
+  if (M > INT32_MAX / kMaxTp) return set_error(ASM_E_INVALID, "%s: M=%lld too large", name, (long long)M);
+  MatvecArgs a;
+  a.fmt = fmt;
+  a.packed = packed;
+  a.scales_f16 = true;
+  a.w = qweights;
+  a.scales = packed ? nullptr : scales_f16;
+  a.x = x;
+  a.y = y_full;
+  a.M = M;
+  a.K = K;
+  a.epi = kEpiGather;
+  a.fuse = &fz;
+  const size_t wbytes = packed ? (size_t)M * (size_t)asm_packed_row_bytes(fmt, K)
+                               : (size_t)M * (size_t)(K / 32) * (fmt == kFmtQ4_0 ? 16 : 32);
+  a.weights_static = is_static(qweights, wbytes);
+  a.act_independent = (flags & ASM_MV_INDEPENDENT) != 0;
+  const cudaError_t e = launch_matvec(a, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorNotSupported)
+    return set_error(ASM_E_UNSUPPORTED, "%s: no bulk-copy plan for M=%lld K=%lld", name, (long long)M, (long long)K);
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
+ASMLLM_API int asm_rowsplit_wait_async(const asm_rowsplit_wait_t* w, void* stream) {
+  const char* name = "asm_rowsplit_wait_async";
+  if (!w) return set_error(ASM_E_INVALID, "%s: null descriptor", name);
+  if (w->n < 0 || w->n > 8) return set_error(ASM_E_INVALID, "%s: n=%d is not in [0, 8]", name, w->n);
+  if (w->tp < 1 || w->tp > kMaxTp || w->rank < 0 || w->rank >= w->tp)
+    return set_error(ASM_E_INVALID, "%s: tp=%d rank=%d", name, w->tp, w->rank);
+  if (w->tp == 1 || w->n == 0) return ASM_OK;  // nothing crosses ranks
+  int rc;
+  if (!w->seq || !w->done) return set_error(ASM_E_INVALID, "%s: seq and done must be set", name);
+  if ((rc = require_device(name, w->seq, "seq")) || (rc = require_device(name, w->done, "done"))) return rc;
+  RowsplitWait k;
+  k.n = w->n;
+  k.tp = w->tp;
+  k.rank = w->rank;
+  k.seq = w->seq;
+  k.done = w->done;
+  for (int j = 0; j < w->n; ++j) {
+    if (w->M[j] <= 0 || w->M[j] > INT32_MAX / kMaxTp) return set_error(ASM_E_INVALID, "%s: M[%d]=%lld", name, j, (long long)w->M[j]);
+    if ((rc = require_device(name, w->own[j], "own")) || (rc = require_device(name, w->y_full[j], "y_full"))) return rc;
+    k.own[j] = static_cast<const unsigned long long*>(w->own[j]);
+    k.y_full[j] = w->y_full[j];
+    k.M[j] = w->M[j];
+  }
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const cudaError_t e = launch_rowsplit_wait(k, sms > 0 ? sms : 1, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
 ASMLLM_API int asm_matmul_q8q8_async(const int8_t* qweights, const float* scales, const float* x,
                                      float* y, int64_t M, int64_t K, void* stream) {
   return async_matvec("asm_matmul_q8q8_async", kFmtQ8_0, false, false, qweights, scales, x, y,
@@ -1896,6 +1981,16 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (strcmp(name, "mv_smem_kb") == 0) return g_opt_mv_smem_kb.exchange(value <= 0 ? 0 : value < 16 ? 16 : value);
   if (strcmp(name, "mv_ctas") == 0) return g_opt_mv_ctas.exchange(value < 1 ? 1 : value > 4 ? 4 : value);
   if (strcmp(name, "mv_kernel") == 0) return g_opt_mv_kernel.exchange(value == 1 || value == 2 ? value : 0);
+  if (strcmp(name, "xchg_wait_us") == 0) {
+    // SM clock cycles at about 2 GHz; set on the current device
+    const int v = value < 0 ? 0 : value;
+    const cudaError_t e = set_xchg_wait_cycles(v > 0 ? (long long)v * 2000LL : 0LL);
+    if (e != cudaSuccess) {
+      cuda_error(e, "asm_set_option(xchg_wait_us)");
+      return -1;
+    }
+    return g_opt_xchg_wait_us.exchange(v);
+  }
   set_error(ASM_E_INVALID, "asm_set_option: unknown option '%s'", name);
   return -1;
 }

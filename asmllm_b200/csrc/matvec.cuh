@@ -24,6 +24,8 @@ constexpr int kEpiResidual = 1;  // y[r] += v (y is the residual stream)
 constexpr int kEpiSwiglu = 2;    // rows (2i, 2i+1) = (gate_i, up_i): h_i = silu(gate_i) * up_i,
                                  // quantized to Q8_0 into image_out block by block
 constexpr int kEpiArgmax = 3;    // y[r] = v, then the next token = argmax over all rows
+constexpr int kEpiGather = 4;    // row-split: y[tp_rank * M + r] = v here, and (seq, v) to every
+                                 // other rank's gather buffer (completed by launch_rowsplit_wait)
 
 struct MvFuse {
   const float* norm_w = nullptr;  // kProNorm: weight [K]
@@ -99,6 +101,25 @@ struct MatvecArgs {
 constexpr unsigned kErrRingTimeout = 1u;  // a shared-memory ring barrier wait gave up
 constexpr unsigned kErrDecodeRange = 2u;  // decode position or token id out of range: step skipped
 constexpr unsigned kErrXchgTimeout = 4u;  // a tensor-parallel exchange wait gave up (a peer never wrote)
+
+// Limit of every exchange / gather wait on the current device, in SM clock
+// cycles (0 = the default, about a second).
+cudaError_t set_xchg_wait_cycles(long long cycles);
+
+// Completion of a step of row-split matvecs (kEpiGather): waits until every
+// peer's rows of each of the n matvecs carry this step's sequence number in
+// this rank's gather buffers, copies them into the full outputs, and advances
+// the step counter.  own[j] = this rank's gather buffer of matvec j ([2][tp][M[j]]
+// words), y_full[j] = its [tp * M[j]] output.
+struct RowsplitWait {
+  int n = 0, tp = 1, rank = 0;
+  const unsigned long long* own[8] = {};
+  float* y_full[8] = {};
+  long long M[8] = {};
+  unsigned* seq = nullptr;   // step counter (same on every rank)
+  unsigned* done = nullptr;  // CTAs finished; zero on entry, left zero
+};
+cudaError_t launch_rowsplit_wait(const RowsplitWait& w, int sms, cudaStream_t stream);
 
 // Bytes of one row of the Q8_0 activation image for nb = K/32 blocks:
 // nb 48-byte slots (32 int8 + 16 pad) then nb (d, qsum) float pairs, rounded to 16.

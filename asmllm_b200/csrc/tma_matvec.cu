@@ -94,6 +94,9 @@ __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned lon
   return v;
 }
 
+// Limit of an exchange wait in SM clock cycles (asm_set_option "xchg_wait_us").
+__device__ long long g_xchg_wait_cycles = kWaitCycles;
+
 // The payload of the exchange word at p once it carries sequence seq; bounded
 // (a peer that never writes sets the error bit and yields 0; after one
 // timeout, `ok` makes the caller's later waits return at once).
@@ -101,10 +104,12 @@ __device__ __forceinline__ unsigned xchg_wait(const unsigned long long* p, unsig
   unsigned long long v = ld_volatile_u64(p);
   if ((unsigned)(v >> 32) == seq) return (unsigned)v;
   if (!ok) return 0u;
+  const long long limit = g_xchg_wait_cycles;
   const long long t0 = clock64();
   do {
+    __nanosleep(32);  // leave issue slots to the kernels running beside the waiting one
     v = ld_volatile_u64(p);
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       ok = false;
       raise_device_error(kErrXchgTimeout);
       return 0u;
@@ -317,7 +322,8 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   // tensor-parallel residual exchange take one contiguous range per CTA.
   const int n_g = (M + RS - 1) / RS;
   const int G = (int)gridDim.x, cta = (int)blockIdx.x;
-  const bool stride = EPI == kEpiStore || EPI == kEpiArgmax || (EPI == kEpiResidual && fz.tp <= 1);
+  const bool stride = EPI == kEpiStore || EPI == kEpiArgmax || EPI == kEpiGather ||
+                      (EPI == kEpiResidual && fz.tp <= 1);
   const int g0 = (int)((long long)n_g * cta / G), g1 = (int)((long long)n_g * (cta + 1) / G);
   const int nq = stride ? (cta < n_g ? (n_g - 1 - cta) / G + 1 : 0) : g1 - g0;
   const int r0 = g0 * RS, r1 = min(M, g1 * RS);  // the contiguous range (SwiGLU, exchange)
@@ -623,6 +629,8 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
           } else {
             y[row] = __fadd_rn(__ldcg(y + row), v);
           }
+        } else if (EPI == kEpiGather) {
+          y[(size_t)fz.tp_rank * M + row] = v;  // this rank's row of the full output (to the peers below)
         } else {
           y[row] = v;
           if (EPI == kEpiArgmax && v == v) {
@@ -668,6 +676,30 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       for (int i = 0; i < kNcw; ++i) mx = wbest[i] > mx ? wbest[i] : mx;
       if (mx) atomicMax(fz.best, mx);
       argmax_arrive(fz, gridDim.x, seq);
+    }
+  }
+  if (EPI == kEpiGather && fz.tp > 1) {
+    // This CTA's rows go to every other rank's gather buffer only once the
+    // previous kernel in the stream has completed.  By induction a rank's
+    // stores of step t then follow its wait kernel of step t - 1, which
+    // followed every peer's stores of step t - 1, which followed each peer's
+    // wait of step t - 2: no rank overwrites a parity a peer still reads.
+    // The step number is read after that wait, when the counter is final.
+    __syncthreads();  // every warp's rows are in y
+    unsigned* s_seq = reinterpret_cast<unsigned*>(part);
+    if (threadIdx.x == 0) {
+      pdl_wait();
+      *s_seq = __ldcg(fz.ar_seq) + 1u;
+    }
+    __syncthreads();
+    const unsigned gseq = *s_seq;
+    for (int i = threadIdx.x; i < nq * RS; i += NCT) {
+      const int q = i / RS, row = group_of(q) * RS + (i - q * RS);
+      if (row >= M) continue;
+      const unsigned long long wv =
+          ((unsigned long long)gseq << 32) | __float_as_uint(__ldcg(y + (size_t)fz.tp_rank * M + row));
+      for (int t = 0; t < fz.tp; ++t)
+        if (t != fz.tp_rank) st_volatile_u64(xchg_word(fz, fz.xchg[t], gseq, fz.tp_rank, row), wv);
     }
   }
   if (EPI == kEpiResidual && fz.tp > 1) {
@@ -935,6 +967,11 @@ cudaError_t launch_tma_fused(const MatvecArgs& a, const TmaPlan& p, int sms, cud
 
 template <int FMT, int RS, int XR, int NBQ>
 cudaError_t launch_tma_r(const MatvecArgs& a, const TmaPlan& p, int sms, cudaStream_t stream, bool pdl) {
+  if (a.epi == kEpiGather) {  // row-split: fp32 x, fp16 scales (planes or packed rows)
+    if (a.image || prologue_of(a) != kProQuant) return cudaErrorNotSupported;
+    return a.packed ? launch_tma_t<FMT, true, false, kProQuant, kEpiGather, RS, XR, NBQ, true>(a, p, sms, stream, pdl)
+                    : launch_tma_t<FMT, true, false, kProQuant, kEpiGather, RS, XR, NBQ>(a, p, sms, stream, pdl);
+  }
   if (is_fused(a)) return launch_tma_fused<FMT, RS, XR, NBQ>(a, p, sms, stream, pdl);
   const bool fused = a.image == nullptr;
   if (a.packed) {
@@ -1006,7 +1043,7 @@ namespace {
 // 1 = warp rings always, 2 = row stages wherever they apply.
 bool use_rows(const MatvecArgs& a, int smem_optin, RowsPlan* rp) {
   const int mode = g_opt_mv_kernel.load();
-  if (mode == 1 || a.packed || a.act_independent) return false;
+  if (mode == 1 || a.packed || a.act_independent || a.epi == kEpiGather) return false;
   if (mode == 0 && a.K / QK <= 128) return false;
   if (!rows_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, rp)) return false;
   if (a.epi == kEpiSwiglu && rp->R < 2) return false;
@@ -1021,6 +1058,13 @@ bool tma_matvec_supported(const MatvecArgs& a, int smem_optin) {
   // are multiples of 16 by the plan; the planes' bases must be too).
   if ((uintptr_t)a.w % 16 != 0 || (!a.packed && (uintptr_t)a.scales % 16 != 0)) return false;
   if (a.image && (uintptr_t)a.image % 16 != 0) return false;
+  if (a.epi == kEpiGather) {  // row-split: fp32 x and fp16 scales only, any chain mode
+    if (a.isums || a.image || !(a.packed || a.scales_f16) || prologue_of(a) != kProQuant) return false;
+    if (!a.fuse || a.fuse->tp < 1 || a.fuse->tp > kMaxTp || a.fuse->tp_rank < 0 || a.fuse->tp_rank >= a.fuse->tp)
+      return false;
+    TmaPlan p;
+    return plan_of(a, smem_optin, &p);
+  }
   if (a.packed && (a.isums || is_fused(a))) return false;
   RowsPlan rp;
   if (use_rows(a, smem_optin, &rp)) {
@@ -1048,6 +1092,69 @@ cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cuda
   if (!plan_of(a, smem_optin, &p)) return cudaErrorInvalidValue;
   if (a.fmt == kFmtQ4_0) return launch_tma_fmt<kFmtQ4_0>(a, p, sms, stream, pdl);
   return launch_tma_fmt<kFmtQ8_0>(a, p, sms, stream, pdl);
+}
+
+// ---------------------------------------------------------- row-split wait
+// One thread per (matvec, peer rank, row) word: spin (bounded) until the word
+// carries this step's sequence, store its value into the full output.  The
+// last CTA advances the step counter.  The next step's matvecs may start
+// (and compute) while this kernel waits; they read the counter and store to
+// the peers only after it has completed (see the kEpiGather epilogue).
+__global__ void __launch_bounds__(256) rowsplit_wait_kernel(const RowsplitWait w) {
+  pdl_trigger();
+  pdl_wait();  // this rank's matvecs of the step are done
+  const unsigned seq = __ldcg(w.seq) + 1u;
+  bool ok = true;
+  for (int j = 0; j < w.n; ++j) {
+    const long long M = w.M[j];
+    const long long total = M * w.tp;  // words of all source ranks (own rows skipped)
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+      const int src = (int)(i / M);
+      if (src == w.rank) continue;
+      const long long row = i - (long long)src * M;
+      const unsigned long long* word = w.own[j] + ((size_t)(seq & 1u) * w.tp + src) * (size_t)M + row;
+      w.y_full[j][(size_t)src * M + row] = __uint_as_float(xchg_wait(word, seq, ok));
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(w.done, 1u) == gridDim.x - 1) {
+      *w.seq = seq;
+      atomicExch(w.done, 0u);
+    }
+  }
+}
+
+cudaError_t launch_rowsplit_wait(const RowsplitWait& w, int sms, cudaStream_t stream) {
+  if (w.n < 0 || w.n > 8 || w.tp < 1 || w.tp > kMaxTp || w.rank < 0 || w.rank >= w.tp || !w.seq || !w.done)
+    return cudaErrorInvalidValue;
+  long long words = 0;
+  for (int j = 0; j < w.n; ++j) {
+    if (w.M[j] <= 0 || !w.own[j] || !w.y_full[j]) return cudaErrorInvalidValue;
+    words += w.M[j] * (w.tp - 1);
+  }
+  long long grid = (words + 255) / 256;
+  if (grid > sms) grid = sms;
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RowsplitWait a = w;
+  void* args[] = {(void*)&a};
+  return cudaLaunchKernelExC(&cfg, (const void*)rowsplit_wait_kernel, args);
+}
+
+cudaError_t set_xchg_wait_cycles(long long cycles) {
+  const long long v = cycles > 0 ? cycles : kWaitCycles;
+  return cudaMemcpyToSymbol(g_xchg_wait_cycles, &v, sizeof(v));
 }
 
 cudaError_t set_device_error_mirror(unsigned* host_mapped) {

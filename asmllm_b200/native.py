@@ -26,8 +26,8 @@ vp, i64, c_int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
 i32, f32 = ctypes.c_int32, ctypes.c_float
 
 # Epilogues of asm_fused_matvec_async (ASM_EPI_*) and device error bits.
-EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_ARGMAX = 0, 1, 2, 3
-DEVERR_RING_TIMEOUT, DEVERR_DECODE_RANGE = 1, 2
+EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU, EPI_ARGMAX, EPI_GATHER = 0, 1, 2, 3, 4
+DEVERR_RING_TIMEOUT, DEVERR_DECODE_RANGE, DEVERR_XCHG_TIMEOUT = 1, 2, 4
 
 
 class FusedMatvec(ctypes.Structure):
@@ -42,6 +42,12 @@ class FusedMatvec(ctypes.Structure):
         ("tp", i32), ("tp_rank", i32), ("xchg_rows", i32), ("vocab_offset", i32),
         ("xchg", vp * 8), ("ar_seq", vp), ("ar_done", vp),
     ]
+
+
+class RowsplitWait(ctypes.Structure):
+    """asm_rowsplit_wait_t (include/asmllm.h)."""
+    _fields_ = [("n", i32), ("tp", i32), ("rank", i32), ("own", vp * 8), ("y_full", vp * 8), ("M", i64 * 8),
+                ("seq", vp), ("done", vp)]
 
 
 class DecodeLayer(ctypes.Structure):
@@ -113,6 +119,9 @@ SIGNATURES = {
     "asm_launch_floor_async": ([i32, i32, i32, vp], c_int),
     "asm_pack_rows_async": ([c_int, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matvec_packed_async": ([c_int, vp, vp, vp, i64, i64, ctypes.c_uint, vp], c_int),
+    "asm_matvec_rowsplit_async": ([c_int, vp, vp, vp, vp, i64, i64, i32, i32, ctypes.POINTER(vp), vp,
+                                   ctypes.c_uint, vp], c_int),
+    "asm_rowsplit_wait_async": ([ctypes.POINTER(RowsplitWait), vp], c_int),
     "asm_matmul_q8q8_f16s_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q4_f32_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_matmul_q8_async": ([vp, vp, vp, vp, i64, i64, vp], c_int),

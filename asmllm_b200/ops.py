@@ -23,6 +23,7 @@ from . import native
 from .native import FMT_Q4_0, FMT_Q8_0, AsmError
 
 MV_INDEPENDENT = 1  # ASM_MV_INDEPENDENT (include/asmllm.h)
+MV_PACKED = 2  # ASM_MV_PACKED
 
 # --------------------------------------------------------------------------
 # Host (numpy) layer: the reference-facing synchronous ABI

@@ -332,9 +332,33 @@ def main():
         for i, w in enumerate(W[c] if W is not None else weights(c)):
             one_matvec(fmt, w, i, chain=chain, mode=mode)
 
+    # N > 1: the sweep's matrices are row-split over the ranks -- rank r holds rows
+    # [r*M, (r+1)*M) of each (N*M) x K matrix (per-GPU work fixed: weak scaling) --
+    # and every matvec's y is all-gathered: each finished row is stored by the
+    # matvec kernel into every rank's gather buffer over NVLink, and one wait
+    # kernel per step completes the full y on each rank.
+    rs, yfull = None, None
+    if world > 1:
+        from asmllm_b200.rowsplit import RowSplitGroup
+
+        rs = RowSplitGroup([M for M, _ in SHAPES], world, rank)
+        yfull = [torch.empty(world * M, device=dev) for M, _ in SHAPES]
+
+    def headline_step(c):
+        if rs is None:
+            step(c)
+            return
+        indep = args.chain == "independent"
+        for i, w in enumerate(weights(c)):
+            if isinstance(w, tuple):
+                rs.matvec(i, FMT_Q4_0, w[0], xs[i], yfull[i], scales=w[1], independent=indep)
+            else:
+                rs.matvec(i, FMT_Q4_0, w, xs[i], yfull[i], independent=indep)
+        rs.wait()
+
     # warm-up: eager steps (also primes the library's launch caches)
     for i in range(max(3, args.warmup)):
-        step(i % COPIES)
+        headline_step(i % COPIES)
     torch.cuda.synchronize()
 
     def capture(nsteps, fn):
@@ -354,8 +378,8 @@ def main():
     if G >= COPIES:
         G -= G % COPIES
     reps, rem = divmod(K_steps, G)
-    gA = capture(G, step)
-    gB = capture(rem, step) if rem else None
+    gA = capture(G, headline_step)
+    gB = capture(rem, headline_step) if rem else None
     gA.replay()  # untimed
     torch.cuda.synchronize()
 
@@ -394,12 +418,31 @@ def main():
     ops.set_option("image_min_k", image_min_k)
     prepass = args.layout == "planes" and args.chain == "dependent"
     launches = K_steps * sum(2 if prepass and image_min_k and K >= image_min_k else 1 for _, K in SHAPES)
+    if rs is not None:
+        launches += K_steps  # the gather's wait kernel, once per step
     # The matvec is the dominant kernel; per-launch figures are per matvec
     # (its quantize pre-pass, when separate, is counted inside the time).
     per_launch_ms = ms / (len(SHAPES) * K_steps)
     per_launch_bytes = step_bytes / len(SHAPES)
     achieved = per_launch_bytes / (per_launch_ms / 1e3) / 1e9
     del gA, gB
+    rowsplit_check = None
+    if rs is not None:
+        # one more step on copy 0, then every rank's full y against the ranks' own
+        # plain matvecs gathered by NCCL: the same bits, row for row
+        headline_step(0)
+        torch.cuda.synchronize()
+        bit_equal, err_bits = True, ops.device_error()
+        for i, w in enumerate(weights(0)):
+            mine = (ops.matvec(FMT_Q4_0, *w, xs[i], independent=True) if isinstance(w, tuple)
+                    else ops.matvec_packed(FMT_Q4_0, w, xs[i]))
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            dist.all_gather(parts, mine)
+            bit_equal = bit_equal and bool(torch.equal(torch.cat(parts), yfull[i]))
+        ok = torch.tensor([1 if bit_equal and err_bits == 0 else 0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        rowsplit_check = {"gathered_y_equals_plain_matvecs": bool(ok.item()), "device_error": err_bits,
+                          "rows_per_rank": [M for M, _ in SHAPES], "ranks": world}
 
     # ---- breakdowns (not part of the timed value) ----
     extras = {}
@@ -438,7 +481,7 @@ def main():
                     "kernels chained the same way")
     extras["config0"] = cfg0
 
-    if not args.no_extras:
+    if not args.no_extras and world == 1:
         for layout in ("packed", "planes"):
             for chain in ("independent", "dependent"):
                 per_shape = {}
@@ -703,7 +746,7 @@ def main():
                 dist.all_reduce(tt, op=dist.ReduceOp.MAX)
                 tb = float(tt.item())
             kvb = B70 * kv70
-            decode70["batch"] = {
+            decode70["batched"] = {
                 "batch": B70, "tokens_per_s": round(B70 * n70 / (tb / 1e3), 1),
                 "ms_per_step": round(tb / n70, 4), "greedy_steps": n70, "prompt_tokens": 16,
                 "engine": "CUDA graphs of per-operation launches; tcgen05 batched product per projection, "
@@ -719,6 +762,50 @@ def main():
         dec.close()
         del dec
         torch.cuda.empty_cache()
+
+    # ---- TP parity: one teacher-forced step of the N-rank decoder against one GPU ----
+    # A one-layer model of the 70B widths (the same weights at every N: they are
+    # generated per head / FFN chunk / vocabulary chunk); the whole sequence is the
+    # prompt, so both sides see the same tokens.  Rank 0 gathers the ranks'
+    # vocabulary slices of the logits and compares them with its own 1-GPU model.
+    tp_parity = None
+    if world > 1:
+        from asmllm_b200 import decode as D
+
+        s70 = D.LLAMA2_70B
+        shp = D.LlamaShape(n_layers=1, dim=s70.dim, n_heads=s70.n_heads, n_kv_heads=s70.n_kv_heads,
+                           head_dim=s70.head_dim, ffn=s70.ffn, vocab=s70.vocab)
+        seq = [3, 141, 59, 26, 53, 58, 97, 93]
+        tdec = D.LlamaDecoder(shp, ctx=32, seed=21, tp=world, tp_rank=rank, group=None)
+        toks = tdec.generate(seq, 1, engine="graph")
+        mine = (list(toks), tdec.logits.float().cpu().numpy(), ops.device_error())
+        tdec.close()
+        del tdec
+        parts = [None] * world
+        dist.all_gather_object(parts, mine)
+        if rank == 0:
+            ref = D.LlamaDecoder(shp, ctx=32, seed=21)
+            rtoks = list(ref.generate(seq, 1, engine="graph"))
+            rl = ref.logits.float().cpu().numpy()
+            rerr = ops.device_error()
+            ref.close()
+            del ref
+            logits = np.concatenate([p[1] for p in parts])
+            err = float(np.abs(logits - rl).max() / np.abs(rl).max())
+            top2 = np.sort(rl)[-2:]
+            tp_parity = {
+                "max_rel_err": round(err, 7), "tolerance": 2e-2, "within_tolerance": err <= 2e-2,
+                "tokens_equal": all(p[0] == rtoks for p in parts),
+                "ranks_agree": all(p[0] == parts[0][0] for p in parts),
+                "top2_margin_rel": round(float((top2[1] - top2[0]) / np.abs(rl).max()), 6),
+                "device_error": max([p[2] for p in parts] + [rerr]),
+                "model": "1 layer of the 70B widths (d 8192, 64 q / 8 KV heads, FFN 28672, vocab 32000), "
+                         f"{len(seq)}-token teacher-forced prompt; logits of the last position",
+            }
+        torch.cuda.empty_cache()
+        dist.barrier()
+    if rs is not None:
+        rs.close()
 
     if rank != 0:
         if world > 1:
@@ -752,7 +839,11 @@ def main():
         "data": "synthetic (seeded; GGUF Q4_0 d=fp16|N(0,0.02)|, nibbles U[0,15]; x N(0,1))",
         "config": {
             "workload": "Q4_0xQ8_0 matvec sweep: 4096x4096, 11008x4096, 4096x11008, 32000x4096, batch 1",
-            "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+            "parallelism": (f"row-split x{world}: rank r holds rows [r*M, (r+1)*M) of each {world}*M x K matrix "
+                            "(M, K as in the workload: per-GPU work fixed) and every y is all-gathered -- each "
+                            "finished row is stored by the matvec kernel into every rank's gather buffer over "
+                            "NVLink (64-bit sequence-tagged words, peer stores), then one wait kernel per step "
+                            "completes the full y on every rank" if world > 1 else "single GPU"),
             "weights_layout": ("resident packed rows: each row's nibbles then its fp16 scales (18 B/block)"
                                if args.layout == "packed" else "resident qs[M][K/32][16] + fp16 scale plane (18 B/block)"),
             "l2": f"rotating {COPIES} weight copies, {COPIES * step_bytes / 1e6:.0f} MB working set > 126 MB L2",
@@ -780,6 +871,10 @@ def main():
         "gpu_launches": launches,
         "clocks": clk,
     }
+    if rowsplit_check is not None:
+        line["rowsplit_check"] = rowsplit_check
+    if tp_parity is not None:
+        line["tp_parity"] = tp_parity
     if decode is not None:
         decode["frac_of_measured_hbm"] = round(decode["achieved_GB/s"] / peak, 4)
         decode["roofline_tokens_per_s"] = round(peak * 1e9 / (decode["weight_bytes_per_token"]
@@ -810,8 +905,8 @@ def main():
         # every GPU streams its 1/N of the weights and KV per token at the measured copy peak
         decode70["roofline_tokens_per_s"] = round(
             peak * 1e9 * world / (decode70["weight_bytes_per_token_per_gpu"] * world + decode70["kv_bytes_per_token_avg"]), 2)
-        if "batch" in decode70:
-            bt = decode70["batch"]
+        if "batched" in decode70:
+            bt = decode70["batched"]
             bt["frac_of_measured_hbm"] = round(bt["achieved_GB/s_per_gpu"] / peak, 4)
             bt["roofline_tokens_per_s"] = round(bt["batch"] * peak * 1e9 * world
                                                 / (decode70["weight_bytes_per_token_per_gpu"] * world
@@ -830,9 +925,11 @@ def main():
                              "engine": decode["engine"]}
     if decode70 is not None:
         summ["decode_70b"] = {"tp": decode70["tensor_parallel"], "tokens_per_s": decode70["tokens_per_s"],
-                              "batch32_tokens_per_s": decode70.get("batch", {}).get("tokens_per_s")}
-        if "tp_parity" in decode70:
-            summ["tp_parity"] = decode70["tp_parity"]
+                              "batch32_tokens_per_s": decode70.get("batched", {}).get("tokens_per_s")}
+    if tp_parity is not None:
+        summ["tp_parity"] = {k: tp_parity[k] for k in ("max_rel_err", "tokens_equal", "within_tolerance")}
+    if rowsplit_check is not None:
+        summ["rowsplit_gather_ok"] = rowsplit_check["gathered_y_equals_plain_matvecs"]
     line["summary"] = summ
     print(json.dumps(line), flush=True)
     if world > 1:

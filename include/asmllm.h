@@ -369,6 +369,8 @@ ASMLLM_API int asm_matmul_q4_noalloc_async(const uint8_t* qweights, const void* 
 /* Device error word bits (asm_device_error). */
 #define ASM_DEVERR_RING_TIMEOUT 1u /* a shared-memory ring wait gave up */
 #define ASM_DEVERR_DECODE_RANGE 2u /* position >= ctx / max_tokens or token id >= vocab: step skipped */
+#define ASM_DEVERR_XCHG_TIMEOUT 4u /* an exchange / gather wait gave up (a peer never wrote) */
+#define ASM_EPI_GATHER 4   /* row-split gather (asm_matvec_rowsplit_async only; not a fused epilogue) */
 
 typedef struct asm_fused_matvec {
   int32_t fmt;      /* 2 = Q4_0, 8 = Q8_0 */
@@ -427,6 +429,48 @@ ASMLLM_API int asm_ipc_alloc(int64_t bytes, void** ptr, void* handle64);
 ASMLLM_API int asm_ipc_open(const void* handle64, void** ptr);
 ASMLLM_API int asm_ipc_close(void* ptr);
 ASMLLM_API int asm_ipc_free(void* ptr);
+
+/* ---- Row-split matvec over a tensor-parallel group (one process per GPU) ----
+ * The reference splits M among its threads (src/runtime/threadpool.c:408-486,
+ * asm_threadpool_dispatch_q4): worker t computes a contiguous range of output
+ * rows and every row lands in the one shared y.  Across GPUs the same split
+ * is: rank r holds rows [r*M, (r+1)*M) of a (tp*M) x K matrix, computes them,
+ * and the full y is all-gathered.  Here the gather rides on the matvec: each
+ * finished row is stored into y_full[rank*M + row] and, as a (sequence,
+ * value) 64-bit word, into every other rank's gather buffer over NVLink
+ * (peer stores, no multicast); asm_rowsplit_wait_async then waits (bounded)
+ * for the peers' words of a step and completes y_full.
+ *   xchg[r]: rank r's gather buffer, at least 2 * tp * M 64-bit words, zero
+ *            before first use (asm_ipc_alloc / asm_ipc_open; own entry unused
+ *            by the matvec).  One buffer per matvec of a step.
+ *   seq:     the group's step counter (device, zero at start, same on every
+ *            rank), read by the matvecs and advanced by asm_rowsplit_wait_async.
+ * ASM_MV_PACKED: qweights are packed rows (asm_pack_rows_async) and
+ * scales_f16 is unused; else planes with fp16 scales.  ASM_MV_INDEPENDENT as
+ * for asm_matvec_ex_async.  A step is: its matvecs, then one
+ * asm_rowsplit_wait_async naming all of them, on one stream.  The next
+ * step's matvecs may compute while the wait runs; each matvec stores its rows
+ * to the peers only after the kernel before it in the stream has completed,
+ * so no rank overwrites a parity a slower rank still reads.  tp = 1 is a
+ * plain matvec into y_full. */
+#define ASM_MV_PACKED 2u
+ASMLLM_API int asm_matvec_rowsplit_async(int fmt, const void* qweights, const uint16_t* scales_f16,
+                                         const float* x, float* y_full, int64_t M, int64_t K, int32_t tp,
+                                         int32_t rank, void* const* xchg, uint32_t* seq, unsigned flags,
+                                         void* stream);
+typedef struct asm_rowsplit_wait {
+  int32_t n;            /* matvecs of the step (<= 8) */
+  int32_t tp, rank;
+  const void* own[8];   /* this rank's gather buffer of matvec j */
+  float* y_full[8];     /* its full output [tp * M[j]] */
+  int64_t M[8];         /* its rows per rank */
+  uint32_t* seq;        /* the step counter */
+  uint32_t* done;       /* device word, zero before the first call, left zero */
+} asm_rowsplit_wait_t;
+/* Waits (each word at most the "xchg_wait_us" limit; a peer that never
+ * writes sets ASM_DEVERR_XCHG_TIMEOUT) until every peer row of the step's
+ * matvecs has arrived, copies them into y_full, advances *seq. */
+ASMLLM_API int asm_rowsplit_wait_async(const asm_rowsplit_wait_t* w, void* stream);
 
 /* RoPE + KV append + attention for position *pos of one layer, one CTA per
  * query head (reference generate.py:281-296 with ops.py:119-141 RoPE):
@@ -613,7 +657,11 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * 16 warps), everything else to the warp-ring kernel; 1 = warp rings always;
  * 2 = row stages wherever they apply (not packed rows, not independent
  * launches).  The two kernels add a row's products in different fixed orders,
- * so y may differ in the last bits between settings (each is deterministic). */
+ * so y may differ in the last bits between settings (each is deterministic).
+ * "xchg_wait_us": limit of every tensor-parallel exchange and row-split
+ * gather wait on the current device, in microseconds at about 2 GHz (0 =
+ * the default, about a second); a wait that runs out sets
+ * ASM_DEVERR_XCHG_TIMEOUT and the kernel returns. */
 ASMLLM_API int asm_set_option(const char* name, int value);
 
 /* Largest K each matvec family supports (shared-memory staging of x). */

@@ -34,14 +34,21 @@ def test_packed_matvec_equals_plane_matvec(cuda, oracle, fmt, M, K):
     row = packed[r].cpu().numpy()
     assert np.array_equal(row[: K // 32 * ub], w[r].reshape(-1).view(np.uint8))
     assert np.array_equal(row[K // 32 * ub:].view(np.float16), s[r].astype(np.float16))
-    y_planes = ops.matvec(fmt, dw, ds, dx).cpu().numpy()
+    # the warp-ring kernel on both layouts (independent launches always take it)
+    y_planes = ops.matvec(fmt, dw, ds, dx, independent=True).cpu().numpy()
     y_packed = ops.matvec_packed(fmt, packed, dx).cpu().numpy()
     y_indep = ops.matvec_packed(fmt, packed, dx, independent=True).cpu().numpy()
+    # a dependent launch on planes: the row-stage kernel for rows of more than
+    # 128 blocks (another fixed summation order), the warp-ring kernel otherwise
+    y_dep = ops.matvec(fmt, dw, ds, dx).cpu().numpy()
     torch.cuda.synchronize()
     assert np.array_equal(y_packed, y_planes)
     assert np.array_equal(y_indep, y_planes)
+    if K // 32 <= 128:
+        assert np.array_equal(y_dep, y_planes)
     ref = oracle.matmul_q4q8(w, s, x) if fmt == 2 else oracle.matmul_q8q8(w, s, x)
     assert rel_err(y_packed, ref) <= YTOL
+    assert rel_err(y_dep, ref) <= YTOL
     assert ops.device_error() == 0
 
 

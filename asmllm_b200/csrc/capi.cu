@@ -273,20 +273,15 @@ int device_in(DeviceState& st, int dev, const void* p, size_t bytes, int slot, c
 }
 
 // Synchronous Q8_0-activation calls quantize x with a separate pre-pass into a
-// per-device image (default) or inside the matvec (ASMLLM_SYNC_FUSED=1).
-// Bit 0: pinned host x mapped into the device and read in place by the
+// per-device image (default) or inside the matvec (option "sync_fused" = 1).
+std::atomic<int> g_opt_sync_fused{0};
+// Option "sync_map" -- bit 0: pinned host x mapped into the device and read in place by the
 // activation pre-pass; bit 1: pinned host y written in place by the matvec.
 // A cleared bit stages that buffer with a copy instead.
 std::atomic<int> g_opt_sync_map{3};
 std::atomic<int> g_opt_xchg_wait_us{0};  // 0 = the default exchange wait limit (about a second)
 
-bool sync_fused() {
-  static const bool v = [] {
-    const char* e = getenv("ASMLLM_SYNC_FUSED");
-    return e && e[0] == '1';
-  }();
-  return v;
-}
+bool sync_fused() { return g_opt_sync_fused.load() != 0; }
 
 void sync_matvec(const char* name, int fmt, bool fp32_act, const void* w, const float* s,
                  const float* x, float* y, int64_t M, int64_t K) {
@@ -1816,8 +1811,7 @@ ASMLLM_API int asm_decode_create(const asm_decode_model_t* m, void** handle) {
 
   // Replicated activations of the persistent kernel: x [xr][dim], then the
   // two images [xr][bytes] (each replica 16-byte aligned).
-  int xr = 1;  // measured: 8 replicas were no faster than 1 on B200
-  if (const char* ev = getenv("ASMLLM_DECODE_XR")) xr = std::max(1, std::min(64, atoi(ev)));
+  const int xr = 1;  // measured: 8 replicas were no faster than 1 on B200
   const size_t x_bytes = (size_t)m->dim * sizeof(float);
   const size_t ia_bytes = act_image_bytes(qdim / 32), ih_bytes = act_image_bytes(m->ffn / 32);
   unsigned char* d_rep = nullptr;
@@ -1980,6 +1974,9 @@ ASMLLM_API int asm_set_option(const char* name, int value) {
   if (strcmp(name, "mv_slots") == 0) return g_opt_mv_slots.exchange(value < 0 ? 0 : value);
   if (strcmp(name, "mv_smem_kb") == 0) return g_opt_mv_smem_kb.exchange(value <= 0 ? 0 : value < 16 ? 16 : value);
   if (strcmp(name, "mv_ctas") == 0) return g_opt_mv_ctas.exchange(value < 1 ? 1 : value > 4 ? 4 : value);
+  if (strcmp(name, "sync_fused") == 0) return g_opt_sync_fused.exchange(value ? 1 : 0);
+  if (strcmp(name, "image_prefetch_mb") == 0)
+    return g_opt_image_prefetch_mb.exchange(value < 0 ? 0 : value > 4096 ? 4096 : value);
   if (strcmp(name, "mv_kernel") == 0) return g_opt_mv_kernel.exchange(value == 1 || value == 2 ? value : 0);
   if (strcmp(name, "xchg_wait_us") == 0) {
     // SM clock cycles at about 2 GHz; set on the current device

@@ -498,10 +498,7 @@ const DevInfo& dev_info(int dev) {
 
 }  // namespace
 
-std::atomic<int> g_opt_pdl{[] {
-  const char* e = getenv("ASMLLM_PDL");
-  return (e && e[0] == '0') ? 0 : 1;
-}()};
+std::atomic<int> g_opt_pdl{1};
 
 // Stream-ordered scratch (activation images and tiles the library makes for
 // one call).  Outside stream capture it comes from a per-device pool that
@@ -556,11 +553,13 @@ void scratch_trim() {
 
 // Runtime switches (asm_set_option): bulk-copy pipeline kernel for the Q8_0
 // families (else the register-streaming kernels) and programmatic dependent
-// launch.  Initial values from ASMLLM_TMA / ASMLLM_PDL (default on).
-std::atomic<int> g_opt_tma{[] {
-  const char* e = getenv("ASMLLM_TMA");
-  return (e && e[0] == '0') ? 0 : 1;
-}()};
+// launch (g_opt_pdl above); both on by default.
+std::atomic<int> g_opt_tma{1};
+
+// L2 prefetch of the following matvec's weights by the activation pre-pass,
+// at most this many MB (asm_set_option "image_prefetch_mb"; 0 = off, the
+// default: no gain measured with the bulk-copy matvecs).
+std::atomic<int> g_opt_image_prefetch_mb{0};
 
 // Matvecs with K at or above this quantize x in a pre-pass kernel instead of
 // in every CTA's prologue (0: never).
@@ -588,14 +587,8 @@ cudaError_t launch_pdl(const void* kernel, dim3 grid, dim3 block, size_t smem, c
   return cudaLaunchKernelExC(&cfg, kernel, args);
 }
 
-// Tunables (environment, read once): CTAs per SM cap and L2 prefetch budget.
-int env_int(const char* name, int dflt) {
-  const char* e = getenv(name);
-  return e ? atoi(e) : dflt;
-}
-const int g_cta_cap = env_int("ASMLLM_CTAS_PER_SM", 0);      // 0: heuristic
-const int g_pf_budget_kb = env_int("ASMLLM_PF_KB", 24);       // per-warp L2 prefetch window
-const int g_img_pf_mb = env_int("ASMLLM_IMG_PF_MB", 0);       // quantize-kernel prefetch of the next weights (MB)
+// L2 prefetch window of each warp of the register-streaming kernels (measured best).
+constexpr int kPfBudgetKb = 24;
 
 template <typename KernelT>
 cudaError_t launch_persistent(KernelT kernel, int ngroups, size_t smem, cudaStream_t stream,
@@ -619,16 +612,15 @@ cudaError_t launch_persistent(KernelT kernel, int ngroups, size_t smem, cudaStre
     std::lock_guard<std::mutex> lk(g_occ_mu);
     g_occ[key] = per_sm;
   }
-  // All co-resident CTAs by default (ASMLLM_CTAS_PER_SM caps it for experiments).
-  int cap = g_cta_cap > 0 ? g_cta_cap : per_sm;
-  if (cap > per_sm) cap = per_sm;
+  // All co-resident CTAs.
+  const int cap = per_sm;
   const long long needed = ((long long)ngroups + kWarps - 1) / kWarps;
   long long grid = (long long)cap * di.sms;
   if (needed < grid) grid = needed;
   if (grid < 1) grid = 1;
   if (pf_arg) {
     const long long groups_per_warp = ((long long)ngroups + grid * kWarps - 1) / (grid * kWarps);
-    long long pf = group_bytes ? ((long long)g_pf_budget_kb * 1024) / (long long)group_bytes : 0;
+    long long pf = group_bytes ? ((long long)kPfBudgetKb * 1024) / (long long)group_bytes : 0;
     if (pf > groups_per_warp) pf = groups_per_warp;
     *pf_arg = (int)pf;
   }
@@ -645,21 +637,6 @@ Cfg pick_cfg(int M, int NU, int sms, bool fp32_act) {
   if (fp32_act) return {2, 2};
   if ((long long)M < (long long)sms * kWarps * 4) return {1, 4};
   return {2, 2};
-}
-
-Cfg cfg_override(Cfg c) {
-  static int forced_rows = -1, forced_u = -1;
-  if (forced_rows < 0) {
-    forced_rows = 0;
-    const char* s = getenv("ASMLLM_MATVEC_CFG");
-    int r = 0, u = 0;
-    if (s && sscanf(s, "%dx%d", &r, &u) == 2) {
-      forced_rows = r;
-      forced_u = u;
-    }
-  }
-  if (forced_rows > 0) return {forced_rows, forced_u};
-  return c;
 }
 
 template <int FMT, int R, int U>
@@ -713,7 +690,7 @@ cudaError_t launch_matvec(const MatvecArgs& a, cudaStream_t stream) {
   if (nb == 0) return cudaMemsetAsync(a.y, 0, (size_t)a.M * sizeof(float), stream);
   const DevInfo& di = dev_info(dev);
   const int NU = a.fmt == kFmtQ4_0 ? nb : 2 * nb;
-  const Cfg c = cfg_override(pick_cfg(M, NU, di.sms, a.fp32_act));
+  const Cfg c = pick_cfg(M, NU, di.sms, a.fp32_act);
 
   const void* w = a.w;
   const void* s = a.scales;
@@ -791,9 +768,9 @@ cudaError_t launch_act_image(const float* x, void* image, long long nrows, int64
   if (grid > cap) grid = cap;
   unsigned char* img = static_cast<unsigned char*>(image);
   long long stride = (long long)act_image_bytes(nb);
-  // Prefetch at most ASMLLM_IMG_PF_MB (default 32) MB of the following matvec's weights,
+  // Prefetch at most "image_prefetch_mb" MB of the following matvec's weights,
   // in proportion between the weight and scale planes; 16-byte aligned starts only.
-  const size_t pf_cap = (size_t)g_img_pf_mb << 20;
+  const size_t pf_cap = (size_t)g_opt_image_prefetch_mb.load() << 20;
   const size_t tot = pf_w_bytes + pf_s_bytes;
   if (tot > pf_cap && tot > 0) {
     pf_w_bytes = (size_t)((double)pf_w_bytes * pf_cap / tot);

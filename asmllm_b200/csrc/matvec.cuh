@@ -239,6 +239,7 @@ extern std::atomic<int> g_opt_mv_rows;
 extern std::atomic<int> g_opt_mv_slots;
 extern std::atomic<int> g_opt_mv_smem_kb;
 extern std::atomic<int> g_opt_mv_kernel;
+extern std::atomic<int> g_opt_image_prefetch_mb;
 extern std::atomic<int> g_opt_mv_ctas;
 
 }  // namespace asmllm

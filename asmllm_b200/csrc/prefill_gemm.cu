@@ -76,13 +76,6 @@
 #include "pipeline.cuh"
 #include "tiles.cuh"
 
-#ifndef ASMLLM_GEMM_TEAMS
-#define ASMLLM_GEMM_TEAMS 1
-#endif
-#ifndef ASMLLM_GEMM_EW
-#define ASMLLM_GEMM_EW (BN >= 64 ? 8 : 4)
-#endif
-
 namespace asmllm {
 
 std::atomic<int> g_opt_gemm_splits{0};
@@ -123,8 +116,8 @@ struct Cfg {
   // With 8 expander warps: two teams of 4 (one thread per row each) that take
   // alternate groups, so two groups are expanded at once (the expansion of one
   // group is latency-bound: shared load -> convert -> tensor-memory store).
-  static constexpr int kTeams = (ASMLLM_GEMM_TEAMS && kXW == 8) ? 2 : 1;
-  static constexpr int kEW = ASMLLM_GEMM_EW;      // epilogue warps (8: two column halves)
+  static constexpr int kTeams = kXW == 8 ? 2 : 1;
+  static constexpr int kEW = BN >= 64 ? 8 : 4;  // epilogue warps (8: two column halves)
   static constexpr int kLoader = 2 + kXW + kEW;  // the tile loader's warp (the last)
   static constexpr int kThreads = (kLoader + 1) * 32;
   static constexpr int kCols = BN * 4 / kEW;     // accumulator columns per epilogue thread

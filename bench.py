@@ -148,84 +148,113 @@ class Clocks:
 # CPU side: oracle port timed on the host cores (cpu_baseline and --impl reference)
 # --------------------------------------------------------------------------
 
-def cpu_sweep_gbs(budget_s, threads, copies=1):
-    """Times the oracle's multi-thread Q4_0 x Q8_0 (NEON semantics, threadpool
-    tiling) on the four sweep shapes; returns (GB/s, sweeps, seconds)."""
-    import numpy as np
-
+def _sweep_data():
     from asmllm_b200 import synth
-    from oracle import oracle as O
 
     data = []
     for i, (M, K) in enumerate(SHAPES):
         qs, s = synth.q4_0_weights(M, K, seed=100 + i)
         data.append((qs, s, synth.activation(K, seed=200 + i), M, K))
-    sweep_bytes = sum(q4_bytes(M, K) for _, _, _, M, K in data)
-    # one untimed sweep (page-in)
+    return data
+
+
+def _cpu_sweep(data, frac, threads):
+    """One sweep of the four shapes by the oracle's multi-thread Q4_0 x Q8_0 (NEON
+    semantics, threadpool tiling): all rows (frac = 1) or the first frac of every
+    shape's rows in whole 16-row tiles; returns the weight bytes read."""
+    from oracle import oracle as O
+
+    nbytes = 0
     for qs, s, x, M, K in data:
-        O.matmul_mt(O.K_Q4Q8, qs, s, x, M, K, threads)
-    n, t0 = 0, time.perf_counter()
-    while True:
-        for qs, s, x, M, K in data:
-            O.matmul_mt(O.K_Q4Q8, qs, s, x, M, K, threads)
-        n += 1
-        el = time.perf_counter() - t0
-        if el >= budget_s or n >= 10000:
-            break
-    return sweep_bytes * n / el / 1e9, n, el
+        rows = M if frac >= 1.0 else max(16, min(M, int(math.ceil(M * frac / 16.0)) * 16))
+        O.matmul_mt(O.K_Q4Q8, qs[:rows], s[:rows], x, rows, K, threads)
+        nbytes += q4_bytes(rows, K)
+    return nbytes
+
+
+def thread_levels(nproc):
+    """T in {1, 2, 4, ..., nproc}: powers of two below the host's thread count, then the count."""
+    out, t = [], 1
+    while t < nproc:
+        out.append(t)
+        t *= 2
+    return out + [nproc]
+
+
+def sample_stats(gbs):
+    """Median and interquartile range of per-sample GB/s."""
+    g = sorted(gbs)
+    if len(g) == 1:
+        return {"median": round(g[0], 3), "iqr": [round(g[0], 3), round(g[0], 3)], "samples": 1}
+    q1, _, q3 = statistics.quantiles(g, n=4, method="inclusive")
+    return {"median": round(statistics.median(g), 3), "iqr": [round(q1, 3), round(q3, 3)], "samples": len(g)}
+
+
+def cpu_thread_sweep(data, frac, budget_s, max_samples=10000):
+    """The CPU protocol shared by the cpu_baseline leg and the reference arm: at every
+    T of thread_levels(host threads), one untimed sweep, then timed sweeps (fraction
+    frac of the rows) for budget_s / len(levels) seconds; per-sample GB/s summarised
+    by median and IQR.  Returns (best T by median, {T: stats})."""
+    from oracle import oracle as O
+
+    levels = thread_levels(O.host_threads())
+    per = {}
+    for T in levels:
+        _cpu_sweep(data, frac, T)
+        gbs, t_end = [], time.perf_counter() + budget_s / len(levels)
+        while time.perf_counter() < t_end and len(gbs) < max_samples:
+            t0 = time.perf_counter()
+            nbytes = _cpu_sweep(data, frac, T)
+            gbs.append(nbytes / (time.perf_counter() - t0) / 1e9)
+        per[T] = sample_stats(gbs)
+    best = max(per, key=lambda t: per[t]["median"])
+    return best, per
 
 
 def run_reference(args, rank, world):
-    """The reference arm: the oracle port of the reference's CPU path, all host threads.
+    """The reference arm: the oracle port of the reference's CPU path on the host cores.
 
-    Each step is a bounded sample of the sweep: the first `rows` of every shape
-    (the same fraction for all four, whole 16-row tiles), sized from one
-    untimed full sweep so the --steps run stays near REF_BUDGET_S seconds."""
+    Protocol: the thread sweep T in {1, 2, 4, ..., nproc} (median and IQR of per-sweep
+    GB/s at each T, ~20 % of the budget) picks T; then --steps timed steps at that T,
+    each a bounded sample of the sweep -- the first `frac` of every shape's rows (whole
+    16-row tiles), sized from one untimed full sweep so the run stays near
+    ASMLLM_REF_BUDGET_S seconds.  value = the median per-step GB/s."""
     if rank != 0:
         return
-    from asmllm_b200 import synth
+    REF_BUDGET_S = float(os.environ.get("ASMLLM_REF_BUDGET_S", "100"))  # seconds of timed CPU work
+    data = _sweep_data()
     from oracle import oracle as O
 
-    REF_BUDGET_S = float(os.environ.get("ASMLLM_REF_BUDGET_S", "100"))  # seconds of timed CPU work
-    threads = O.host_threads()
-    data = []
-    for i, (M, K) in enumerate(SHAPES):
-        qs, s = synth.q4_0_weights(M, K, seed=100 + i)
-        data.append((qs, s, synth.activation(K, seed=200 + i), M, K))
-
-    def sweep(frac):
-        nbytes = 0
-        for qs, s, x, M, K in data:
-            rows = M if frac >= 1.0 else max(16, min(M, int(math.ceil(M * frac / 16.0)) * 16))
-            O.matmul_mt(O.K_Q4Q8, qs[:rows], s[:rows], x, rows, K, threads)
-            nbytes += q4_bytes(rows, K)
-        return nbytes
-
     t0 = time.perf_counter()
-    sweep(1.0)
+    _cpu_sweep(data, 1.0, O.host_threads())
     t_full = time.perf_counter() - t0
-    frac = min(1.0, REF_BUDGET_S / max(1e-9, args.steps * t_full))
+    frac = min(1.0, 0.8 * REF_BUDGET_S / max(1e-9, args.steps * t_full))
+    threads, per = cpu_thread_sweep(data, frac, 0.2 * REF_BUDGET_S)
     for _ in range(max(1, args.warmup)):
-        sweep(frac)
-    nbytes = 0
-    t0 = time.perf_counter()
+        _cpu_sweep(data, frac, threads)
+    gbs, total = [], 0.0
     for _ in range(args.steps):
-        nbytes += sweep(frac)
-    el = time.perf_counter() - t0
-    gbs = nbytes / el / 1e9
-    sample = (f"{args.steps} steps, each the first {frac * 100:.1f}% of the rows of each of the 4 shapes "
-              f"({nbytes / args.steps / 1e6:.1f} MB/step), after {max(1, args.warmup)} untimed; C restatement of "
-              "the NEON asm_matmul_q4 with the reference threadpool tiling (the reference NASM/GAS cannot be "
-              "assembled here: no nasm, no aarch64 toolchain)")
+        t0 = time.perf_counter()
+        nbytes = _cpu_sweep(data, frac, threads)
+        el = time.perf_counter() - t0
+        total += el
+        gbs.append(nbytes / el / 1e9)
+    st = sample_stats(gbs)
+    sample = (f"thread sweep T in {list(per)} (median GB/s {[per[t]['median'] for t in per]}), then "
+              f"{args.steps} steps at T={threads}, each the first {frac * 100:.1f}% of the rows of each of the 4 "
+              f"shapes, after {max(1, args.warmup)} untimed; value = median per-step GB/s, IQR {st['iqr']}; C "
+              "restatement of the NEON asm_matmul_q4 with the reference threadpool tiling (the reference NASM/GAS "
+              "cannot be assembled here: no nasm, no aarch64 toolchain)")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "impl": "reference", "metric": METRIC, "value": st["median"], "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(el / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(total / args.steps * 1e3, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": "Q4_0xQ8_0 matvec sweep: 4096x4096, 11008x4096, 4096x11008, 32000x4096, batch 1",
                    "weights": "fp32-scale ABI layout in host RAM", "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_baseline": {"value": st["median"], "unit": "GB/s", "cores": threads, "kind": "port", "sample": sample,
+                         "iqr": st["iqr"], "thread_sweep": {str(t): v for t, v in per.items()}},
+        "e2e": {"value": st["median"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
@@ -816,13 +845,12 @@ def main():
     peak, peak_kind = load_peaks()
     cpu = None
     if world == 1:
-        from oracle import oracle as O
-
-        threads = O.host_threads()
-        gbs, n, sec = cpu_sweep_gbs(args.cpu_budget, threads)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"{n} sweeps of the 4 shapes in {sec:.1f} s; C restatement of the NEON asm_matmul_q4 "
-                         "with the reference threadpool row tiling (reference asm not assemblable here)"}
+        best, per = cpu_thread_sweep(_sweep_data(), 1.0, args.cpu_budget)
+        cpu = {"value": per[best]["median"], "unit": "GB/s", "cores": best, "kind": "port",
+               "iqr": per[best]["iqr"], "thread_sweep": {str(t): v for t, v in per.items()},
+               "sample": f"full sweeps of the 4 shapes at T in {list(per)} threads, {args.cpu_budget:.0f} s in all; "
+                         f"value = median per-sweep GB/s at the best T ({best}); C restatement of the NEON "
+                         "asm_matmul_q4 with the reference threadpool row tiling (reference asm not assemblable here)"}
     traffic = load_traffic()
     line = {
         "metric": METRIC,

@@ -658,6 +658,10 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * 2 = row stages wherever they apply (not packed rows, not independent
  * launches).  The two kernels add a row's products in different fixed orders,
  * so y may differ in the last bits between settings (each is deterministic).
+ * "sync_fused": 1 = the synchronous Q8_0-activation entries quantize x
+ * inside the matvec kernel instead of in a pre-pass into a per-device image
+ * (default 0).  "image_prefetch_mb": the activation pre-pass also pulls up to
+ * this many MB of the following matvec's weights into L2 (default 0 = off).
  * "xchg_wait_us": limit of every tensor-parallel exchange and row-split
  * gather wait on the current device, in microseconds at about 2 GHz (0 =
  * the default, about a second); a wait that runs out sets

@@ -1,14 +1,17 @@
 """Small, bounded workload for profiling the matvec kernels under ncu.
 
     python -m asmllm_b200.profdrive [--fmt q4|q8] [--mode fused|image] [--launches N]
-                                    [--path tma|ldg] MxK [MxK ...]
+                                    [--path tma|ldg] [--layout planes|packed]
+                                    [--chain dependent|independent] MxK [MxK ...]
     python -m asmllm_b200.profdrive --decode N [--layers L] [--warm W]
     python -m asmllm_b200.profdrive --gemm N [--launches L] MxK [MxK ...]
 
 For each shape it builds one weight matrix on cuda:0 (random seeded quants,
 fp16 scales, declared static like model weights), then runs N matvecs
 (default 2) on torch's current stream.  Device memory stays at the size of
-the largest matrix, so an ncu capture of it ends quickly.
+the largest matrix, so an ncu capture of it ends quickly.  --layout packed
+streams packed rows (asm_pack_rows_async) as the bench's headline does;
+--chain independent launches with ASM_MV_INDEPENDENT.
 
 --gemm N runs the tensor-core batched product (N tokens, Q4_0) L times per
 shape, from one activation image of N rows.
@@ -38,6 +41,8 @@ def main() -> None:
     ap.add_argument("--mode", choices=["fused", "image"], default="fused")
     ap.add_argument("--launches", type=int, default=2)
     ap.add_argument("--path", choices=["tma", "ldg"], default="tma")
+    ap.add_argument("--layout", choices=["planes", "packed"], default="planes")
+    ap.add_argument("--chain", choices=["dependent", "independent"], default="dependent")
     args = ap.parse_args()
     if args.decode:
         from dataclasses import replace
@@ -85,15 +90,24 @@ def main() -> None:
         x = torch.randn(K, device=dev, generator=gen)
         y = torch.empty(M, device=dev)
         torch.cuda.synchronize()
-        ops.mark_static(qs, d)
+        indep = args.chain == "independent"
+        if args.layout == "packed":
+            w = ops.pack_rows(fmt, qs, d)
+            del qs, d
+            qs, d = w, None
+            ops.mark_static(w)
+        else:
+            ops.mark_static(qs, d)
         for _ in range(args.launches):
-            if args.mode == "fused":
-                ops.matvec(fmt, qs, d, x, out=y)
+            if args.layout == "packed":
+                ops.matvec_packed(fmt, qs, x, out=y, independent=indep)
+            elif args.mode == "fused":
+                ops.matvec(fmt, qs, d, x, out=y, independent=indep)
             else:
                 img = ops.act_image_dev(x)
                 ops.matvec_image(fmt, qs, d, img, K, out=y)
         torch.cuda.synchronize()
-        ops.unmark_static(qs, d)
+        ops.unmark_static(*([qs] if d is None else [qs, d]))
         del qs, d
     err = ops.device_error()
     print(f"profdrive: {len(args.shapes)} shape(s) x {args.launches} launch(es), device error word {err}")

@@ -32,10 +32,10 @@
 //     timeout the kernel sets bit 0 of g_device_error, lets the copies it
 //     issued land, and returns.
 //
-// Rows of more than 128 blocks in launches that wait for the previous kernel
-// (decode chains, the plain entries) are streamed by the row-stage kernel of
-// tma_rows.cuh instead (use_rows below): in such chains its CTA-wide ~16 KB
-// stages measured 20-40 % faster than per-warp rings of long rows.
+// The fused decode-step matvecs, and plain matvecs with rows of more than 128
+// blocks in launches that wait for the previous kernel, are streamed by the
+// row-stage kernel of tma_rows.cuh instead (use_rows below): in such chains
+// its CTA-wide ~16 KB stages measured 6-40 % faster than per-warp rings.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -322,8 +322,10 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
   // tensor-parallel residual exchange take one contiguous range per CTA.
   const int n_g = (M + RS - 1) / RS;
   const int G = (int)gridDim.x, cta = (int)blockIdx.x;
-  const bool stride = EPI == kEpiStore || EPI == kEpiArgmax || EPI == kEpiGather ||
-                      (EPI == kEpiResidual && fz.tp <= 1);
+  // (The row-split gather keeps contiguous ranges: a CTA's rows then go to a
+  // peer as consecutive 64-bit words, so each warp store is one 256-byte burst
+  // over NVLink instead of 32 scattered words.)
+  const bool stride = EPI == kEpiStore || EPI == kEpiArgmax || (EPI == kEpiResidual && fz.tp <= 1);
   const int g0 = (int)((long long)n_g * cta / G), g1 = (int)((long long)n_g * (cta + 1) / G);
   const int nq = stride ? (cta < n_g ? (n_g - 1 - cta) / G + 1 : 0) : g1 - g0;
   const int r0 = g0 * RS, r1 = min(M, g1 * RS);  // the contiguous range (SwiGLU, exchange)
@@ -345,6 +347,34 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
     if (indep && threadIdx.x == 0) pdl_wait();
     return;
   }
+
+  // Source of a quantizing prologue and its register batches: 4 lanes per
+  // block (8 elements each), 64 blocks per pass; the loads of up to PB passes
+  // are issued before any use, so x costs one L2 round trip per PB passes
+  // (one in all for K <= 12288).
+  const float* x = PRO != kProImage ? prologue_source(fz, act, nb * QK) : nullptr;
+  const int lane4 = threadIdx.x & 3;
+  constexpr int BPP = NCT / 4;  // blocks per pass
+  constexpr int PB = 6;         // passes per batch of loads
+  float4 v0[PB], v1[PB];
+  auto load_batch = [&](int base) {
+#pragma unroll
+    for (int p = 0; p < PB; ++p) {
+      const int b = base + p * BPP + (threadIdx.x >> 2);
+      if (b < nb) {
+        const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * QK) + 2 * lane4;
+        v0[p] = __ldcg(src);
+        v1[p] = __ldcg(src + 1);
+      } else {
+        v0[p] = v1[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+  };
+  // An independent launch's x does not come from the previous kernel: its
+  // first batch is requested before the barrier set-up and the ring's first
+  // copies, so the L2 round trip overlaps them.
+  const bool early = PRO == kProQuant && indep && fz.x_copy == nullptr;
+  if (early) load_batch(0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNcw * NSW; ++i) mbar_init(smem_u32(&bars[i]), 1);
@@ -407,28 +437,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
 
   // ---------------------------------------------------------- activation image
   if (PRO != kProImage) {
-    // 4 lanes per block (8 elements each), 64 blocks per pass; the loads of up
-    // to PB passes are issued before any use, so x costs one L2 round trip
-    // per PB passes (one in all for K <= 12288).
-    const float* x = prologue_source(fz, act, nb * QK);
     const bool copy = fz.x_copy != nullptr && blockIdx.x == 0;
-    const int lane4 = threadIdx.x & 3;
-    constexpr int BPP = NCT / 4;  // blocks per pass
-    constexpr int PB = 6;         // passes per batch of loads
-    float4 v0[PB], v1[PB];
-    auto load_batch = [&](int base) {
-#pragma unroll
-      for (int p = 0; p < PB; ++p) {
-        const int b = base + p * BPP + (threadIdx.x >> 2);
-        if (b < nb) {
-          const float4* src = reinterpret_cast<const float4*>(x + (size_t)b * QK) + 2 * lane4;
-          v0[p] = __ldcg(src);
-          v1[p] = __ldcg(src + 1);
-        } else {
-          v0[p] = v1[p] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      }
-    };
     auto sq4 = [](float4 v) {
       return __fadd_rn(__fadd_rn(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y)),
                        __fadd_rn(__fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w)));
@@ -439,7 +448,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       // rms = sqrt(mean(x^2) + eps), one fixed-order sum shared by every thread.
       float ssum = 0.0f;
       for (int base = 0; base < nb; base += PB * BPP) {
-        load_batch(base);
+        if (!(early && base == 0)) load_batch(base);
 #pragma unroll
         for (int p = 0; p < PB; ++p) {
           const int b = base + p * BPP + (threadIdx.x >> 2);
@@ -464,7 +473,7 @@ tma_matvec_kernel(const uint8_t* __restrict__ w, const void* __restrict__ scales
       }
     }
     for (int base = 0; base < nb; base += PB * BPP) {
-      if (!((PRO == kProNorm || copy) && held)) load_batch(base);
+      if (!((PRO == kProNorm || copy) && held) && !(early && base == 0)) load_batch(base);
 #pragma unroll
       for (int p = 0; p < PB; ++p) {
         if (base + p * BPP >= nb) break;  // uniform across the CTA
@@ -1036,15 +1045,19 @@ bool plan_of(const MatvecArgs& a, int smem_optin, TmaPlan* p) {
 
 namespace {
 
-// Which kernel streams a launch: rows longer than 128 blocks whose launch
-// waits for the previous kernel (a decode chain, the plain entries) go to the
-// row-stage kernel, everything else (short rows, packed rows, independent
-// launches) to the warp-ring kernel.  Option "mv_kernel": 0 = that choice,
-// 1 = warp rings always, 2 = row stages wherever they apply.
+// Which kernel streams a launch: the fused decode-step matvecs and plain
+// matvecs with rows longer than 128 blocks whose launch waits for the
+// previous kernel go to the row-stage kernel; everything else (plain short
+// rows, packed rows, independent launches, the row-split gather) to the
+// warp-ring kernel.  Measured: 7B decode 572 -> 606 tokens/s with the fused
+// K = 4096 matvecs on row stages, 465 with warp rings everywhere; plain
+// dependent K = 4096 chains are a few percent faster on warp rings.
+// Option "mv_kernel": 0 = that choice, 1 = warp rings always, 2 = row
+// stages wherever they apply.
 bool use_rows(const MatvecArgs& a, int smem_optin, RowsPlan* rp) {
   const int mode = g_opt_mv_kernel.load();
   if (mode == 1 || a.packed || a.act_independent || a.epi == kEpiGather) return false;
-  if (mode == 0 && a.K / QK <= 128) return false;
+  if (mode == 0 && a.K / QK <= 128 && !is_fused(a)) return false;
   if (!rows_plan(a.fmt, a.isums ? false : a.scales_f16, a.K / QK, smem_optin, rp)) return false;
   if (a.epi == kEpiSwiglu && rp->R < 2) return false;
   return true;

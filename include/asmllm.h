@@ -651,10 +651,11 @@ ASMLLM_API int asm_matmul_q5_async(const uint8_t* ql, const uint8_t* qh, const f
  * shared-memory budget of a CTA in KB (default 110, which leaves room on
  * every SM for a CTA of the next launch; a plan that does not fit takes the
  * whole opt-in shared memory); "mv_ctas" CTAs per SM (default 1).
- * "mv_kernel": which bulk-copy kernel streams a matvec: 0 (default) = rows of
- * more than 128 blocks in launches that wait for the previous kernel go to the
- * row-stage kernel (one producer warp, ~16 KB stages of whole rows shared by
- * 16 warps), everything else to the warp-ring kernel; 1 = warp rings always;
+ * "mv_kernel": which bulk-copy kernel streams a matvec: 0 (default) = the
+ * fused decode-step matvecs (asm_fused_matvec_async) and plain matvecs with
+ * rows of more than 128 blocks in launches that wait for the previous kernel
+ * go to the row-stage kernel (one producer warp, ~16 KB stages of whole rows
+ * shared by 16 warps), everything else to the warp-ring kernel; 1 = warp rings always;
  * 2 = row stages wherever they apply (not packed rows, not independent
  * launches).  The two kernels add a row's products in different fixed orders,
  * so y may differ in the last bits between settings (each is deterministic).

@@ -17,6 +17,8 @@ one step must be there.
 """
 from __future__ import annotations
 
+import contextlib
+
 import numpy as np
 import pytest
 
@@ -50,6 +52,17 @@ def dev_weights(torch, fmt, M, K, seed):
     return torch.from_numpy(w).cuda(), torch.from_numpy(s).cuda().half()
 
 
+@contextlib.contextmanager
+def row_stages():
+    """Plain matvecs on the row-stage kernel: the kernel the fused decode-step
+    matvecs take, so the comparisons below are of one summation order."""
+    prev = ops.set_option("mv_kernel", 2)
+    try:
+        yield
+    finally:
+        ops.set_option("mv_kernel", prev)
+
+
 def image_parts(img, nb):
     """(int8 values [nb, 32], (d, qsum) bytes [nb, 8]) of a Q8_0 activation image
     (the 16 pad bytes of each 48-byte slot carry nothing)."""
@@ -74,7 +87,8 @@ def test_norm_prologue_equals_unfused_on_normed_x(cuda, DO, fmt, M, K):
     dw, ds = dev_weights(torch, fmt, M, K, seed=40)
     x, nw = exact_inputs(K, 41)
     xn = DO.rmsnorm(x, nw, 1e-5)
-    y_plain = ops.matvec(fmt, dw, ds, torch.from_numpy(xn).cuda())
+    with row_stages():
+        y_plain = ops.matvec(fmt, dw, ds, torch.from_numpy(xn).cuda())
     y = torch.full((M,), float("nan"), device="cuda")
     ops.fused_matvec(fmt, dw, ds, native.EPI_STORE, x=torch.from_numpy(x).cuda(), norm_w=torch.from_numpy(nw).cuda(),
                      eps=1e-5, y=y)
@@ -104,7 +118,9 @@ def test_residual_epilogue(cuda, K):
     x = torch.from_numpy(synth.activation(K, seed=46)).cuda()
     y0 = torch.from_numpy(100 * synth.activation(M, seed=47)).cuda()
     img = ops.act_image_dev(x)
-    plain = ops.matvec_image(FMT_Q4_0, dw, ds, img, K)
+    with row_stages():
+        plain = ops.matvec_image(FMT_Q4_0, dw, ds, img, K)
+        plain_x = ops.matvec(FMT_Q4_0, dw, ds, x)
     y = y0.clone()
     ops.fused_matvec(FMT_Q4_0, dw, ds, native.EPI_RESIDUAL, image=img, y=y)
     torch.cuda.synchronize()
@@ -112,7 +128,7 @@ def test_residual_epilogue(cuda, K):
     y = y0.clone()
     ops.fused_matvec(FMT_Q4_0, dw, ds, native.EPI_RESIDUAL, x=x, y=y)  # quantizing prologue
     torch.cuda.synchronize()
-    assert torch.equal(y, y0 + ops.matvec(FMT_Q4_0, dw, ds, x))
+    assert torch.equal(y, y0 + plain_x)
 
 
 @pytest.mark.parametrize("ffn,K", [(1536, 512), (11008, 4096)])

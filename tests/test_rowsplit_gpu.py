@@ -123,8 +123,8 @@ def test_rowsplit_wait_times_out_when_a_peer_never_writes(cuda):
     assert ops.device_error() == 0
 
 
-@pytest.mark.parametrize("K", [4096, 8192], ids=["warp-ring", "row-stage"])
-def test_tp_residual_exchange_times_out_when_a_peer_never_writes(cuda, K):
+@pytest.mark.parametrize("K,kernel", [(4096, 1), (8192, 2)], ids=["warp-ring", "row-stage"])
+def test_tp_residual_exchange_times_out_when_a_peer_never_writes(cuda, K, kernel):
     """A tp = 2 row-parallel projection (the decode step's o / down) whose peer exchange
     buffer is a local buffer nobody writes: the kernel's bounded wait must run out."""
     torch = cuda
@@ -147,12 +147,14 @@ def test_tp_residual_exchange_times_out_when_a_peer_never_writes(cuda, K):
     d.ar_seq, d.ar_done = ar_seq.data_ptr(), ar_done.data_ptr()
     assert ops.device_error() == 0
     prev = ops.set_option("xchg_wait_us", 2000)
+    prev_kernel = ops.set_option("mv_kernel", kernel)  # 1: warp rings, 2: row stages
     try:
         native.check(native.lib().asm_fused_matvec_async(ctypes.byref(d), None))
         torch.cuda.synchronize()
         err = ops.device_error()
     finally:
         ops.set_option("xchg_wait_us", prev)
+        ops.set_option("mv_kernel", prev_kernel)
     assert err & native.DEVERR_XCHG_TIMEOUT
     # the partials went out: rank 0's rows in "rank 1's" buffer, [parity 1][source rank 0], sequence 1
     assert int((peer[2 * M:3 * M] >> 32).min().item()) == 1

@@ -403,9 +403,10 @@ def main():
         return g
 
     K_steps = args.steps
+    # one graph of all K steps when K <= 300 (a second graph launch inside a
+    # short timed region would add its host-side launch gap to the time);
+    # consecutive steps use the weight copies in turn across replays too
     G = min(K_steps, 300)
-    if G >= COPIES:
-        G -= G % COPIES
     reps, rem = divmod(K_steps, G)
     gA = capture(G, headline_step)
     gB = capture(rem, headline_step) if rem else None

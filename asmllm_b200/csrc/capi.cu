@@ -675,6 +675,38 @@ ASMLLM_API int asm_gemm_image_async(int fmt, const void* qweights, const void* s
   return ASM_OK;
 }
 
+ASMLLM_API int asm_gemm_narrow_async(int fmt, const void* qweights, const void* scales_f16, const void* images,
+                                     int64_t image_stride, float* y, int64_t M, int64_t N, int64_t K,
+                                     void* stream) {
+  const char* name = "asm_gemm_narrow_async";
+  if (fmt != kFmtQ4_0 && fmt != kFmtQ8_0) return set_error(ASM_E_INVALID, "%s: fmt %d is not 2 or 8", name, fmt);
+  if (M <= 0 || N <= 0 || K <= 0 || K % 32 || M > INT32_MAX)
+    return set_error(ASM_E_INVALID, "%s: need M, N > 0 and K > 0 a multiple of 32", name);
+  if (N > kNarrowMaxN)
+    return set_error(ASM_E_UNSUPPORTED, "%s: N=%lld tokens (at most %d; use asm_gemm_image_async)", name,
+                     (long long)N, kNarrowMaxN);
+  if (image_stride < (int64_t)act_image_bytes(K / 32) || image_stride % 16)
+    return set_error(ASM_E_INVALID, "%s: image_stride %lld below the image size or not a multiple of 16", name,
+                     (long long)image_stride);
+  int rc;
+  if ((rc = require_device(name, qweights, "qweights")) || (rc = require_device(name, scales_f16, "scales")) ||
+      (rc = require_device(name, images, "images")) || (rc = require_device(name, y, "y")))
+    return rc;
+  if ((uintptr_t)qweights % 16 || (uintptr_t)images % 16 || (uintptr_t)scales_f16 % 2 || (uintptr_t)y % 4)
+    return set_error(ASM_E_INVALID, "%s: qweights and images must be 16-byte aligned", name);
+  int dev = 0, sms = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if ((size_t)N * ((size_t)(K / 32) * 40 + 127) > (size_t)optin)
+    return set_error(ASM_E_UNSUPPORTED, "%s: N=%lld images of K=%lld exceed the shared memory", name, (long long)N,
+                     (long long)K);
+  const cudaError_t e = launch_gemm_narrow(fmt, qweights, scales_f16, images, (long long)image_stride, y, M, N, K,
+                                           sms > 0 ? sms : 1, optin, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_error(e, name);
+  return ASM_OK;
+}
+
 ASMLLM_API int64_t asm_act_tiles_bytes(int64_t N, int64_t K) {
   if (N <= 0 || K <= 0 || K % 32 || N > INT32_MAX) return 0;
   return (int64_t)act_tiles_bytes(N, K);

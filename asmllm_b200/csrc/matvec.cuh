@@ -152,6 +152,12 @@ bool tma_matvec_supported(const MatvecArgs& a, int smem_optin);
 // True when a asks for a decode fusion (which only the bulk-copy kernel has).
 bool matvec_is_fused(const MatvecArgs& a);
 cudaError_t launch_tma_matvec(const MatvecArgs& a, int sms, int smem_optin, cudaStream_t stream, bool pdl);
+// Y [N][M] for N <= kNarrowMaxN activation images, every weight byte read once
+// for all N rows (narrow_gemm.cuh); row n equals the warp-ring matvec of row n.
+constexpr int kNarrowMaxN = 8;
+cudaError_t launch_gemm_narrow(int fmt, const void* w, const void* scales_f16, const void* images,
+                               long long image_stride, float* y, long long M, long long N, long long K, int sms,
+                               int smem_optin, cudaStream_t stream);
 // Reads (and optionally clears) the device error word the kernels set when a
 // bounded wait gives up (bit 0: a shared-memory ring barrier timed out).
 cudaError_t read_device_error(unsigned* out, bool clear);

@@ -1042,6 +1042,7 @@ bool plan_of(const MatvecArgs& a, int smem_optin, TmaPlan* p) {
 }  // namespace
 
 #include "tma_rows.cuh"
+#include "narrow_gemm.cuh"
 
 namespace {
 

@@ -94,6 +94,7 @@ SIGNATURES = {
     "asm_matmul_q5_mt": ([vp, vp, vp, vp, vp, i64, i64, c_int], None),
     "asm_matmul_q5_async": ([vp, vp, vp, vp, vp, i64, i64, vp], c_int),
     "asm_gemm_image_async": ([c_int, vp, vp, vp, i64, vp, i64, i64, i64, vp], c_int),
+    "asm_gemm_narrow_async": ([c_int, vp, vp, vp, i64, vp, i64, i64, i64, vp], c_int),
     "asm_act_tiles_bytes": ([i64, i64], i64),
     "asm_act_tiles_from_image_async": ([vp, i64, i64, i64, vp, vp], c_int),
     "asm_gemm_tiles_async": ([c_int, vp, vp, vp, vp, i64, i64, i64, vp], c_int),

@@ -429,6 +429,25 @@ def gemm_image(fmt: int, qweights, scales, images, K: int, out=None, stream=None
     return out
 
 
+def gemm_narrow(fmt: int, qweights, scales, images, K: int, out=None, stream=None):
+    """Y [N, M] for N <= 8 activation-image rows (uint8 [N, bytes]) on the CUDA cores,
+    every weight byte read once for all N rows (asm_gemm_narrow_async); row n equals
+    the warp-ring matvec of row n bit for bit.  Scales fp16 [M, K/32]."""
+    torch = _torch()
+    wdt = torch.uint8 if fmt == FMT_Q4_0 else torch.int8
+    _check_dev(qweights, (wdt,), "qweights")
+    _check_dev(scales, (torch.float16,), "scales")
+    _check_dev(images, (torch.uint8,), "images")
+    M = scales.shape[0]
+    N = images.shape[0]
+    if out is None:
+        out = torch.empty((N, M), dtype=torch.float32, device=images.device)
+    rc = native.lib().asm_gemm_narrow_async(fmt, _ptr(qweights), _ptr(scales), _ptr(images), images.stride(0),
+                                            _ptr(out), M, N, K, _stream_handle(stream))
+    native.check(rc)
+    return out
+
+
 def gemm(fmt: int, qweights, scales, X, out=None, stream=None, tiles=None):
     """Y [N, M] = W x_n for the N rows of X fp32 [N, K]: quantize every row to Q8_0
     into activation tiles (asm_rows_norm_tiles_async without a norm), then the

@@ -702,6 +702,19 @@ def main():
                 row[f"{M}x{K}"] = {"us": round(t * 1e6, 2), "TOPS": round(2.0 * M * N * K / t / 1e12, 1),
                                    "weight_GB/s": round(q4_bytes(M, K) / t / 1e9, 1),
                                    "us_with_quantize": round(tq * 1e6, 2)}
+                if N <= 8:  # the CUDA-core product for a few tokens, from activation images
+                    img = ops.act_image_dev(X)
+                    g_n = capture(reps, lambda c, i=i: ops.gemm_narrow(FMT_Q4_0, *Wp[c][i], img, K, out=out))
+                    g_n.replay()
+                    torch.cuda.synchronize()
+                    a0.record()
+                    g_n.replay()
+                    a1.record()
+                    a1.synchronize()
+                    del g_n
+                    tn = a0.elapsed_time(a1) / reps / 1e3
+                    row[f"{M}x{K}"]["narrow"] = {"us": round(tn * 1e6, 2),
+                                                 "weight_GB/s": round(q4_bytes(M, K) / tn / 1e9, 1)}
             prefill[f"N={N}"] = row
         for row in Wp:
             for qs, d in row:
@@ -925,7 +938,9 @@ def main():
                       "applied in fp32 from tensor memory; Q4_0 stages by TMA (tensor map, 128-byte swizzle), "
                       "activation tiles by bulk copy; K split over a cluster (DSMEM reduction) when N is small",
             "ops": "2*M*N*K multiply-adds per call; 'us' = the product from activation tiles, 'us_with_quantize' "
-                   "= quantizing the fp32 rows into tiles plus the product",
+                   "= quantizing the fp32 rows into tiles plus the product; 'narrow' (N <= 8) = "
+                   "asm_gemm_narrow_async from activation images on the CUDA cores (each weight byte read once "
+                   "for all N rows)",
             "l2": "three weight copies per shape used in turn (> 126 MB L2)",
             "launch": "CUDA graph of 30 calls per shape and mode, timed with CUDA events", "per_shape": prefill,
             "peak_note": f"dense int8 tensor peak = 2x the measured bf16 {bf16} TFLOP/s (MEASURED_PEAKS.json); "

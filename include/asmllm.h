@@ -558,6 +558,18 @@ ASMLLM_API int asm_gemm_image_async(int fmt, const void* qweights, const void* s
                                     int64_t image_stride, float* y, int64_t M, int64_t N, int64_t K,
                                     void* stream);
 
+/* The same product for a few tokens (1 <= N <= 8) on the CUDA cores: at
+ * such N the work is bound by the weight stream, so every weight byte is read
+ * from HBM once and applied to all N activation rows (held in shared memory,
+ * N * (K/32 * 40 bytes) must fit it).  Row n of y equals the Q4_0 / Q8_0 x
+ * Q8_0 matvec of activation row n computed by the matvec entries' warp-ring
+ * kernel (asm_matvec_ex_async with ASM_MV_INDEPENDENT, asm_matvec_packed_async)
+ * bit for bit.  Arguments as asm_gemm_image_async; N > 8 is ASM_E_UNSUPPORTED.
+ * No single counterpart in the reference. */
+ASMLLM_API int asm_gemm_narrow_async(int fmt, const void* qweights, const void* scales_f16, const void* images,
+                                     int64_t image_stride, float* y, int64_t M, int64_t N, int64_t K,
+                                     void* stream);
+
 /* Activation tiles: N Q8_0-quantized rows of K values laid out as the fp16
  * operand of the tensor-core product (the int8 quants are exact in fp16).
  * np = N rounded up to 16, 32, 64 or a multiple of 128; plane B (K/32 * np *
